@@ -1,0 +1,412 @@
+#!/usr/bin/env python
+"""Benchmark of the fused packed-int4 MoE expert layer on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (configuration 1 of the benchmark definition, the single-GPU GEMV-bound case): a
+Qwen3-30B-A3B-shaped int4 MoE layer -- hidden 2048, expert intermediate 768, 128 experts, top-8
+softmax routing renormalised, int4 codes packed 8 per int32 with an fp16 scale per 128, activations
+bf16 ~N(0,1) -- at a decode batch of 32 tokens (the batch 1 and 8 points are reported in
+`sweep`).  A step is one layer call over one batch; steps rotate over `--layers` distinct layers
+(each with its own experts and routing), so every step's ~270 MB of expert weights exceeds the
+126 MB L2 and nothing is re-read from cache.  Data are seeded synthetic (no checkpoint exists here).
+
+One JSON line on rank 0: `value` is whole-job tokens/s with inputs resident in HBM (device-timed
+with CUDA events, max over ranks); `e2e` is the same metric through the public API with host
+buffers (pinned H2D of x / expert ids / weights and D2H of the output inside the timed region);
+`roofline` is the dominant kernel (gate/up) against the measured HBM copy bandwidth;
+`cpu_baseline` is the oracle port of the reference's CPU path on this host's cores.
+
+`--impl reference` times the reference's CPU implementation of the path -- the oracle port of
+`stock_experts_prefill(linear=_linear_fp32)` (the reference is Python and cannot travel to the
+GPU host) -- on the same workload, with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "int4 MoE expert-layer tokens/s and % HBM/tensor roofline at 1/2/4/8 B200"
+WORKLOAD = dict(name="cfg1: Qwen3-30B-A3B-shaped int4 MoE layer, decode", hidden=2048, inter=768,
+                experts=128, top_k=8, tokens=32, group=128)
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM = 6650.0
+
+
+def hbm_peak():
+    try:
+        return float(json.loads(PEAKS.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM, "fallback"
+
+
+# ── distributed plumbing ─────────────────────────────────────────────────────────────────
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ── clocks ───────────────────────────────────────────────────────────────────────────────
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.out = self.proc.communicate(timeout=5)[0]
+            except Exception:
+                self.proc.kill()
+                self.out = ""
+
+    def summary(self):
+        if self.proc is None or not getattr(self, "out", ""):
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ── workload ─────────────────────────────────────────────────────────────────────────────
+
+def make_layer(seed, wl, device, experts_slice=None):
+    """One layer's expert blobs (generated on the device from a seeded CUDA generator)."""
+    import vaayu_b200 as vb
+    from vaayu_b200 import synthetic
+    g = torch.Generator(device=device).manual_seed(seed)
+    blobs = []
+    lo, hi = experts_slice or (0, wl["experts"])
+    for e in range(wl["experts"]):
+        by_role = synthetic.make_expert(wl["hidden"], wl["inter"], g, group=wl["group"])
+        if lo <= e < hi:
+            blobs.append(vb.build_expert_blob(by_role))
+    return blobs
+
+
+def make_tokens(seed, wl, tokens, device):
+    from vaayu_b200 import synthetic
+    g = torch.Generator(device=device).manual_seed(10_000 + seed)
+    return synthetic.make_tokens(tokens, wl["hidden"], wl["experts"], wl["top_k"], g)
+
+
+def unique_bytes(table, idx):
+    ids = sorted(set(idx.reshape(-1).tolist()))
+    return table.weight_bytes(ids), len(ids)
+
+
+def gate_up_bytes(table, idx):
+    """Algorithmic bytes of the gate/up stage: the routed experts' gate + up codes and scales."""
+    from vaayu_b200.moe_patch import blob_layout
+    lay = blob_layout(table.geom)
+    bits, gs, _ = table.geom
+    per_expert = 0
+    for role in ("gate", "up"):
+        rows, cols = lay[role][2], lay[role][3]
+        per_expert += rows * cols * bits // 8 + rows * (cols // gs) * table.blobs[0]["flat"]["scale"].element_size()
+    return per_expert * len(set(idx.reshape(-1).tolist()))
+
+
+def time_steps(fn, steps, device):
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        fn(i)
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / steps
+
+
+def run_ours(args, rank, world, local):
+    import vaayu_b200 as vb
+    from vaayu_b200 import packed_expert_kernels as pk
+    device = torch.device("cuda", local)
+    wl = dict(WORKLOAD)
+    T, K = wl["tokens"], wl["top_k"]
+    if world > 1:
+        from vaayu_b200 import ep
+        return ep.run_bench(args, rank, world, local, wl)
+
+    layers = [pk.ExpertTable(make_layer(1000 * l, wl, device)) for l in range(args.layers)]
+    batches = {}
+    for t in sorted({T, 1, 8}):
+        batches[t] = [tuple(v.to(device) for v in make_tokens(l, wl, t, device)) for l in range(args.layers)]
+    out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
+    ws = torch.empty(pk.moe_workspace_bytes(layers[0], T, K), dtype=torch.uint8, device=device)
+    L = args.layers
+
+    def step_for(t):
+        bt = batches[t]
+        o = out[:t]
+
+        def step(i):
+            x, w, idx = bt[i % L]
+            vb.moe_forward(x, idx, w, layers[i % L], out=o, path=vb.PATH_DECODE, workspace=ws)
+        return step
+
+    main_step = step_for(T)
+    for i in range(args.warmup):
+        main_step(i)
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        ms = time_steps(main_step, args.steps, device)
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+    value = T * world / (ms / 1e3)
+
+    # per-stage timing (serialised stages): the gate/up kernel's own duration for the roofline
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    import ctypes
+    handles = (ctypes.c_void_p * 4)(*[e.cuda_event for e in evs])
+    stage = {"plan": [], "gate_up": [], "down": []}
+    for i in range(max(3, min(args.steps, 20))):
+        x, w, idx = batches[T][i % L]
+        c = pk._make_call(layers[i % L].geom_s, x, T, K, layers[i % L].n_experts,
+                          layers[i % L].table.data_ptr(), idx.data_ptr(), 6, w, w.stride(0),
+                          w.stride(1), None, out, None, None)
+        c.stage_events, c.n_stage_events = ctypes.cast(handles, ctypes.c_void_p), 4
+        pk._enqueue(c, vb.PATH_DECODE, device, ws)
+        torch.cuda.synchronize(device)
+        stage["plan"].append(evs[0].elapsed_time(evs[1]))
+        stage["gate_up"].append(evs[1].elapsed_time(evs[2]))
+        stage["down"].append(evs[2].elapsed_time(evs[3]))
+    gu_ms = statistics.mean(stage["gate_up"])
+    gu_bytes = statistics.mean(gate_up_bytes(layers[l], batches[T][l][2]) + T * wl["hidden"] * 2
+                               for l in range(L))
+    peak, peak_kind = hbm_peak()
+    achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+    layer_bytes = statistics.mean(unique_bytes(layers[l], batches[T][l][2])[0] + T * wl["hidden"] * 6
+                                  for l in range(L))
+    uniq = statistics.mean(unique_bytes(layers[l], batches[T][l][2])[1] for l in range(L))
+    traffic = None
+    tfile = ROOT / "profiles" / "gate_up_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    # sweep: batch 1 and 8 (device-timed the same way)
+    sweep = {}
+    for t in (1, 8):
+        st = step_for(t)
+        for i in range(3):
+            st(i)
+        m = time_steps(st, args.steps, device)
+        b = statistics.mean(unique_bytes(layers[l], batches[t][l][2])[0] for l in range(L))
+        sweep[f"T={t}"] = {"tokens_per_s": t / (m / 1e3), "ms_per_step": m,
+                           "layer_GBps": b / (m / 1e3) / 1e9}
+
+    # end to end through the public API with host buffers
+    pin = [(x.cpu().pin_memory(), w.cpu().pin_memory(), idx.cpu().pin_memory()) for x, w, idx in batches[T]]
+    dx = torch.empty_like(batches[T][0][0])
+    dw = torch.empty_like(batches[T][0][1])
+    di = torch.empty_like(batches[T][0][2])
+    out_h = torch.empty(T, wl["hidden"], dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        xh, wh, ih = pin[i % L]
+        dx.copy_(xh, non_blocking=True)
+        dw.copy_(wh, non_blocking=True)
+        di.copy_(ih, non_blocking=True)
+        vb.moe_forward(dx, di, dw, layers[i % L], out=out, path=vb.PATH_DECODE, workspace=ws)
+        out_h.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    e2e_ms = max_over_ranks(time_steps(e2e_step, args.steps, device), world)
+    h2d = dx.numel() * dx.element_size() + dw.numel() * dw.element_size() + di.numel() * di.element_size()
+    d2h = out_h.numel() * out_h.element_size()
+
+    cpu = cpu_baseline(layers[0], batches[T][0], wl) if rank == 0 else None
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1))",
+        "config": {"workload": wl["name"], "hidden": wl["hidden"], "expert_intermediate": wl["inter"],
+                   "experts": wl["experts"], "top_k": wl["top_k"], "tokens_per_gpu": T,
+                   "group_size": wl["group"], "layers_rotated": L,
+                   "l2": f"inputs larger than L2: each step reads ~{layer_bytes / 1e6:.0f} MB of "
+                         f"expert weights, steps rotate over {L} layers",
+                   "parallelism": "ep1", "unique_experts_per_step": uniq},
+        "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "roofline": {"kernel": "gate_up_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": gu_bytes,
+                     "launch_ms": gu_ms},
+        "layer": {"GBps": layer_bytes / (ms / 1e3) / 1e9, "frac_of_hbm": layer_bytes / (ms / 1e3) / 1e9 / peak,
+                  "stage_ms": {k: statistics.mean(v) for k, v in stage.items()}},
+        "sweep": sweep,
+        "cpu_baseline": cpu,
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line))
+
+
+# ── the CPU side: oracle port of the reference's path ───────────────────────────────────────
+
+def _oracle_inputs(table, batch):
+    from tests import helpers as H
+    experts = [H.oracle_expert(b) for b in table.blobs]
+    x, w, idx = batch
+    return experts, H.to_np(x), H.to_np(idx), w.cpu().numpy()
+
+
+def cpu_baseline(table, batch, wl, budget_s=10.0):
+    from oracle import oracle as O
+    experts, x, idx, w = _oracle_inputs(table, batch)
+    threads = os.cpu_count() or 1
+    O.moe_layer(table.geom, experts, x, O.BF16, idx, w, O.F32, O.F16, threads=threads)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.moe_layer(table.geom, experts, x, O.BF16, idx, w, O.F32, O.F16, threads=threads)
+        reps += 1
+        if time.perf_counter() - t0 >= budget_s or reps >= 200:
+            break
+    el = time.perf_counter() - t0
+    return {"value": reps * x.shape[0] / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} full layer calls of the benchmark workload ({x.shape[0]} tokens each, "
+                      f"{el:.1f} s), C oracle restating stock_experts_prefill(linear=_linear_fp32)"}
+
+
+def run_reference(args, rank, world, local):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    wl = dict(WORKLOAD)
+    device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    if device.type == "cuda":
+        from vaayu_b200 import packed_expert_kernels as pk
+        table = pk.ExpertTable(make_layer(0, wl, device))
+        batch = make_tokens(0, wl, wl["tokens"], device)
+    else:
+        from vaayu_b200 import synthetic
+        import vaayu_b200 as vb
+
+        class _T:
+            pass
+        g = torch.Generator().manual_seed(0)
+        table = _T()
+        table.blobs = [vb.build_expert_blob(synthetic.make_expert(wl["hidden"], wl["inter"], g))
+                       for _ in range(wl["experts"])]
+        table.geom = table.blobs[0]["geom"]
+        batch = synthetic.make_tokens(wl["tokens"], wl["hidden"], wl["experts"], wl["top_k"], g)
+    experts, x, idx, w = _oracle_inputs(table, batch)
+    threads = os.cpu_count() or 1
+    run = lambda: O.moe_layer(table.geom, experts, x, O.BF16, idx, w, O.F32, O.F16, threads=threads)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    el = time.perf_counter() - t0
+    ms = el * 1e3 / args.steps
+    v = wl["tokens"] / (ms / 1e3)
+    sample = f"{args.steps} layer calls of {wl['tokens']} tokens (the full benchmark workload)"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations",
+        "data": "synthetic (seeded)",
+        "config": {"workload": wl["name"], "hidden": wl["hidden"], "expert_intermediate": wl["inter"],
+                   "experts": wl["experts"], "top_k": wl["top_k"], "tokens_per_gpu": wl["tokens"],
+                   "group_size": wl["group"]},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--layers", type=int, default=8)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, world, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world, local)
+        else:
+            run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

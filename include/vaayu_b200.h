@@ -1,0 +1,248 @@
+/*
+ * vaayu_b200.h -- C ABI of the B200 (sm_100a) fused packed-int4 MoE expert path.
+ *
+ * One shared library, libvaayu_b200.so, exports these entry points.  They replace the Triton
+ * kernels and the torch dequant of archish9/Vaayu's packed-expert path; citations are paths
+ * inside that project.  Conventions shared by every entry point:
+ *
+ *   - All tensor arguments are DEVICE pointers of the current CUDA device; sizes are element
+ *     counts; strides are in elements.  Nothing here takes ownership of any buffer.
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream).  Every entry point only
+ *     ENQUEUES work on it and returns; it never synchronises and never allocates device memory
+ *     (scratch comes from the caller's `workspace`).
+ *   - The return value is a status: VY_OK (0) or a negative VY_ERR_* code; vy_last_error()
+ *     gives the message of the calling thread's last failure.  Unsupported geometry is
+ *     VY_ERR_UNSUPPORTED: there is no fallback path behind any entry point.
+ *   - dtype codes are the vy_dtype values below.
+ */
+#ifndef VAAYU_B200_H
+#define VAAYU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VY_ABI_VERSION 1
+
+enum vy_status {
+    VY_OK = 0,
+    VY_ERR_UNSUPPORTED = -1, /* geometry / dtype the kernels do not take */
+    VY_ERR_INVALID = -2,     /* null pointer, negative size, inconsistent shapes */
+    VY_ERR_ALIGNMENT = -3,   /* a pointer or stride breaks the 16-byte rule of a vector load */
+    VY_ERR_WORKSPACE = -4,   /* workspace smaller than vy_moe_workspace_size() asked for */
+    VY_ERR_CUDA = -5,        /* a CUDA runtime error while enqueueing */
+    VY_ERR_DEVICE = -6       /* the current device is not an sm_100 part */
+};
+
+enum vy_dtype {
+    VY_BF16 = 0,
+    VY_F16 = 1,
+    VY_F32 = 2,
+    VY_E4M3 = 3, /* float8_e4m3fn */
+    VY_E8M0 = 4, /* float8_e8m0fnu (power-of-two scales) */
+    VY_I32 = 5,
+    VY_I64 = 6
+};
+
+/* The calling thread's last error message ("" after a success). */
+const char* vy_last_error(void);
+/* VY_ABI_VERSION of the loaded library. */
+int vy_abi_version(void);
+
+/* ── int-b packed dequant helpers ───────────────────────────────────────────────────────── */
+
+/*
+ * Inverse of compressed-tensors' pack_to_int32 along the last dim: element j of a word at bits
+ * [b*j, b*j+b); out = code - 2^(b-1) as int8.  packed [rows, words_per_row], out [rows, cols].
+ * Replaces vaayu/moe_patch.py:668-710 `unpack_int32_to_int8` (bits dividing 32).
+ */
+int vy_unpack_int32_to_int8(const int32_t* packed, int64_t rows, int64_t words_per_row,
+                            int32_t bits, int64_t cols, int8_t* out, void* stream);
+
+/*
+ * One flat blob stream dequantised in one pass: out[i] = act(act(code_i - 2^(b-1)) *
+ * act(scale[i / group_size])), act = out_dtype (bf16 / fp16 / fp32).
+ * Replaces vaayu/moe_patch.py:750-791 `_fused_dequant_kernel` / `_fused_dequant_fn`, the body
+ * of `dequantize_expert_blob` (:849-864).  bits in {2, 4, 8}; group_size a multiple of 32/bits.
+ */
+int vy_dequant_flat(const int32_t* packed, int64_t n_words, int32_t bits, const void* scale,
+                    int32_t scale_dtype, int32_t group_size, void* out, int32_t out_dtype,
+                    void* stream);
+
+/*
+ * One projection [rows, cols] dequantised: out[r, c] = act(act(u - z) * act(scale[r, c / gs])),
+ * z = 2^(b-1) when `zero` is NULL (the reference's symmetric format), else the stored zero code
+ * of compressed-tensors' row-packed zero points zero[ceil(rows*b/32), cols/gs].
+ * Replaces vaayu/moe_patch.py:713-744 `dequantize_packed_weight`; the zero-point form is an
+ * extension (the reference refuses it, :724-729).
+ */
+int vy_dequant_packed_weight(const int32_t* packed, int64_t rows, int64_t cols, int32_t bits,
+                             const void* scale, int32_t scale_dtype, int32_t group_size,
+                             const int32_t* zero, void* out, int32_t out_dtype, void* stream);
+
+/* ── block-scaled FP8 / FP4 ────────────────────────────────────────────────────────────── */
+
+/*
+ * out[r, c] = out_dtype(float(w[r, c]) * float(scale[r / bo, c / bi])), bo = rows / srows,
+ * bi = cols / scols; w e4m3, scale fp32 / bf16 / e8m0.
+ * Replaces vaayu/model_code/deepseek_v4/modeling_deepseek_v4.py:228-240 `dequantize_block_scaled`.
+ */
+int vy_fp8_dequant(const uint8_t* w, int64_t rows, int64_t cols, const void* scale,
+                   int32_t scale_dtype, int64_t srows, int64_t scols, void* out,
+                   int32_t out_dtype, void* stream);
+
+/*
+ * NVFP4: w [rows, cols/2] bytes holding two e2m1 codes (low nibble = even column), scale
+ * [rows, cols/group_size] e4m3; out[r, c] = out_dtype(e2m1 * float(scale)).
+ * No reference function (the nearest is the checkpoint-shipped fp4 GEMM behind
+ * modeling_deepseek_v4.py:315-323, 353-363); the e2m1 table is the OCP MX one.
+ */
+int vy_fp4_dequant(const uint8_t* w, int64_t rows, int64_t cols, const uint8_t* scale,
+                   int32_t group_size, void* out, int32_t out_dtype, void* stream);
+
+/*
+ * Dequant fused into a decode GEMV: out[t, n] = bf16(sum_k deq(W)[n, k] * x[t, k]), fp32
+ * accumulation, x [n_tokens, k] bf16 (row stride x_stride), out [n_tokens, n] bf16 (row
+ * stride out_stride), n_tokens <= 16.  The dequantised weight is exactly what vy_fp8_dequant /
+ * vy_fp4_dequant produce.  No reference function: the reference dequantises at load
+ * (modeling_deepseek_v4.py:243-270) and multiplies in bf16.
+ */
+int vy_fp8_gemv(const uint8_t* w, int64_t n, int64_t k, const void* scale, int32_t scale_dtype,
+                int64_t srows, int64_t scols, const void* x, int64_t x_stride,
+                int64_t n_tokens, void* out, int64_t out_stride, void* stream);
+int vy_fp4_gemv(const uint8_t* w, int64_t n, int64_t k, const uint8_t* scale,
+                int32_t group_size, const void* x, int64_t x_stride, int64_t n_tokens,
+                void* out, int64_t out_stride, void* stream);
+
+/* ── routing ───────────────────────────────────────────────────────────────────────────── */
+
+/*
+ * softmax(fp32 logits) -> top-k -> renormalised weights: weights [n_tokens, top_k] fp32,
+ * ids [n_tokens, top_k] int64, largest first (ties to the lower expert id).
+ * Replaces the fallback branch of vaayu/moe_patch.py:130-167 `route_experts` (:160-161) and of
+ * `_route` (:2331-2334).  logits [n_tokens, n_experts] in logit_dtype, row stride.
+ */
+int vy_moe_topk_softmax(const void* logits, int32_t logit_dtype, int64_t row_stride,
+                        int64_t n_tokens, int32_t n_experts, int32_t top_k, float* weights,
+                        int64_t* ids, void* stream);
+
+/*
+ * Routed gather/permute plan, on the device (no host sync): the rows (token * top_k + slot)
+ * grouped by expert id -- stable, ascending id -- and each token's slots in ascending expert id.
+ *   order       [n_tokens*top_k]  row ids, each expert's rows a contiguous run in row order
+ *   live_expert [n_experts]       the routed expert ids, ascending; entries >= n_live unused
+ *   live_start  [n_experts+1]     live_start[i] = first position of live_expert[i] in `order`
+ *   slot_order  [n_tokens*top_k]  row ids of token t's slots, ascending expert id then slot
+ *   counters    [4]               n_live, rows dropped for an out-of-range id, 0, 0
+ * Replaces vaayu/packed_expert_kernels.py:676-717 `_prefill_plan` / `_prefill_tables` (host
+ * argsort + pinned upload) and vaayu/moe_patch.py:306-326 `compute_expert_dispatch`.
+ * ids [n_tokens, top_k] contiguous, ids_dtype VY_I32 or VY_I64.  n_experts <= 1024.
+ */
+int vy_moe_route_permute(const void* ids, int32_t ids_dtype, int64_t n_tokens, int32_t top_k,
+                         int32_t n_experts, int32_t* order, int32_t* live_expert,
+                         int32_t* live_start, int32_t* slot_order, int32_t* counters,
+                         void* stream);
+
+/* ── the fused expert layer ────────────────────────────────────────────────────────────── */
+
+/*
+ * Geometry of one expert blob (`build_expert_blob`, vaayu/moe_patch.py:794-846): three
+ * projections gate [inter, hidden], up [inter, hidden], down [hidden, inter] packed along K in
+ * one int32 stream, one scale stream and (optionally) one row-packed zero-point stream.  The
+ * offsets say where each role starts inside its stream (index 0 gate, 1 up, 2 down), so any
+ * role order is accepted (the reference's blobs are ordered gate, down, up).
+ */
+typedef struct vy_expert_geom {
+    int32_t hidden;
+    int32_t inter;
+    int32_t bits;         /* 4 */
+    int32_t group_size;   /* power of two >= 32, dividing hidden and inter */
+    int32_t scale_dtype;  /* VY_BF16 / VY_F16 / VY_F32 */
+    int32_t has_zero;     /* 0: symmetric (zero 2^(b-1)), 1: zero-point stream present */
+    int64_t word_off[3];
+    int64_t scale_off[3];
+    int64_t zero_off[3];
+} vy_expert_geom;
+
+/*
+ * One MoE layer call.  Row j = t * top_k + k is slot k of token t; it routes to expert
+ * expert_ids[j] (an index into expert_table) with weight
+ *   weights[t * w_tok_stride + (w_index ? w_index[j] : k) * w_slot_stride].
+ * expert_table[e] = {packed stream, scale stream, zero stream (or 0)} device addresses of
+ * expert e's blob (int64 each).  Per row: g = act(x.Wg), u = act(x.Wu), a = act(silu(g)),
+ * h = act(a * u), y = act(h.Wd), c = fp32(y) * w (rounded to act when w_dtype == act_dtype),
+ * and out[t] = the fp32 sum of token t's c in ascending expert index, then slot
+ * (vaayu/moe_patch.py:914-940).  `out` is overwritten.  When `contrib` is non-NULL the per-row
+ * c go there ([n_tokens*top_k, hidden] fp32) and `out` is not written (the expert-parallel
+ * combine sums them on the token's home rank).  `h_out` (optional, [n_tokens*top_k, inter],
+ * act dtype) receives each row's h: a stage probe for tests.
+ */
+typedef struct vy_moe_call {
+    const vy_expert_geom* geom;
+    int32_t act_dtype;        /* VY_BF16 or VY_F16 */
+    int32_t n_experts;
+    int32_t top_k;
+    int32_t ids_dtype;        /* VY_I32 / VY_I64 */
+    int64_t n_tokens;
+    const void* x;            /* [n_tokens, hidden], act dtype */
+    int64_t x_row_stride;
+    const int64_t* expert_table;
+    const void* expert_ids;   /* [n_tokens, top_k] contiguous */
+    const void* weights;
+    int32_t w_dtype;          /* VY_F32 / VY_BF16 / VY_F16 */
+    int32_t reserved0;
+    int64_t w_tok_stride;
+    int64_t w_slot_stride;
+    const int32_t* w_index;   /* optional */
+    float* out;               /* [n_tokens, hidden] fp32 */
+    int64_t out_row_stride;
+    float* contrib;           /* optional */
+    void* h_out;              /* optional */
+    void* workspace;
+    size_t workspace_bytes;
+    /* Optional per-stage timing (the reference's per-phase profile, vaayu/moe_patch.py:2431-2438):
+     * when non-NULL, n_stage_events (>= 4) cudaEvent_t handles recorded on `stream` before the
+     * routing plan, after it, after the gate/up stage and after the down/combine stage.  Recording
+     * them serialises the stages (no programmatic overlap): a profiling mode, not the fast path. */
+    void* const* stage_events;
+    int32_t n_stage_events;
+    int32_t reserved1;
+} vy_moe_call;
+
+/* Bytes of workspace vy_moe_decode (path 0) / vy_moe_prefill (path 1) need for `call`. */
+size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path);
+
+/*
+ * The layer through the bandwidth-bound kernels: a token-batched dequant GEMV that reads each
+ * routed expert's packed weights once for all its tokens.  For decode-sized calls.
+ * Replaces vaayu/packed_expert_kernels.py:130-176 `_gate_up_kernel` / `_down_kernel` and their
+ * launcher `_launch` (:390-396) behind `packed_experts_decode` (:459-480).
+ */
+int vy_moe_decode(const vy_moe_call* call, void* stream);
+
+/*
+ * The layer through the tensor-core grouped GEMM (tcgen05, accumulators in TMEM): int4
+ * dequantised into shared memory, 128-row tiles per expert.  For prefill-sized calls.
+ * Replaces vaayu/packed_expert_kernels.py:178-260 `_gate_up_grouped` / `_down_grouped` /
+ * `_reduce_kernel` and `_prefill_launch` (:760-777) behind `packed_experts_prefill` (:838-861).
+ */
+int vy_moe_prefill(const vy_moe_call* call, void* stream);
+
+/*
+ * out[t] = sum of contrib[t * top_k + k] over the token's slots in ascending expert id, then
+ * slot (fp32), for contributions gathered back from other ranks.  Replaces
+ * vaayu/packed_expert_kernels.py:249-260 `_reduce_kernel` with the order
+ * `accumulate_expert_outputs` (vaayu/moe_patch.py:914-940) sums in.
+ */
+int vy_moe_combine(const float* contrib, const void* expert_ids, int32_t ids_dtype,
+                   int64_t n_tokens, int32_t top_k, int64_t hidden, float* out,
+                   int64_t out_row_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VAAYU_B200_H */

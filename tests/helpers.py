@@ -77,3 +77,71 @@ def expert_from_components(by_role: dict) -> dict:
     if "weight_zero_point" in by_role["gate"]:
         zero = np.concatenate([to_np(by_role[r]["weight_zero_point"]).reshape(-1) for r in roles])
     return {"packed": packed.astype(np.int32), "scale": scale, "zero": zero}
+
+
+# ── GPU-suite helpers: the oracle on the same tensors the kernels see ─────────────────────
+
+def oracle_expert(blob: dict) -> dict:
+    """A `build_expert_blob` blob (any device) as the oracle's numpy expert dict."""
+    f = blob["flat"]
+    return {"packed": to_np(f["packed"]).astype(np.int32), "scale": to_np(f["scale"]),
+            "zero": None if "zero" not in f else to_np(f["zero"]).astype(np.int32)}
+
+
+def oracle_layer(blobs, x, eidx, rw, w_index=None, want_h=False, want_y=False, threads=0):
+    """Oracle of one layer call: blobs indexed by expert id; eidx [T, K]; rw [T, K] (or flat
+    with w_index)."""
+    from oracle import oracle as O
+    experts = [oracle_expert(b) for b in blobs]
+    sc = CODE[blobs[0]["flat"]["scale"].dtype]
+    res = O.moe_layer(blobs[0]["geom"], experts, to_np(x), CODE[x.dtype], to_np(eidx),
+                      to_np(rw.reshape(-1)) if w_index is None else to_np(rw.reshape(-1)),
+                      CODE[rw.dtype], sc,
+                      w_index=None if w_index is None else np.asarray(w_index, np.int32),
+                      want_h=want_h, want_y=want_y, threads=threads)
+    return res
+
+
+def make_blobs(hid, inter, n, gs=128, seed=0, zeros=False, scale_dtype=None, device="cuda"):
+    """n synthetic expert blobs (CPU generator, so every machine draws the same bits)."""
+    import vaayu_b200 as vb
+    from vaayu_b200 import synthetic
+    scale_dtype = scale_dtype or torch.float16
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        by_role = synthetic.make_expert(hid, inter, g, group=gs, zeros=zeros, scale_dtype=scale_dtype)
+        by_role = {r: {k: (v if k == "weight_shape" else v.to(device)) for k, v in c.items()}
+                   for r, c in by_role.items()}
+        out.append(vb.build_expert_blob(by_role))
+    return out
+
+
+def fp64_layer(blobs, x, eidx, rw):
+    """The truth: the exact dequantised weights, float64 everywhere."""
+    from oracle import oracle as O
+    geom = blobs[0]["geom"]
+    bits, gs, roles = geom
+    lay = O.layout(geom)
+    xf = f32(to_np(x), CODE[x.dtype])
+    eidx = np.asarray(to_np(eidx)).reshape(xf.shape[0], -1)
+    w = f32(to_np(rw), CODE[rw.dtype]).reshape(eidx.shape)
+    out = np.zeros((xf.shape[0], lay["gate"][3]))
+    mats_cache = {}
+    for t in range(eidx.shape[0]):
+        for k in range(eidx.shape[1]):
+            e = int(eidx[t, k])
+            if e not in mats_cache:
+                ex = oracle_expert(blobs[e])
+                mats = {}
+                for role, rows, cols in roles:
+                    w_at, s_at, _r, _c = lay[role]
+                    es = ex["scale"]
+                    d = O.dequant_role(ex["packed"][w_at:], rows, cols, bits, es[s_at:],
+                                       CODE[blobs[e]["flat"]["scale"].dtype], gs, 2)
+                    mats[role] = d.astype(np.float64)
+                mats_cache[e] = mats
+            m = mats_cache[e]
+            g, u = m["gate"] @ xf[t], m["up"] @ xf[t]
+            out[t] += (m["down"] @ (g / (1 + np.exp(-g)) * u)) * w[t, k]
+    return out

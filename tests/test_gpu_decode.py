@@ -1,0 +1,248 @@
+"""GPU: the decode kernels (token-batched int4 GEMV) against the oracle and the reference's own
+goldens, with the reference tests' bars (tests/test_packed_expert_kernels.py:118-298)."""
+import numpy as np
+import pytest
+import torch
+
+import vaayu_b200 as vb
+from tests import helpers as T
+from vaayu_b200 import packed_expert_kernels as pk
+
+pytestmark = pytest.mark.gpu
+
+# (hidden, intermediate, group, top_k): the reference test's two int4 geometries, and cfg1's
+GEOMS = [pytest.param(2048, 512, 32, 10, id="qwen3next-int4-g32"),
+         pytest.param(3072, 1536, 128, 8, id="minimax-like-int4-g128"),
+         pytest.param(2048, 768, 128, 8, id="cfg1-qwen3-30b-a3b")]
+
+
+def _case(hid, inter, gs, k, seed=0, w_dtype=torch.float32, zeros=False):
+    """(x, pairs, w, blobs): expert i (ascending id) routed in a shuffled slot."""
+    blobs = T.make_blobs(hid, inter, k, gs=gs, seed=hid + inter + gs, zeros=zeros)
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(1, hid, generator=g) * 0.5).to(torch.bfloat16).cuda()
+    w = torch.rand(1, k, generator=g) + 0.05
+    w = (w / w.sum(-1, keepdim=True)).to(w_dtype).cuda()
+    slots = torch.randperm(k, generator=g).tolist()
+    return x, [(blobs[i], slots[i]) for i in range(k)], w, blobs, slots
+
+
+def _run(x, pairs, w):
+    out = torch.full((1, x.shape[1]), float("nan"), device="cuda")
+    vb.packed_experts_decode(x, pairs, w, out, None)
+    torch.cuda.synchronize()
+    return out
+
+
+def _oracle(x, blobs, slots, w, **kw):
+    k = len(blobs)
+    return T.oracle_layer(blobs, x, torch.arange(k).view(1, k), w, w_index=slots, **kw)
+
+
+def test_decode_matches_the_reference_golden():
+    g = T.golden("decode")
+    hid, inter, bits, gs, k = (int(v) for v in g["meta"])
+    blobs = [{"flat": {"packed": torch.from_numpy(g[f"e{i}_packed"]).cuda(),
+                       "scale": torch.from_numpy(g[f"e{i}_scale"].view(np.float16)).cuda()},
+              "geom": T.geom(hid, inter, bits, gs)} for i in range(k)]
+    x = T.from_np(g["x"]).cuda()
+    pairs = [(blobs[i], int(g["slots"][i])) for i in range(k)]
+    for tag, dt in (("fp32", torch.float32), ("bf16", torch.bfloat16)):
+        w = T.from_np(g[f"w_{tag}"]).cuda() if dt == torch.bfloat16 else torch.from_numpy(g[f"w_{tag}"]).cuda()
+        got = _run(x, pairs, w)
+        ref = g[f"out_{tag}"]
+        assert T.rel_l2(got.cpu().numpy(), ref) <= 1e-3
+        assert T.max_abs_over_rms(got.cpu().numpy(), ref) <= 2e-2
+    h = torch.empty(k, inter, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(1, hid, device="cuda")
+    pk._launch(x, pairs, torch.from_numpy(g["w_fp32"]).cuda(), out, h_out=h)
+    torch.cuda.synchronize()
+    assert (T.to_np(h) == g["h"]).mean() >= 0.99
+
+
+@pytest.mark.parametrize("hid,inter,gs,k", GEOMS)
+def test_each_rounding_point_matches_the_oracle(hid, inter, gs, k):
+    """Stage by stage: h (gate/up/SiLU/product) and the down output (weight 1) rounded where the
+    stock loop rounds; only the order inside each dot product may differ."""
+    x, pairs, w, blobs, slots = _case(hid, inter, gs, k)
+    h = torch.empty(k, inter, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(1, hid, device="cuda")
+    pk._launch(x, pairs, w, out, h_out=h)
+    ones = torch.ones(1, k, device="cuda")
+    contrib = torch.empty(k, hid, device="cuda")
+    table = pk.ExpertTable(blobs)
+    vb.moe_forward(x, torch.arange(k, device="cuda").view(1, k), ones, table, contrib=contrib)
+    torch.cuda.synchronize()
+    _o, h_ref, y_ref = _oracle(x, blobs, list(range(k)), ones, want_h=True, want_y=True)
+    assert (T.to_np(h) == h_ref).mean() >= 0.99, "gate/up/SiLU/product stage"
+    assert (contrib.cpu().numpy() == y_ref).mean() >= 0.99, "down stage"
+
+
+@pytest.mark.parametrize("w_dtype", [torch.float32, torch.bfloat16], ids=["fp32-w", "bf16-w"])
+def test_the_expert_sum_runs_in_table_order(w_dtype):
+    """EXACT: out = the fp32 sum, in table order, of each pair's own contribution."""
+    x, pairs, w, blobs, slots = _case(2048, 512, 32, 10, w_dtype=w_dtype)
+    full = _run(x, pairs, w)
+    k = len(pairs)
+    contrib = torch.empty(k, 2048, device="cuda")
+    ids = torch.arange(k, device="cuda", dtype=torch.int32).view(1, k)
+    w_idx = torch.tensor(slots, dtype=torch.int32, device="cuda")
+    vb.moe_forward(x, ids, w, pk.ExpertTable(blobs), contrib=contrib, w_index=w_idx)
+    c = contrib.cpu().numpy()
+    expected = np.zeros(2048, np.float32)
+    for i in range(k):
+        expected = (expected + c[i]).astype(np.float32)
+    assert np.array_equal(full.cpu().numpy()[0], expected)
+
+
+@pytest.mark.parametrize("hid,inter,gs,k", GEOMS)
+def test_kernel_output_is_as_accurate_as_the_stock_arithmetic(hid, inter, gs, k):
+    x, pairs, w, blobs, slots = _case(hid, inter, gs, k)
+    got = _run(x, pairs, w).cpu().numpy()
+    ref = _oracle(x, blobs, slots, w)
+    assert T.rel_l2(got, ref) <= 1e-3
+    assert T.max_abs_over_rms(got, ref) <= 2e-2
+    ids = torch.zeros(1, k, dtype=torch.long)
+    ids[0, torch.tensor(slots)] = torch.arange(k)
+    truth = T.fp64_layer(blobs, x, ids, w)
+    assert T.rel_l2(got, truth) <= 1.25 * T.rel_l2(ref, truth) + 1e-12
+
+
+def test_bf16_routing_weights_round_like_the_stock_loop():
+    x, pairs, w, blobs, slots = _case(2048, 512, 32, 10, w_dtype=torch.bfloat16)
+    got = _run(x, pairs, w).cpu().numpy()
+    ref = _oracle(x, blobs, slots, w)
+    assert (T.bf16_round_np(got) == T.bf16_round_np(ref)).mean() >= 0.99
+    assert T.rel_l2(got, ref) <= 1e-3
+
+
+def test_the_output_does_not_depend_on_where_the_blobs_live():
+    x, pairs, w, blobs, slots = _case(2048, 512, 32, 10)
+    clones = [({"flat": {n: t.clone() for n, t in b["flat"].items()}, "geom": b["geom"]}, s)
+              for b, s in pairs]
+    assert torch.equal(_run(x, pairs, w), _run(x, clones, w))
+
+
+def test_a_zero_weight_duplicate_slot_changes_nothing():
+    x, pairs, w, blobs, slots = _case(2048, 512, 32, 10)
+    k = w.shape[1]
+    w2 = torch.cat([w, torch.zeros(1, 1, dtype=w.dtype, device=w.device)], dim=1)
+    dup = pairs[:1] + [(pairs[0][0], k)] + pairs[1:]
+    assert torch.equal(_run(x, pairs, w), _run(x, dup, w2))
+
+
+def test_back_to_back_calls_do_not_share_a_table():
+    cases = [_case(2048, 512, 32, 10, seed=s) for s in range(3 * len(pk._TABLES._slots))]
+    outs = []
+    for x, pairs, w, _b, _s in cases:
+        out = torch.empty(1, x.shape[1], device="cuda")
+        vb.packed_experts_decode(x, pairs, w, out, None)
+        outs.append(out)
+    torch.cuda.synchronize()
+    for (x, pairs, w, _b, _s), out in zip(cases, outs):
+        assert torch.equal(out, _run(x, pairs, w))
+
+
+def test_a_nan_inside_the_experts_is_not_masked():
+    x, pairs, w, blobs, slots = _case(2048, 512, 32, 10)
+    x = x.clone()
+    x[0, 5] = float("nan")
+    assert torch.isnan(_run(x, pairs, w)).all()
+
+
+def test_an_unsupported_geometry_raises_instead_of_falling_back():
+    x, pairs, w, blobs, slots = _case(192, 96, 32, 2)
+    with pytest.raises(NotImplementedError):
+        _run(x, pairs, w)
+
+
+def test_a_call_mixing_geometries_raises_instead_of_falling_back():
+    x, pairs, w, blobs, slots = _case(2048, 512, 32, 10)
+    other = T.make_blobs(2048, 512, 1, gs=64, seed=9)[0]
+    with pytest.raises(NotImplementedError, match="one geometry"):
+        _run(x, pairs[:9] + [(other, pairs[9][1])], w)
+    dense = {"dense": dict(zip(("gate", "down", "up"), vb.expert_weights_from_entry(blobs[0], x.dtype)))}
+    with pytest.raises(NotImplementedError):
+        _run(x, [(dense, pairs[0][1])] + pairs[1:], w)
+
+
+# ── token-batched decode through the resident table (device routing, no host sync) ────────
+
+def _batched(hid, inter, gs, n_exp, top_k, tokens, seed=0, zeros=False, act=torch.bfloat16,
+             w_dtype=torch.float32):
+    blobs = T.make_blobs(hid, inter, n_exp, gs=gs, seed=seed + 100, zeros=zeros)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(tokens, hid, generator=g).to(act).cuda()
+    w, idx = torch.topk(torch.randn(tokens, n_exp, generator=g).softmax(-1), top_k, -1)
+    w = (w / w.sum(-1, keepdim=True)).to(w_dtype).cuda()
+    return blobs, x, idx.cuda(), w
+
+
+@pytest.mark.parametrize("tokens", [1, 8, 32, 64])
+def test_batched_decode_matches_the_oracle(tokens):
+    blobs, x, idx, w = _batched(2048, 768, 128, 32, 8, tokens)
+    got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=vb.PATH_DECODE).cpu().numpy()
+    ref = T.oracle_layer(blobs, x, idx, w)
+    assert T.rel_l2(got, ref) <= 1e-3
+    assert T.max_abs_over_rms(got, ref) <= 2e-2
+    assert (T.bf16_round_np(got) == T.bf16_round_np(ref)).mean() >= 0.99
+
+
+def test_many_tokens_on_one_expert_take_several_passes():
+    """64 tokens all routed to the same 4 experts: 64 columns per expert, two 32-token passes."""
+    blobs, x, idx, w = _batched(1024, 512, 128, 8, 4, 64, seed=3)
+    idx = torch.arange(4, device="cuda").repeat(64, 1)
+    got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=vb.PATH_DECODE).cpu().numpy()
+    assert T.rel_l2(got, T.oracle_layer(blobs, x, idx, w)) <= 1e-3
+
+
+def test_zero_point_layer_matches_the_oracle():
+    blobs, x, idx, w = _batched(1024, 512, 128, 16, 4, 4, seed=7, zeros=True)
+    got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=vb.PATH_DECODE).cpu().numpy()
+    ref = T.oracle_layer(blobs, x, idx, w)
+    assert T.rel_l2(got, ref) <= 1e-3 and T.max_abs_over_rms(got, ref) <= 2e-2
+
+
+def test_fp16_activations_match_the_oracle():
+    blobs, x, idx, w = _batched(1024, 512, 64, 16, 4, 8, seed=8, act=torch.float16,
+                                w_dtype=torch.float16)
+    got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=vb.PATH_DECODE).cpu().numpy()
+    ref = T.oracle_layer(blobs, x, idx, w)
+    assert T.rel_l2(got, ref) <= 1e-3
+
+
+def test_a_token_does_not_depend_on_its_batch():
+    blobs, x, idx, w = _batched(2048, 768, 128, 32, 8, 24, seed=2)
+    table = pk.ExpertTable(blobs)
+    full = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE)
+    for t in (0, 11, 23):
+        alone = vb.moe_forward(x[t:t + 1], idx[t:t + 1], w[t:t + 1], table, path=vb.PATH_DECODE)
+        assert torch.equal(alone[0], full[t])
+
+
+def test_strided_inputs_and_outputs_are_read_as_what_they_hold():
+    blobs, x, idx, w = _batched(1024, 512, 128, 16, 4, 8, seed=4)
+    table = pk.ExpertTable(blobs)
+    dense = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE)
+    wide_x = torch.zeros(8, 2048, dtype=x.dtype, device="cuda")
+    wide_x[:, 512:1536] = x
+    wide_w = torch.zeros(8, 12, device="cuda")
+    wide_w[:, 3:7] = w
+    wide_o = torch.full((8, 3000), 7.0, device="cuda")
+    out = wide_o[:, 1000:2024]
+    vb.moe_forward(wide_x[:, 512:1536], idx, wide_w[:, 3:7], table, out=out, path=vb.PATH_DECODE)
+    assert torch.equal(out, dense)
+    assert (wide_o[:, :1000] == 7.0).all() and (wide_o[:, 2024:] == 7.0).all()
+
+
+def test_an_expert_id_outside_the_table_is_dropped():
+    blobs, x, idx, w = _batched(1024, 512, 128, 8, 2, 4, seed=5)
+    table = pk.ExpertTable(blobs)
+    bad = idx.clone()
+    bad[1, 1] = 99
+    got = vb.moe_forward(x, bad, w, table, path=vb.PATH_DECODE)
+    w2 = w.clone()
+    w2[1, 1] = 0.0
+    ref = vb.moe_forward(x, idx, w2, table, path=vb.PATH_DECODE)
+    assert torch.equal(got[0], ref[0]) and torch.equal(got[2:], ref[2:])
+    assert torch.allclose(got[1], ref[1], rtol=0, atol=1e-6)

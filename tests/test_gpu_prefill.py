@@ -1,0 +1,216 @@
+"""GPU: `packed_experts_prefill` (multi-token calls) against the oracle, with the reference's
+prefill test bars (tests/test_packed_prefill_kernels.py:115-437)."""
+import numpy as np
+import pytest
+import torch
+
+import vaayu_b200 as vb
+from tests import helpers as T
+from vaayu_b200 import packed_expert_kernels as pk
+
+pytestmark = pytest.mark.gpu
+
+BF = torch.bfloat16
+GEOMS = [pytest.param(2048, 512, 32, id="qwen3next-int4-g32"),
+         pytest.param(3072, 1536, 128, id="minimax-dims-int4-g128"),
+         pytest.param(1024, 512, 64, id="int4-g64")]
+QWEN = (2048, 512, 32)
+
+
+def _case(hid, inter, gs, *, n_exp=24, tokens=40, top_k=6, seed=0, w_dtype=torch.float32, eidx=None):
+    """(x, eidx, w, blobs): ids are not dense (every third id), so ids != table positions."""
+    base = T.make_blobs(hid, inter, 8, gs=gs, seed=hid + inter + gs)
+    ids = [3 * i + 1 for i in range(n_exp)]
+    blobs = {e: base[i % len(base)] for i, e in enumerate(ids)}
+    g = torch.Generator().manual_seed(seed)
+    if eidx is None:
+        eidx = torch.stack([torch.tensor(ids)[torch.randperm(n_exp, generator=g)[:top_k]]
+                            for _ in range(tokens)])
+    x = (torch.randn(eidx.shape[0], hid, generator=g) * 0.5).to(BF).cuda()
+    w = torch.rand(eidx.shape, generator=g) + 0.05
+    return x, eidx, (w / w.sum(-1, keepdim=True)).to(w_dtype).cuda(), blobs
+
+
+def _dense(eidx, blobs):
+    """(blob list indexed 0..U-1, eidx remapped to it) for the oracle."""
+    live = sorted({int(e) for e in eidx.reshape(-1).tolist()})
+    pos = {e: i for i, e in enumerate(live)}
+    return [blobs[e] for e in live], eidx.clone().apply_(lambda e: pos[e])
+
+
+def _launch(x, eidx, w, blobs):
+    out = torch.full(x.shape, float("nan"), device="cuda")
+    vb.packed_experts_prefill(x, eidx, w, blobs, out, None)
+    torch.cuda.synchronize()
+    return out
+
+
+def _oracle(x, eidx, w, blobs, **kw):
+    lst, e2 = _dense(eidx, blobs)
+    return T.oracle_layer(lst, x, e2, w, **kw)
+
+
+@pytest.mark.parametrize("hid,inter,gs", GEOMS)
+def test_each_stage_is_correctly_rounded(hid, inter, gs):
+    x, eidx, w, blobs = _case(hid, inter, gs)
+    n = eidx.numel()
+    h = torch.empty(n, inter, dtype=BF, device="cuda")
+    y = torch.empty(n, hid, device="cuda")
+    ones = torch.ones_like(w)
+    pk._prefill_launch(x, eidx, ones, blobs, None, path=pk._prefill_path(), h_out=h, contrib=y)
+    torch.cuda.synchronize()
+    _o, h_ref, y_ref = _oracle(x, eidx, ones, blobs, want_h=True, want_y=True)
+    assert (T.to_np(h) == h_ref).mean() >= 0.99, "gate/up/SiLU/product stage"
+    assert (y.cpu().numpy() == y_ref).mean() >= 0.99, "down stage"
+
+
+@pytest.mark.parametrize("w_dtype", [torch.float32, BF], ids=["fp32-w", "bf16-w"])
+def test_the_contribution_is_the_rounded_down_output_times_its_weight(w_dtype):
+    """EXACT, both promotions: an fp32 weight leaves an fp32 product; a weight already in the
+    activation dtype makes the product round to it."""
+    x, eidx, w, blobs = _case(*QWEN, w_dtype=w_dtype)
+    n, hid = eidx.numel(), QWEN[0]
+    down, y = torch.empty(n, hid, device="cuda"), torch.empty(n, hid, device="cuda")
+    pk._prefill_launch(x, eidx, torch.ones_like(w), blobs, None, path=pk._prefill_path(), contrib=down)
+    pk._prefill_launch(x, eidx, w, blobs, None, path=pk._prefill_path(), contrib=y)
+    torch.cuda.synchronize()
+    assert torch.equal(y, (down.to(BF) * w.reshape(-1, 1)).float())
+
+
+@pytest.mark.parametrize("hid,inter,gs", GEOMS)
+def test_the_token_sum_runs_in_expert_id_order(hid, inter, gs):
+    x, eidx, w, blobs = _case(hid, inter, gs)
+    n, top_k = eidx.numel(), eidx.shape[1]
+    y = torch.empty(n, hid, device="cuda")
+    pk._prefill_launch(x, eidx, w, blobs, None, path=pk._prefill_path(), contrib=y)
+    out = _launch(x, eidx, w, blobs).cpu().numpy()
+    yc = y.cpu().numpy()
+    expected = np.zeros(out.shape, np.float32)
+    for t in range(eidx.shape[0]):
+        for k in np.argsort(eidx[t].numpy(), kind="stable"):
+            expected[t] = (expected[t] + yc[t * top_k + k]).astype(np.float32)
+    assert np.array_equal(out, expected)
+
+
+@pytest.mark.parametrize("hid,inter,gs", GEOMS)
+def test_kernel_output_is_as_accurate_as_the_fp32_gemm_replay(hid, inter, gs):
+    x, eidx, w, blobs = _case(hid, inter, gs)
+    got = _launch(x, eidx, w, blobs).cpu().numpy()
+    ref = _oracle(x, eidx, w, blobs)
+    assert T.rel_l2(got, ref) <= 2e-3
+    assert T.max_abs_over_rms(got, ref) <= 2e-2
+    lst, e2 = _dense(eidx, blobs)
+    truth = T.fp64_layer(lst, x, e2, w)
+    assert T.rel_l2(got, truth) <= 1.05 * T.rel_l2(ref, truth) + 1e-12
+
+
+def test_a_token_does_not_depend_on_the_tokens_it_shares_a_call_with():
+    x, eidx, w, blobs = _case(*QWEN, tokens=40)
+    full = _launch(x, eidx, w, blobs)
+    for t in (0, 17, 39):
+        alone = _launch(x[t:t + 1], eidx[t:t + 1], w[t:t + 1], blobs)
+        assert torch.equal(alone[0], full[t]), f"token {t}"
+
+
+def test_block_boundaries():
+    """Experts with 1, 16, 17 and 40 rows, plus 130 rows (a 128-row tile and a tail)."""
+    counts = {1: 1, 4: 16, 7: 17, 10: 40, 25: 130}
+    slots = [e for e, c in counts.items() for _ in range(c)]
+    filler = [13, 16, 19, 22]
+    eidx = torch.tensor([[e, filler[i % 4]] for i, e in enumerate(slots)])
+    x, eidx, w, blobs = _case(*QWEN, top_k=2, eidx=eidx)
+    full = _launch(x, eidx, w, blobs)
+    assert not torch.isnan(full).any()
+    for t in (0, 1, 16, 17, 33, 34, 73, 74, 200, len(slots) - 1):
+        alone = _launch(x[t:t + 1], eidx[t:t + 1], w[t:t + 1], blobs)
+        assert torch.equal(alone[0], full[t]), f"token {t}"
+    assert T.rel_l2(full.cpu().numpy(), _oracle(x, eidx, w, blobs)) <= 2e-3
+
+
+def test_the_output_does_not_depend_on_where_the_blobs_live_or_their_order():
+    x, eidx, w, blobs = _case(*QWEN)
+    moved = {e: {"flat": {n: t.clone() for n, t in b["flat"].items()}, "geom": b["geom"]}
+             for e, b in reversed(list(blobs.items()))}
+    assert torch.equal(_launch(x, eidx, w, blobs), _launch(x, eidx, w, moved))
+
+
+def test_a_zero_weight_duplicate_slot_changes_nothing():
+    x, eidx, w, blobs = _case(*QWEN)
+    eidx2 = torch.cat([eidx, eidx[:, :1]], dim=1)
+    w2 = torch.cat([w, torch.zeros_like(w[:, :1])], dim=1)
+    assert torch.equal(_launch(x, eidx, w, blobs), _launch(x, eidx2, w2, blobs))
+
+
+def test_one_token():
+    x, eidx, w, blobs = _case(*QWEN, tokens=1)
+    assert T.rel_l2(_launch(x, eidx, w, blobs).cpu().numpy(), _oracle(x, eidx, w, blobs)) <= 2e-3
+
+
+def test_a_nan_token_poisons_its_own_row_and_no_other():
+    x, eidx, w, blobs = _case(*QWEN)
+    clean = _launch(x, eidx, w, blobs)
+    x = x.clone()
+    x[0, 5] = float("nan")
+    got = _launch(x, eidx, w, blobs)
+    assert torch.isnan(got[0]).all()
+    assert torch.equal(got[1:], clean[1:])
+
+
+def test_strided_views_are_read_and_written_as_what_they_hold():
+    x, eidx, w, blobs = _case(*QWEN)
+    dense = _launch(x, eidx, w, blobs)
+    wide = torch.zeros(2 * x.shape[0], x.shape[1], dtype=BF, device="cuda")
+    wide[::2] = x
+    assert torch.equal(_launch(wide[::2], eidx, w, blobs), dense)
+    wo = torch.full((2 * x.shape[0], x.shape[1]), 7.0, device="cuda")
+    vb.packed_experts_prefill(x, eidx, w, blobs, wo[::2], None)
+    assert torch.equal(wo[::2], dense) and (wo[1::2] == 7.0).all()
+    x1, e1, w1, b1 = _case(*QWEN, top_k=1, tokens=20)
+    ww = torch.zeros(w1.shape[0], 3, device="cuda")
+    ww[:, 1:2] = w1
+    assert torch.equal(_launch(x1, e1, ww[:, 1:2], b1), _launch(x1, e1, w1, b1))
+
+
+def test_the_blobs_may_be_freed_as_soon_as_the_launch_returns():
+    x, eidx, w, blobs = _case(*QWEN)
+    expected = _launch(x, eidx, w, blobs)
+    mine = {e: {"flat": {n: t.clone() for n, t in b["flat"].items()}, "geom": b["geom"]}
+            for e, b in blobs.items()}
+    sizes = [(t.shape, t.dtype) for b in mine.values() for t in b["flat"].values()]
+    out = torch.empty(x.shape, device="cuda")
+    vb.packed_experts_prefill(x, eidx, w, mine, out, None)
+    del mine
+    junk = [torch.zeros(shape, dtype=dtype, device="cuda") for shape, dtype in sizes]
+    torch.cuda.synchronize()
+    assert torch.equal(out, expected) and len(junk) == len(sizes)
+
+
+def test_a_routed_expert_with_no_entry_contributes_nothing():
+    x, eidx, w, blobs = _case(*QWEN)
+    first = int(eidx[0, 0])
+    missing = {e: b for e, b in blobs.items() if e != first}
+    got = _launch(x, eidx, w, missing)
+    w0 = w.clone()
+    w0[eidx.cuda() == first] = 0.0
+    ref = _launch(x, eidx, w0, blobs)
+    assert torch.allclose(got, ref, rtol=0, atol=1e-6)
+
+
+def test_a_call_mixing_geometries_raises():
+    x, eidx, w, blobs = _case(*QWEN)
+    other = T.make_blobs(2048, 512, 1, gs=64, seed=9)[0]
+    first = int(eidx[0, 0])
+    with pytest.raises(NotImplementedError):
+        _launch(x, eidx, w, {**blobs, first: other})
+
+
+def test_back_to_back_calls_do_not_share_a_table():
+    cases = [_case(*QWEN, tokens=5 + 3 * s, seed=s) for s in range(3 * len(pk._PF_TABLES._slots))]
+    outs = []
+    for x, eidx, w, blobs in cases:
+        out = torch.empty(x.shape, device="cuda")
+        vb.packed_experts_prefill(x, eidx, w, blobs, out, None)
+        outs.append(out)
+    torch.cuda.synchronize()
+    for (x, eidx, w, blobs), out in zip(cases, outs):
+        assert torch.equal(out, _launch(x, eidx, w, blobs))

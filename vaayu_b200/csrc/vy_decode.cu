@@ -1,0 +1,701 @@
+// vy_decode.cu -- the bandwidth-bound expert layer: a token-batched int4 dequant GEMV.
+//
+// Work is cut so that every routed expert's packed weights cross HBM exactly once per call,
+// whatever the number of tokens routed to it:
+//
+//   gate_up_kernel  one warp = 16 rows of one live expert's gate AND up projections, all of
+//                   the expert's tokens (up to 8*NB per pass).  Codes stream through a
+//                   per-warp cp.async ring (128 K elements per stage, kGuDepth stages in
+//                   flight); each thread dequantises the 16-byte chunks it copied itself into
+//                   activation-dtype pairs with two packed ops per pair (sub, mul: the
+//                   reference's exact rounding of every weight) and feeds them to m16n8k16
+//                   tensor-core fragments (fp32 accumulate) whose N dimension is the tokens.
+//                   Epilogue: g, u, SiLU, product, each rounded to the activation dtype, into
+//                   h (stored in the pair-permuted order the down kernel reads).
+//   down_kernel     one CTA = 16 output rows of the down projection; its warps walk the live
+//                   experts, compute y = h . Wd^T for every routed row, multiply by the routing
+//                   weight and park the fp32 contribution in shared memory; the CTA then sums
+//                   each token's contributions in ascending expert id and writes its 16
+//                   columns of `out` -- no atomics, no second pass over HBM.
+//
+// The dequantised operand never touches shared memory, which is what keeps this path on HBM
+// bandwidth: a tcgen05 GEMM would have to write every dequantised weight to shared memory and
+// read it back (2 x 2 bytes per int4 weight), more shared-memory traffic per SM than the SM has
+// at HBM rate, and its smallest tile (M = 64 / 128) would be mostly empty at 1-8 tokens.
+#include "vy_moe.cuh"
+
+namespace vy {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kStageK = 128;    // K elements of one row per pipeline stage (64 bytes of codes)
+constexpr int kGuDepth = 6;     // gate/up ring: stages in flight per warp (2 KB each)
+constexpr int kDnDepth = 8;     // down ring: stages in flight per warp (1 KB each)
+constexpr int kTileRows = 16;
+
+struct GateUpParams {
+    int hidden, inter, gs, top_k;
+    const int64_t* table;
+    int64_t w_off[2], s_off[2], z_off[2];   // gate, up
+    const int32_t* order;
+    const int32_t* live_expert;
+    const int32_t* live_start;
+    const int32_t* unit_start;
+    int32_t* counters;
+    const uint16_t* x_perm;
+    uint16_t* h_perm;
+    uint16_t* h_out;
+};
+
+struct DownParams {
+    int hidden, inter, gs, top_k;
+    int64_t n_tokens;
+    const int64_t* table;
+    int64_t w_off, s_off, z_off;
+    const int32_t* order;
+    const int32_t* live_expert;
+    const int32_t* live_start;
+    const int32_t* slot_order;
+    int32_t* counters;
+    const uint16_t* h_perm;
+    const void* weights;
+    int w_dtype;
+    bool w_round;
+    int64_t w_tok_stride, w_slot_stride;
+    const int32_t* w_index;
+    float* out;
+    int64_t out_stride;
+    float* ybuf_g;      // non-null: contributions to global [n][hidden], no in-CTA combine
+};
+
+// Everything a warp needs about the unit (expert, 16-row tile, token pass) it works on.
+struct Unit {
+    const int32_t* pk;
+    const void* sc;
+    const int32_t* zp;
+    int tile, row0, ncols;   // row0 = first row of this pass in `order`
+    bool ok;
+};
+
+__device__ __forceinline__ int find_live(const int32_t* unit_start, int n_live, int pass_global) {
+    int lo = 0, hi = n_live - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (unit_start[mid] <= pass_global) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+template <int NB>
+__device__ __forceinline__ Unit resolve_gu(const GateUpParams& p, int n_live, int tiles, int u) {
+    Unit un;
+    const int pass_global = u / tiles;
+    un.tile = u - pass_global * tiles;
+    const int li = find_live(p.unit_start, n_live, pass_global);
+    const int pass = pass_global - p.unit_start[li];
+    const int e = p.live_expert[li];
+    const int first = p.live_start[li], count = p.live_start[li + 1] - first;
+    un.row0 = first + pass * NB * 8;
+    un.ncols = min(NB * 8, count - pass * NB * 8);
+    un.pk = reinterpret_cast<const int32_t*>(p.table[3 * e]);
+    un.sc = reinterpret_cast<const void*>(p.table[3 * e + 1]);
+    un.zp = reinterpret_cast<const int32_t*>(p.table[3 * e + 2]);
+    un.ok = ((reinterpret_cast<uintptr_t>(un.pk) & 15u) == 0) && un.pk != nullptr && un.sc != nullptr;
+    return un;
+}
+
+template <int ACT, int SC, bool ZERO>
+__device__ __forceinline__ void load_scale_bias(const void* sc, const int32_t* zp, int64_t s_off,
+                                                int64_t z_off, int row, int groups, int grp,
+                                                uint32_t& s_pair, uint32_t& b_pair) {
+    const float s = round_act<ACT>(load_scale<SC>(sc, s_off + int64_t(row) * groups + grp));
+    const uint32_t sb = act_bits<ACT>(s);
+    s_pair = sb | (sb << 16);
+    uint32_t z = 8u;
+    if constexpr (ZERO) {
+        const uint32_t zw = static_cast<uint32_t>(__ldg(zp + z_off + int64_t(row >> 3) * groups + grp));
+        z = (zw >> (4 * (row & 7))) & 15u;
+    }
+    b_pair = int4_bias_pair<ACT>(z);
+}
+
+template <int ACT>
+__device__ __forceinline__ void dequant4(const uint4& w, uint32_t bias, uint32_t scale,
+                                         uint32_t (&out)[4][4]) {
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int wi = 0; wi < 4; ++wi)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            out[wi][j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[wi], j), bias), scale);
+}
+
+template <int ACT, int SC, bool ZERO, int NB>
+__global__ void __launch_bounds__(kWarps * 32) gate_up_kernel(GateUpParams p) {
+    extern __shared__ uint4 ring[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    uint4* my_ring = ring + warp * (kGuDepth * 4 * 32);
+
+    grid_dependency_wait();
+    grid_dependents_launch();
+
+    const int n_live = p.counters[0];
+    if (n_live <= 0) return;
+    const int tiles = p.inter / kTileRows;
+    const int total_units = p.unit_start[n_live] * tiles;
+    const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+    if (gw >= total_units) return;
+    const int my_units = (total_units - gw + nw - 1) / nw;
+    const int spu = p.hidden / kStageK;
+    const int total_stages = my_units * spu;
+    const int wpr = p.hidden / 8;
+    const int groups = p.hidden / p.gs;
+
+    // issue cursor
+    int iu = -1;
+    Unit iunit{};
+    auto issue = [&](int s) {
+        if (s < total_stages) {
+            const int ui = s / spu, ks = s - ui * spu;
+            if (ui != iu) {
+                iu = ui;
+                iunit = resolve_gu<NB>(p, n_live, tiles, gw + ui * nw);
+            }
+            if (iunit.ok) {
+                const int slot = s % kGuDepth;
+                const int64_t rg = int64_t(iunit.tile * kTileRows + g) * wpr + ks * 16 + tig * 4;
+                const int32_t* src_g = iunit.pk + p.w_off[0] + rg;
+                const int32_t* src_u = iunit.pk + p.w_off[1] + rg;
+                uint4* dst = my_ring + slot * 128 + lane;
+                cp_async16(dst, src_g);
+                cp_async16(dst + 32, src_g + 8 * wpr);
+                cp_async16(dst + 64, src_u);
+                cp_async16(dst + 96, src_u + 8 * wpr);
+            }
+        }
+        cp_async_commit();
+    };
+
+#pragma unroll
+    for (int s = 0; s < kGuDepth - 1; ++s) issue(s);
+
+    float acc_g[NB][4], acc_u[NB][4];
+#pragma unroll
+    for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc_g[cb][i] = acc_u[cb][i] = 0.f;
+
+    int cu = -1;
+    Unit cunit{};
+    int xoff[NB];
+    for (int s = 0; s < total_stages; ++s) {
+        issue(s + kGuDepth - 1);
+        const int ui = s / spu, ks = s - ui * spu;
+        if (ui != cu) {
+            cu = ui;
+            cunit = resolve_gu<NB>(p, n_live, tiles, gw + ui * nw);
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb) {
+                const int col = cb * 8 + g;
+                xoff[cb] = col < cunit.ncols ? (p.order[cunit.row0 + col] / p.top_k) * p.hidden : -1;
+            }
+            if (!cunit.ok && lane == 0) atomicOr(p.counters + 2, 1);
+        }
+        cp_async_wait<kGuDepth - 1>();
+        if (cunit.ok) {
+            const uint4* st = my_ring + (s % kGuDepth) * 128 + lane;
+            const uint4 wg0 = st[0], wg8 = st[32], wu0 = st[64], wu8 = st[96];
+            const int row = cunit.tile * kTileRows + g;
+            const int grp = (ks * kStageK + tig * 32) / p.gs;
+            uint32_t sg0, bg0, sg8, bg8, su0, bu0, su8, bu8;
+            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[0], p.z_off[0], row, groups, grp, sg0, bg0);
+            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[0], p.z_off[0], row + 8, groups, grp, sg8, bg8);
+            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[1], p.z_off[1], row, groups, grp, su0, bu0);
+            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[1], p.z_off[1], row + 8, groups, grp, su8, bu8);
+            const int kx = ks * kStageK + tig * 32;
+            const uint32_t wgw0[4] = {wg0.x, wg0.y, wg0.z, wg0.w}, wgw8[4] = {wg8.x, wg8.y, wg8.z, wg8.w};
+            const uint32_t wuw0[4] = {wu0.x, wu0.y, wu0.z, wu0.w}, wuw8[4] = {wu8.x, wu8.y, wu8.z, wu8.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                uint32_t ag0[4], ag8[4], au0[4], au8[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    ag0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wgw0[wi], j), bg0), sg0);
+                    ag8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wgw8[wi], j), bg8), sg8);
+                    au0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wuw0[wi], j), bu0), su0);
+                    au8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wuw8[wi], j), bu8), su8);
+                }
+#pragma unroll
+                for (int cb = 0; cb < NB; ++cb) {
+                    uint4 xv = make_uint4(0u, 0u, 0u, 0u);
+                    if (xoff[cb] >= 0) xv = ld_nc_v4(p.x_perm + xoff[cb] + kx + wi * 8);
+                    mma_16816<ACT>(acc_g[cb], ag0[0], ag8[0], ag0[1], ag8[1], xv.x, xv.y);
+                    mma_16816<ACT>(acc_g[cb], ag0[2], ag8[2], ag0[3], ag8[3], xv.z, xv.w);
+                    mma_16816<ACT>(acc_u[cb], au0[0], au8[0], au0[1], au8[1], xv.x, xv.y);
+                    mma_16816<ACT>(acc_u[cb], au0[2], au8[2], au0[3], au8[3], xv.z, xv.w);
+                }
+            }
+        }
+        if (ks == spu - 1) {
+            if (cunit.ok) {
+#pragma unroll
+                for (int cb = 0; cb < NB; ++cb) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int col = cb * 8 + 2 * tig + (i & 1);
+                        if (col < cunit.ncols) {
+                            const int r = cunit.tile * kTileRows + g + 8 * (i >> 1);
+                            const int rowid = p.order[cunit.row0 + col];
+                            const float gv = round_act<ACT>(acc_g[cb][i]);
+                            const float uv = round_act<ACT>(acc_u[cb][i]);
+                            const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
+                            const uint32_t hb = act_bits<ACT>(__fmul_rn(av, uv));
+                            p.h_perm[int64_t(rowid) * p.inter + perm8(r)] = static_cast<uint16_t>(hb);
+                            if (p.h_out) p.h_out[int64_t(rowid) * p.inter + r] = static_cast<uint16_t>(hb);
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc_g[cb][i] = acc_u[cb][i] = 0.f;
+        }
+    }
+    cp_async_wait<0>();
+}
+
+template <int ACT, int SC, bool ZERO, int NB>
+__global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
+    extern __shared__ uint4 ring[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    uint4* my_ring = ring + warp * (kDnDepth * 2 * 32);
+    float* ybuf = reinterpret_cast<float*>(ring + kWarps * kDnDepth * 2 * 32);
+    const int tile = blockIdx.x;
+
+    grid_dependency_wait();
+
+    const int n_live = p.counters[0];
+    const int spu = p.inter / kStageK;
+    const int wpr = p.inter / 8;
+    const int groups = p.inter / p.gs;
+    constexpr int kCols = NB * 8;
+
+    // The warp's work: experts li = warp, warp + kWarps, ...; each in ceil(count / kCols) passes.
+    // Cursor over (li, pass, ks).
+    struct Cursor {
+        int li, pass, npass, ks;
+    };
+    auto npass_of = [&](int li) -> int {
+        if (li >= n_live) return 0;
+        const int c = p.live_start[li + 1] - p.live_start[li];
+        return (c + kCols - 1) / kCols;
+    };
+    auto advance = [&](Cursor& c) {
+        if (++c.ks == spu) {
+            c.ks = 0;
+            if (++c.pass == c.npass) {
+                c.pass = 0;
+                c.li += kWarps;
+                c.npass = npass_of(c.li);
+            }
+        }
+    };
+    Cursor ic{warp, 0, npass_of(warp), 0};
+    int ic_li = -1;
+    const int32_t* ipk = nullptr;
+    bool iok = false;
+    int s_issue = 0;
+    auto issue = [&]() {
+        if (ic.li < n_live) {
+            if (ic.li != ic_li) {
+                ic_li = ic.li;
+                const int e = p.live_expert[ic.li];
+                ipk = reinterpret_cast<const int32_t*>(p.table[3 * e]);
+                iok = ipk != nullptr && (reinterpret_cast<uintptr_t>(ipk) & 15u) == 0;
+            }
+            if (iok) {
+                const int slot = s_issue % kDnDepth;
+                const int32_t* src = ipk + p.w_off + int64_t(tile * kTileRows + g) * wpr + ic.ks * 16 + tig * 4;
+                uint4* dst = my_ring + slot * 64 + lane;
+                cp_async16(dst, src);
+                cp_async16(dst + 32, src + 8 * wpr);
+            }
+            advance(ic);
+        }
+        ++s_issue;
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int s = 0; s < kDnDepth - 1; ++s) issue();
+
+    Cursor cc{warp, 0, npass_of(warp), 0};
+    int cc_li = -1;
+    const void* csc = nullptr;
+    const int32_t* czp = nullptr;
+    bool cok = false;
+    int hoff[NB];
+    int row0 = 0, ncols = 0;
+    float acc[NB][4];
+#pragma unroll
+    for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[cb][i] = 0.f;
+
+    for (int s = 0; cc.li < n_live; ++s) {
+        issue();
+        if (cc.ks == 0) {
+            if (cc.li != cc_li) {
+                cc_li = cc.li;
+                const int e = p.live_expert[cc.li];
+                const int32_t* pk = reinterpret_cast<const int32_t*>(p.table[3 * e]);
+                csc = reinterpret_cast<const void*>(p.table[3 * e + 1]);
+                czp = reinterpret_cast<const int32_t*>(p.table[3 * e + 2]);
+                cok = pk != nullptr && csc != nullptr && (reinterpret_cast<uintptr_t>(pk) & 15u) == 0;
+                if (!cok && lane == 0) atomicOr(p.counters + 2, 1);
+            }
+            const int first = p.live_start[cc.li], count = p.live_start[cc.li + 1] - first;
+            row0 = first + cc.pass * kCols;
+            ncols = min(kCols, count - cc.pass * kCols);
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb) {
+                const int col = cb * 8 + g;
+                hoff[cb] = col < ncols ? p.order[row0 + col] * p.inter : -1;
+            }
+        }
+        cp_async_wait<kDnDepth - 1>();
+        if (cok) {
+            const uint4* st = my_ring + (s % kDnDepth) * 64 + lane;
+            const uint4 w0 = st[0], w8 = st[32];
+            const int row = tile * kTileRows + g;
+            const int grp = (cc.ks * kStageK + tig * 32) / p.gs;
+            uint32_t s0, b0, s8, b8;
+            load_scale_bias<ACT, SC, ZERO>(csc, czp, p.s_off, p.z_off, row, groups, grp, s0, b0);
+            load_scale_bias<ACT, SC, ZERO>(csc, czp, p.s_off, p.z_off, row + 8, groups, grp, s8, b8);
+            const int kh = cc.ks * kStageK + tig * 32;
+            const uint32_t ww0[4] = {w0.x, w0.y, w0.z, w0.w}, ww8[4] = {w8.x, w8.y, w8.z, w8.w};
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi) {
+                uint32_t a0[4], a8[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    a0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(ww0[wi], j), b0), s0);
+                    a8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(ww8[wi], j), b8), s8);
+                }
+#pragma unroll
+                for (int cb = 0; cb < NB; ++cb) {
+                    uint4 hv = make_uint4(0u, 0u, 0u, 0u);
+                    if (hoff[cb] >= 0) hv = ld_nc_v4(p.h_perm + hoff[cb] + kh + wi * 8);
+                    mma_16816<ACT>(acc[cb], a0[0], a8[0], a0[1], a8[1], hv.x, hv.y);
+                    mma_16816<ACT>(acc[cb], a0[2], a8[2], a0[3], a8[3], hv.z, hv.w);
+                }
+            }
+        }
+        if (cc.ks == spu - 1) {
+            if (cok) {
+#pragma unroll
+                for (int cb = 0; cb < NB; ++cb) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int col = cb * 8 + 2 * tig + (i & 1);
+                        if (col < ncols) {
+                            const int r = g + 8 * (i >> 1);
+                            const int rowid = p.order[row0 + col];
+                            const int64_t t = rowid / p.top_k;
+                            const int k = rowid - int(t) * p.top_k;
+                            const int widx = p.w_index ? p.w_index[rowid] : k;
+                            const float wv = load_as_float(p.weights, p.w_dtype,
+                                                           t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
+                            float c = __fmul_rn(round_act<ACT>(acc[cb][i]), wv);
+                            if (p.w_round) c = round_act<ACT>(c);
+                            if (p.ybuf_g) p.ybuf_g[int64_t(rowid) * p.hidden + tile * kTileRows + r] = c;
+                            else ybuf[rowid * kTileRows + r] = c;
+                        }
+                    }
+                }
+            }
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[cb][i] = 0.f;
+        }
+        advance(cc);
+    }
+    cp_async_wait<0>();
+    if (p.ybuf_g) return;
+    __syncthreads();
+    // each token's 16 columns: contributions in ascending expert id, then slot
+    const int K = p.top_k;
+    for (int64_t idx = threadIdx.x; idx < p.n_tokens * kTileRows; idx += blockDim.x) {
+        const int64_t t = idx / kTileRows;
+        const int r = static_cast<int>(idx - t * kTileRows);
+        float a = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const int rowid = p.slot_order[t * K + k];
+            if (rowid >= 0) a += ybuf[rowid * kTileRows + r];
+        }
+        p.out[t * p.out_stride + tile * kTileRows + r] = a;
+    }
+}
+
+// ── host side ─────────────────────────────────────────────────────────────────────────────
+
+size_t gu_smem() { return size_t(kWarps) * kGuDepth * 4 * 32 * sizeof(uint4); }
+size_t dn_ring_smem() { return size_t(kWarps) * kDnDepth * 2 * 32 * sizeof(uint4); }
+constexpr size_t kDnSmemCap = 200 * 1024;
+
+template <typename Kernel, typename Params>
+cudaError_t launch_pdl(Kernel kernel, int grid, size_t smem, cudaStream_t s, const Params& prm) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kWarps * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, prm);
+}
+
+template <int ACT, int SC, bool ZERO, int NB>
+int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, size_t dn_smem,
+               cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+    // Resident CTAs per SM of the persistent gate/up grid, from the occupancy calculator (the
+    // warp -> unit assignment is static, so the whole grid must be resident at once).
+    static int gu_blocks_per_sm = 0;
+    if (gu_blocks_per_sm == 0) {
+        cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(gu_smem()));
+        cudaFuncSetAttribute(down_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kDnSmemCap));
+        int nblk = 0;
+        cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &nblk, gate_up_kernel<ACT, SC, ZERO, NB>, kWarps * 32, gu_smem());
+        if (oe != cudaSuccess || nblk < 1)
+            return fail(VY_ERR_CUDA, "gate/up occupancy: %s", cudaGetErrorString(oe));
+        gu_blocks_per_sm = nblk;
+    }
+    const int gu_grid = gu_blocks_per_sm * sm_count;
+    cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_grid, gu_smem(), s, gu);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
+    if (timed) cudaEventRecord(ev[2], s);
+    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn.hidden / kTileRows, dn_smem, s, dn);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "down launch: %s", cudaGetErrorString(e));
+    return check_launch("vy_moe_decode");
+}
+
+template <int ACT, int SC, bool ZERO>
+int dispatch_nb(int nb, const GateUpParams& gu, const DownParams& dn, int sm_count, size_t dn_smem,
+                cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+    if (nb == 1) return run_decode<ACT, SC, ZERO, 1>(gu, dn, sm_count, dn_smem, s, ev, timed);
+    if (nb == 2) return run_decode<ACT, SC, ZERO, 2>(gu, dn, sm_count, dn_smem, s, ev, timed);
+    return run_decode<ACT, SC, ZERO, 4>(gu, dn, sm_count, dn_smem, s, ev, timed);
+}
+
+template <int ACT, int SC>
+int dispatch_zero(bool zero, int nb, const GateUpParams& gu, const DownParams& dn, int sm_count,
+                  size_t dn_smem, cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+    return zero ? dispatch_nb<ACT, SC, true>(nb, gu, dn, sm_count, dn_smem, s, ev, timed)
+                : dispatch_nb<ACT, SC, false>(nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+}
+
+template <int ACT>
+int dispatch_sc(int sc, bool zero, int nb, const GateUpParams& gu, const DownParams& dn, int sm_count,
+                size_t dn_smem, cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+    switch (sc) {
+        case VY_BF16: return dispatch_zero<ACT, VY_BF16>(zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+        case VY_F16: return dispatch_zero<ACT, VY_F16>(zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+        default: return dispatch_zero<ACT, VY_F32>(zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+    }
+}
+
+struct DecodeLayout {
+    int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters;
+    uint16_t *x_perm, *h_perm;
+    float* ybuf_g;
+    size_t bytes;
+    bool combine_in_cta;
+};
+
+int nb_for(int64_t n_tokens) { return n_tokens <= 8 ? 1 : (n_tokens <= 16 ? 2 : 4); }
+
+DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
+    const int64_t n = c->n_tokens * c->top_k;
+    const int E = c->n_experts;
+    const int64_t H = c->geom->hidden, I = c->geom->inter;
+    Carve cv{static_cast<char*>(base), 0};
+    DecodeLayout L{};
+    L.order = cv.take<int32_t>(n);
+    L.live_expert = cv.take<int32_t>(E);
+    L.live_start = cv.take<int32_t>(E + 1);
+    L.unit_start = cv.take<int32_t>(E + 1);
+    L.slot_order = cv.take<int32_t>(n);
+    L.counters = cv.take<int32_t>(4);
+    L.x_perm = cv.take<uint16_t>(c->n_tokens * H);
+    L.h_perm = cv.take<uint16_t>(n * I);
+    const size_t ybuf_bytes = size_t(n) * kTileRows * sizeof(float);
+    L.combine_in_cta = (c->contrib == nullptr) && (dn_ring_smem() + ybuf_bytes <= kDnSmemCap);
+    L.ybuf_g = nullptr;
+    if (c->contrib == nullptr && !L.combine_in_cta) L.ybuf_g = cv.take<float>(n * H);
+    L.bytes = cv.used;
+    return L;
+}
+
+}  // namespace
+
+// Shared validation of a vy_moe_call (decode and prefill).
+int validate_call(const vy_moe_call* c) {
+    if (!c || !c->geom) return fail(VY_ERR_INVALID, "null call or geometry");
+    const vy_expert_geom& g = *c->geom;
+    if (g.bits != 4) return fail(VY_ERR_UNSUPPORTED, "bits %d: the expert kernels take int4", g.bits);
+    if (g.group_size < 32 || (g.group_size & (g.group_size - 1)))
+        return fail(VY_ERR_UNSUPPORTED, "group size %d (a power of two >= 32)", g.group_size);
+    if (g.hidden <= 0 || g.inter <= 0 || g.hidden % 128 || g.inter % 128)
+        return fail(VY_ERR_UNSUPPORTED, "hidden %d / intermediate %d: both must be multiples of 128",
+                    g.hidden, g.inter);
+    if (g.hidden % g.group_size || g.inter % g.group_size)
+        return fail(VY_ERR_UNSUPPORTED, "group size %d does not divide hidden %d / intermediate %d",
+                    g.group_size, g.hidden, g.inter);
+    if (g.scale_dtype != VY_BF16 && g.scale_dtype != VY_F16 && g.scale_dtype != VY_F32)
+        return fail(VY_ERR_UNSUPPORTED, "scale dtype %d", g.scale_dtype);
+    for (int r = 0; r < 3; ++r)
+        if (g.word_off[r] % 4 || g.word_off[r] < 0)
+            return fail(VY_ERR_ALIGNMENT, "role %d starts at word %lld (not 16-byte aligned)", r,
+                        (long long)g.word_off[r]);
+    if (c->act_dtype != VY_BF16 && c->act_dtype != VY_F16)
+        return fail(VY_ERR_UNSUPPORTED, "activation dtype %d (bf16 / fp16)", c->act_dtype);
+    if (c->w_dtype != VY_BF16 && c->w_dtype != VY_F16 && c->w_dtype != VY_F32)
+        return fail(VY_ERR_UNSUPPORTED, "routing-weight dtype %d", c->w_dtype);
+    if (c->ids_dtype != VY_I32 && c->ids_dtype != VY_I64)
+        return fail(VY_ERR_UNSUPPORTED, "expert-id dtype %d", c->ids_dtype);
+    int st = plan_validate(c->n_tokens, c->top_k, c->n_experts);
+    if (st != VY_OK) return st;
+    const int64_t n = c->n_tokens * c->top_k;
+    if (c->n_tokens * int64_t(g.hidden) >= (int64_t(1) << 31) || n * int64_t(g.inter) >= (int64_t(1) << 31) ||
+        n * int64_t(g.hidden) >= (int64_t(1) << 31))
+        return fail(VY_ERR_UNSUPPORTED, "call too large for 32-bit element offsets");
+    if (c->n_tokens > 0) {
+        if (!c->x || !c->expert_table || !c->expert_ids || !c->weights)
+            return fail(VY_ERR_INVALID, "null input pointer");
+        if (!c->out && !c->contrib) return fail(VY_ERR_INVALID, "neither out nor contrib given");
+        if (c->x_row_stride < g.hidden) return fail(VY_ERR_INVALID, "x row stride %lld", (long long)c->x_row_stride);
+        if (c->out && !c->contrib && c->out_row_stride < g.hidden)
+            return fail(VY_ERR_INVALID, "out row stride %lld", (long long)c->out_row_stride);
+    }
+    return VY_OK;
+}
+
+}  // namespace vy
+
+using namespace vy;
+
+extern "C" size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path) {
+    if (!call || !call->geom) return 0;
+    if (path == 1) return prefill_workspace_bytes(call);
+    return decode_layout(call, nullptr).bytes + 256;
+}
+
+extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if ((st = validate_call(c)) != VY_OK) return st;
+    if (c->n_tokens == 0) return ok();
+    DecodeLayout L = decode_layout(c, nullptr);
+    if (!c->workspace || c->workspace_bytes < L.bytes + 256)
+        return fail(VY_ERR_WORKSPACE, "workspace %zu bytes, %zu needed", c->workspace_bytes, L.bytes + 256);
+    char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 255) & ~uintptr_t(255));
+    L = decode_layout(c, base);
+    const vy_expert_geom& g = *c->geom;
+    cudaStream_t s = as_stream(stream);
+    const int nb = nb_for(c->n_tokens);
+
+    PlanArgs pa{};
+    pa.ids = c->expert_ids;
+    pa.ids64 = c->ids_dtype == VY_I64;
+    pa.n_tokens = c->n_tokens;
+    pa.top_k = c->top_k;
+    pa.n_experts = c->n_experts;
+    pa.order = L.order;
+    pa.live_expert = L.live_expert;
+    pa.live_start = L.live_start;
+    pa.unit_start = L.unit_start;
+    pa.slot_order = L.slot_order;
+    pa.counters = L.counters;
+    pa.tok_per_unit = nb * 8;
+    pa.x = c->x;
+    pa.x_stride = c->x_row_stride;
+    pa.x_vec = aligned16(c->x) && (c->x_row_stride % 8 == 0);
+    pa.hidden = g.hidden;
+    pa.x_perm = L.x_perm;
+    cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
+    const bool timed = ev != nullptr && c->n_stage_events >= 4;
+    if (timed) cudaEventRecord(ev[0], s);
+    if ((st = launch_plan(pa, dev->sm_count, s)) != VY_OK) return st;
+    if (timed) cudaEventRecord(ev[1], s);
+
+    GateUpParams gu{};
+    gu.hidden = g.hidden;
+    gu.inter = g.inter;
+    gu.gs = g.group_size;
+    gu.top_k = c->top_k;
+    gu.table = c->expert_table;
+    gu.w_off[0] = g.word_off[0];
+    gu.w_off[1] = g.word_off[1];
+    gu.s_off[0] = g.scale_off[0];
+    gu.s_off[1] = g.scale_off[1];
+    gu.z_off[0] = g.zero_off[0];
+    gu.z_off[1] = g.zero_off[1];
+    gu.order = L.order;
+    gu.live_expert = L.live_expert;
+    gu.live_start = L.live_start;
+    gu.unit_start = L.unit_start;
+    gu.counters = L.counters;
+    gu.x_perm = L.x_perm;
+    gu.h_perm = L.h_perm;
+    gu.h_out = static_cast<uint16_t*>(c->h_out);
+
+    DownParams dn{};
+    dn.hidden = g.hidden;
+    dn.inter = g.inter;
+    dn.gs = g.group_size;
+    dn.top_k = c->top_k;
+    dn.n_tokens = c->n_tokens;
+    dn.table = c->expert_table;
+    dn.w_off = g.word_off[2];
+    dn.s_off = g.scale_off[2];
+    dn.z_off = g.zero_off[2];
+    dn.order = L.order;
+    dn.live_expert = L.live_expert;
+    dn.live_start = L.live_start;
+    dn.slot_order = L.slot_order;
+    dn.counters = L.counters;
+    dn.h_perm = L.h_perm;
+    dn.weights = c->weights;
+    dn.w_dtype = c->w_dtype;
+    dn.w_round = c->w_dtype == c->act_dtype;
+    dn.w_tok_stride = c->w_tok_stride;
+    dn.w_slot_stride = c->w_slot_stride;
+    dn.w_index = c->w_index;
+    dn.out = c->out;
+    dn.out_stride = c->out_row_stride;
+    dn.ybuf_g = c->contrib ? c->contrib : L.ybuf_g;
+
+    const int sm_count = dev->sm_count;
+    const size_t dn_smem = dn_ring_smem() + (L.combine_in_cta ? size_t(c->n_tokens * c->top_k) * kTileRows * sizeof(float) : 0);
+    const bool zero = g.has_zero != 0;
+    st = c->act_dtype == VY_BF16 ? dispatch_sc<VY_BF16>(g.scale_dtype, zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed)
+                                 : dispatch_sc<VY_F16>(g.scale_dtype, zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+    if (st != VY_OK) return st;
+    if (!c->contrib && !L.combine_in_cta)
+        st = launch_combine(L.ybuf_g, c->expert_ids, c->ids_dtype == VY_I64, c->n_tokens, c->top_k,
+                            g.hidden, c->out, c->out_row_stride, dev->sm_count, s);
+    if (st != VY_OK) return st;
+    if (timed) cudaEventRecord(ev[3], s);
+    return ok();
+}

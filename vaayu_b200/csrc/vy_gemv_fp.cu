@@ -1,0 +1,231 @@
+// vy_gemv_fp.cu -- FP8-e4m3 / FP4-e2m1 block-scaled dequant fused into a decode GEMV
+// (batch <= 16): y[t, n] = bf16(sum_k deq(W)[n, k] * x[t, k]), fp32 accumulation.
+//
+// One CTA = 16 weight rows; its 8 warps split K into 8 contiguous ranges (split-K inside the
+// CTA, so the grid has n/16 CTAs even for a single output tile row), each warp streams its
+// range with 128-bit no-allocate loads, dequantises into bf16 pairs in registers (exactly the
+// values vy_fp8_dequant / vy_fp4_dequant produce) and accumulates m16n8k16 tensor-core
+// fragments whose N dimension is the tokens.  The 8 partial tiles are summed in warp order in
+// shared memory: the result does not depend on scheduling.
+#include <cuda_fp8.h>
+
+#include "vy_common.cuh"
+
+namespace vy {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kUnroll = 4;
+
+__device__ __forceinline__ float e4m3f(uint32_t b) {
+    __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b & 0xFFu), __NV_E4M3);
+    return __half2float(__half(h));
+}
+
+__device__ __forceinline__ float e2m1f(uint32_t nib) {
+    uint32_t e = (nib >> 1) & 3u, m = nib & 1u;
+    uint32_t bits = e ? (((e + 126u) << 23) | (m << 22)) : (m ? 0x3F000000u : 0u);
+    return __uint_as_float(bits | ((nib & 8u) << 28));
+}
+
+__device__ __forceinline__ float block_scale(const void* p, int dtype, int64_t i) {
+    switch (dtype) {
+        case VY_F32: return __ldg(reinterpret_cast<const float*>(p) + i);
+        case VY_BF16: return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16*>(p) + i));
+        case VY_F16: return __half2float(__ldg(reinterpret_cast<const __half*>(p) + i));
+        default: {
+            uint8_t b = __ldg(reinterpret_cast<const uint8_t*>(p) + i);
+            if (b == 0xFF) return __int_as_float(0x7FC00000);
+            if (b == 0) return 5.877471754111438e-39f;
+            return __int_as_float(static_cast<int>(b) << 23);
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t bf16_pair(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+struct GemvParams {
+    const uint8_t* w;
+    int64_t n, k;
+    const void* scale;
+    int scale_dtype;
+    int64_t srows, scols, bo, bi;   // fp8 block scales
+    int gs;                         // fp4 group
+    const __nv_bfloat16* x;
+    int64_t x_stride;
+    int n_tokens;
+    __nv_bfloat16* out;
+    int64_t out_stride;
+};
+
+// KIND 0: fp8 (16 B = 16 codes of a row per thread per step; a step covers 64 K per row)
+// KIND 1: fp4 (16 B = 32 codes; a step covers 128 K per row)
+template <int KIND, int NB>
+__global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
+    constexpr int kPerThread = KIND == 0 ? 16 : 32;    // K elements per thread per step
+    constexpr int kStepK = 4 * kPerThread;             // K per step per row
+    __shared__ float part[kWarps][16][NB * 8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const int64_t row0 = int64_t(blockIdx.x) * 16;
+    const int64_t steps = p.k / kStepK;
+    const int64_t per_warp = (steps + kWarps - 1) / kWarps;
+    const int64_t s_lo = warp * per_warp, s_hi = min(steps, s_lo + per_warp);
+    const int64_t rA = row0 + g, rB = row0 + g + 8;
+    const bool okA = rA < p.n, okB = rB < p.n;
+    const int64_t row_bytes = KIND == 0 ? p.k : p.k / 2;
+    const uint8_t* wA = p.w + (okA ? rA : 0) * row_bytes;
+    const uint8_t* wB = p.w + (okB ? rB : 0) * row_bytes;
+
+    float acc[NB][4];
+#pragma unroll
+    for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[cb][i] = 0.f;
+
+    for (int64_t s0 = s_lo; s0 < s_hi; s0 += kUnroll) {
+        uint4 va[kUnroll], vb[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t s = s0 + u;
+            const int64_t off = (s * kStepK + tig * kPerThread) / (KIND == 0 ? 1 : 2);
+            va[u] = make_uint4(0, 0, 0, 0);
+            vb[u] = make_uint4(0, 0, 0, 0);
+            if (s < s_hi) {
+                if (okA) va[u] = ld_nc_v4(wA + off);
+                if (okB) vb[u] = ld_nc_v4(wB + off);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t s = s0 + u;
+            if (s >= s_hi) break;
+            const int64_t k0 = s * kStepK + tig * kPerThread;
+            float sa, sb;
+            if constexpr (KIND == 0) {
+                sa = okA ? block_scale(p.scale, p.scale_dtype, (rA / p.bo) * p.scols + k0 / p.bi) : 0.f;
+                sb = okB ? block_scale(p.scale, p.scale_dtype, (rB / p.bo) * p.scols + k0 / p.bi) : 0.f;
+            }
+            const uint32_t wa[4] = {va[u].x, va[u].y, va[u].z, va[u].w};
+            const uint32_t wb[4] = {vb[u].x, vb[u].y, vb[u].z, vb[u].w};
+            // mma step q covers this thread's elements 4q..4q+3 (fp8) / 4q..4q+3 (fp4)
+            constexpr int kSteps = kPerThread / 4;
+#pragma unroll
+            for (int q = 0; q < kSteps; ++q) {
+                uint32_t a0, a1, a2, a3;
+                if constexpr (KIND == 0) {
+                    const uint32_t xa = wa[q], xb = wb[q];   // 4 codes: elements 4q..4q+3
+                    a0 = bf16_pair(__fmul_rn(e4m3f(xa), sa), __fmul_rn(e4m3f(xa >> 8), sa));
+                    a2 = bf16_pair(__fmul_rn(e4m3f(xa >> 16), sa), __fmul_rn(e4m3f(xa >> 24), sa));
+                    a1 = bf16_pair(__fmul_rn(e4m3f(xb), sb), __fmul_rn(e4m3f(xb >> 8), sb));
+                    a3 = bf16_pair(__fmul_rn(e4m3f(xb >> 16), sb), __fmul_rn(e4m3f(xb >> 24), sb));
+                } else {
+                    const int64_t gi = (k0 + 4 * q) / p.gs;
+                    const float fa = okA ? e4m3f(__ldg(reinterpret_cast<const uint8_t*>(p.scale) + rA * (p.k / p.gs) + gi)) : 0.f;
+                    const float fb = okB ? e4m3f(__ldg(reinterpret_cast<const uint8_t*>(p.scale) + rB * (p.k / p.gs) + gi)) : 0.f;
+                    const uint32_t xa = (wa[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;   // 4 nibbles
+                    const uint32_t xb = (wb[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
+                    a0 = bf16_pair(__fmul_rn(e2m1f(xa), fa), __fmul_rn(e2m1f(xa >> 4), fa));
+                    a2 = bf16_pair(__fmul_rn(e2m1f(xa >> 8), fa), __fmul_rn(e2m1f(xa >> 12), fa));
+                    a1 = bf16_pair(__fmul_rn(e2m1f(xb), fb), __fmul_rn(e2m1f(xb >> 4), fb));
+                    a3 = bf16_pair(__fmul_rn(e2m1f(xb >> 8), fb), __fmul_rn(e2m1f(xb >> 12), fb));
+                }
+#pragma unroll
+                for (int cb = 0; cb < NB; ++cb) {
+                    const int t = cb * 8 + g;
+                    uint2 xv = make_uint2(0u, 0u);
+                    if (t < p.n_tokens)
+                        xv = *reinterpret_cast<const uint2*>(p.x + int64_t(t) * p.x_stride + k0 + 4 * q);
+                    mma_16816<VY_BF16>(acc[cb], a0, a1, a2, a3, xv.x, xv.y);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) part[warp][g + 8 * (i >> 1)][cb * 8 + 2 * tig + (i & 1)] = acc[cb][i];
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < 16 * NB * 8; idx += blockDim.x) {
+        const int r = idx / (NB * 8), t = idx % (NB * 8);
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) a += part[w][r][t];
+        if (t < p.n_tokens && row0 + r < p.n)
+            p.out[int64_t(t) * p.out_stride + row0 + r] = __float2bfloat16_rn(a);
+    }
+}
+
+int launch_gemv(int kind, const GemvParams& p, cudaStream_t s) {
+    const unsigned grid = static_cast<unsigned>((p.n + 15) / 16);
+    const bool two = p.n_tokens > 8;
+    if (kind == 0) {
+        if (two) fp_gemv_kernel<0, 2><<<grid, kWarps * 32, 0, s>>>(p);
+        else fp_gemv_kernel<0, 1><<<grid, kWarps * 32, 0, s>>>(p);
+    } else {
+        if (two) fp_gemv_kernel<1, 2><<<grid, kWarps * 32, 0, s>>>(p);
+        else fp_gemv_kernel<1, 1><<<grid, kWarps * 32, 0, s>>>(p);
+    }
+    return check_launch(kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv");
+}
+
+int common_checks(const uint8_t* w, int64_t n, int64_t k, const void* x, int64_t x_stride,
+                  int64_t n_tokens, void* out, int64_t out_stride, int64_t step) {
+    if (n < 0 || k < 0 || n_tokens < 0) return fail(VY_ERR_INVALID, "negative size");
+    if (n_tokens > 16) return fail(VY_ERR_UNSUPPORTED, "batch %lld > 16", (long long)n_tokens);
+    if (k % step) return fail(VY_ERR_UNSUPPORTED, "k %lld is not a multiple of %lld", (long long)k, (long long)step);
+    if (n == 0 || n_tokens == 0) return VY_OK;
+    if (!w || !x || !out) return fail(VY_ERR_INVALID, "null pointer");
+    if (!aligned16(w)) return fail(VY_ERR_ALIGNMENT, "weight not 16-byte aligned");
+    if ((reinterpret_cast<uintptr_t>(x) & 7u) || (x_stride % 4))
+        return fail(VY_ERR_ALIGNMENT, "x must be 8-byte aligned with a row stride multiple of 4");
+    if (x_stride < k || out_stride < n) return fail(VY_ERR_INVALID, "row stride too small");
+    return VY_OK;
+}
+
+}  // namespace
+}  // namespace vy
+
+using namespace vy;
+
+extern "C" int vy_fp8_gemv(const uint8_t* w, int64_t n, int64_t k, const void* scale,
+                           int32_t scale_dtype, int64_t srows, int64_t scols, const void* x,
+                           int64_t x_stride, int64_t n_tokens, void* out, int64_t out_stride,
+                           void* stream) {
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if ((st = common_checks(w, n, k, x, x_stride, n_tokens, out, out_stride, 64)) != VY_OK) return st;
+    if (n == 0 || n_tokens == 0) return ok();
+    if (srows <= 0 || scols <= 0 || n % srows || k % scols)
+        return fail(VY_ERR_INVALID, "scale [%lld, %lld] does not tile [%lld, %lld]", (long long)srows,
+                    (long long)scols, (long long)n, (long long)k);
+    if ((k / scols) % 16) return fail(VY_ERR_UNSUPPORTED, "fp8 block width %lld (multiple of 16)", (long long)(k / scols));
+    if (scale_dtype != VY_F32 && scale_dtype != VY_BF16 && scale_dtype != VY_F16 && scale_dtype != VY_E8M0)
+        return fail(VY_ERR_UNSUPPORTED, "block-scale dtype %d", scale_dtype);
+    if (!scale) return fail(VY_ERR_INVALID, "null scale");
+    GemvParams p{w, n, k, scale, scale_dtype, srows, scols, n / srows, k / scols, 0,
+                 reinterpret_cast<const __nv_bfloat16*>(x), x_stride, static_cast<int>(n_tokens),
+                 reinterpret_cast<__nv_bfloat16*>(out), out_stride};
+    return launch_gemv(0, p, as_stream(stream));
+}
+
+extern "C" int vy_fp4_gemv(const uint8_t* w, int64_t n, int64_t k, const uint8_t* scale,
+                           int32_t group_size, const void* x, int64_t x_stride, int64_t n_tokens,
+                           void* out, int64_t out_stride, void* stream) {
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if ((st = common_checks(w, n, k, x, x_stride, n_tokens, out, out_stride, 128)) != VY_OK) return st;
+    if (n == 0 || n_tokens == 0) return ok();
+    if (group_size <= 0 || group_size % 4 || k % group_size)
+        return fail(VY_ERR_UNSUPPORTED, "fp4 group %d", group_size);
+    if (!scale) return fail(VY_ERR_INVALID, "null scale");
+    GemvParams p{w, n, k, scale, VY_E4M3, 0, 0, 0, 0, group_size,
+                 reinterpret_cast<const __nv_bfloat16*>(x), x_stride, static_cast<int>(n_tokens),
+                 reinterpret_cast<__nv_bfloat16*>(out), out_stride};
+    return launch_gemv(1, p, as_stream(stream));
+}

@@ -1,0 +1,56 @@
+// vy_moe.cuh -- internal interfaces between the routing, decode and prefill translation units.
+#pragma once
+
+#include "vy_common.cuh"
+
+namespace vy {
+
+constexpr int kMaxTopK = 32;
+constexpr int kMaxExperts = 1024;
+
+// Arguments of the routing plan kernel (block 0) and the activation permutation (blocks >= 1).
+struct PlanArgs {
+    const void* ids;
+    bool ids64;
+    int64_t n_tokens;
+    int top_k;
+    int n_experts;
+    int32_t* order;        // [n]       row ids grouped by expert (stable)
+    int32_t* live_expert;  // [E]       routed expert ids ascending
+    int32_t* live_start;   // [E+1]     start of each live expert's run in `order`
+    int32_t* unit_start;   // [E+1]     optional: prefix of ceil(count / tok_per_unit)
+    int32_t* slot_order;   // [n]       token t's row ids, ascending expert id then slot
+    int32_t* counters;     // [4]       n_live, dropped rows, kernel error flags, spare
+    int tok_per_unit;
+    // activation permutation (x -> x_perm, 8-element groups), skipped when x_perm is null
+    const void* x;
+    int64_t x_stride;
+    bool x_vec;
+    int64_t hidden;
+    uint16_t* x_perm;
+};
+
+size_t plan_smem_bytes(int n_experts);
+int plan_validate(int64_t n_tokens, int top_k, int n_experts);
+int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream);
+int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
+                   int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
+                   cudaStream_t stream);
+
+// Shared validation of a vy_moe_call (decode and prefill entry points).
+int validate_call(const vy_moe_call* c);
+size_t prefill_workspace_bytes(const vy_moe_call* c);
+
+// Workspace carve-up shared by the decode and prefill entry points.
+struct Carve {
+    char* base;
+    size_t used;
+    template <typename T>
+    T* take(size_t count) {
+        size_t off = (used + 255) & ~size_t(255);
+        used = off + count * sizeof(T);
+        return base ? reinterpret_cast<T*>(base + off) : nullptr;
+    }
+};
+
+}  // namespace vy

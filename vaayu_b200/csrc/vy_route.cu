@@ -1,0 +1,386 @@
+// vy_route.cu -- routing on the device: softmax top-k, the routed gather/permute plan (a
+// stable counting sort of (token, slot) rows by expert id), the activation permutation the
+// GEMV kernels read, and the ordered weighted combine.
+#include <climits>
+
+#include "vy_moe.cuh"
+
+namespace vy {
+namespace {
+
+constexpr int kPlanThreads = 1024;
+constexpr int kPlanWarps = kPlanThreads / 32;
+constexpr int kPermThreads = 256;
+
+__device__ __forceinline__ int load_id(const void* ids, bool ids64, int64_t j) {
+    if (ids64) {
+        int64_t v = reinterpret_cast<const int64_t*>(ids)[j];
+        return (v < INT32_MIN || v > INT32_MAX) ? -1 : static_cast<int>(v);
+    }
+    return reinterpret_cast<const int32_t*>(ids)[j];
+}
+
+// Exclusive scan of one int per thread over the block; returns this thread's prefix and puts
+// the total in *total.  `scratch` holds kPlanWarps + 1 ints.
+__device__ int block_exclusive_scan(int v, int* scratch, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    if (lane == 31) scratch[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < kPlanWarps ? scratch[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += y;
+        }
+        if (lane < kPlanWarps) scratch[lane] = w;   // inclusive prefix of warp sums
+        if (lane == kPlanWarps - 1) scratch[kPlanWarps] = w;
+    }
+    __syncthreads();
+    int base = warp > 0 ? scratch[warp - 1] : 0;
+    *total = scratch[kPlanWarps];
+    int excl = base + x - v;
+    __syncthreads();
+    return excl;
+}
+
+// Block 0: the plan.  Blocks >= 1: the activation permutation (x -> x_perm).
+__global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
+    if (blockIdx.x > 0) {
+        // each thread permutes one 8-element group of one token's activations
+        const int64_t groups_per_tok = p.hidden / 8;
+        const int64_t total = p.n_tokens * groups_per_tok;
+        for (int64_t q = (blockIdx.x - 1) * int64_t(blockDim.x) + threadIdx.x; q < total;
+             q += int64_t(gridDim.x - 1) * blockDim.x) {
+            const int64_t t = q / groups_per_tok, c = (q % groups_per_tok) * 8;
+            const uint16_t* src = reinterpret_cast<const uint16_t*>(p.x) + t * p.x_stride + c;
+            uint16_t v[8];
+            if (p.x_vec) {
+                *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(src);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = src[j];
+            }
+            uint4 o;
+            o.x = v[0] | (uint32_t(v[4]) << 16);
+            o.y = v[1] | (uint32_t(v[5]) << 16);
+            o.z = v[2] | (uint32_t(v[6]) << 16);
+            o.w = v[3] | (uint32_t(v[7]) << 16);
+            *reinterpret_cast<uint4*>(p.x_perm + t * p.hidden + c) = o;
+        }
+        return;
+    }
+    extern __shared__ int cnt[];                            // [kPlanWarps][n_experts]
+    __shared__ int scan_scratch[kPlanWarps + 1];
+    __shared__ int dropped;
+    const int E = p.n_experts, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t n = p.n_tokens * p.top_k;
+    const int64_t seg = (n + kPlanWarps - 1) / kPlanWarps;
+    const int64_t lo = warp * seg, hi = min(n, lo + seg);
+    int* my = cnt + warp * E;
+    if (threadIdx.x == 0) dropped = 0;
+    for (int e = lane; e < E; e += 32) my[e] = 0;
+    __syncthreads();
+    // 1. per-warp histogram of its contiguous segment of rows
+    for (int64_t base = lo; base < hi; base += 32) {
+        const int64_t row = base + lane;
+        int e = -1;
+        if (row < hi) {
+            e = load_id(p.ids, p.ids64, row);
+            if (e < 0 || e >= E) {
+                atomicAdd(&dropped, 1);
+                e = -1;
+            }
+        }
+        const unsigned mask = __match_any_sync(0xffffffffu, e);
+        if (e >= 0 && lane == __ffs(mask) - 1) my[e] += __popc(mask);
+        __syncwarp();
+    }
+    __syncthreads();
+    // 2. totals, expert starts, the live list, unit prefix; per-warp counts become each
+    //    warp's first position inside the expert's run (warp order = row order: stable)
+    const int e = threadIdx.x;
+    int tot = 0;
+    if (e < E)
+        for (int w = 0; w < kPlanWarps; ++w) tot += cnt[w * E + e];
+    int n_rows, n_live, n_units;
+    const int start = block_exclusive_scan(tot, scan_scratch, &n_rows);
+    const int live_idx = block_exclusive_scan(tot > 0 ? 1 : 0, scan_scratch, &n_live);
+    const int units = (tot > 0 && p.tok_per_unit > 0) ? (tot + p.tok_per_unit - 1) / p.tok_per_unit : 0;
+    const int ustart = block_exclusive_scan(units, scan_scratch, &n_units);
+    if (e < E) {
+        if (tot > 0) {
+            p.live_expert[live_idx] = e;
+            p.live_start[live_idx] = start;
+            if (p.unit_start) p.unit_start[live_idx] = ustart;
+        }
+        int running = start;
+        for (int w = 0; w < kPlanWarps; ++w) {
+            const int c = cnt[w * E + e];
+            cnt[w * E + e] = running;
+            running += c;
+        }
+    }
+    if (threadIdx.x == 0) {
+        p.live_start[n_live] = n_rows;
+        if (p.unit_start) p.unit_start[n_live] = n_units;
+        p.counters[0] = n_live;
+        p.counters[1] = dropped;
+        p.counters[2] = 0;
+        p.counters[3] = 0;
+    }
+    __syncthreads();
+    // 3. stable scatter: position = warp's next slot for the id + rank among equal ids
+    for (int64_t base = lo; base < hi; base += 32) {
+        const int64_t row = base + lane;
+        int ex = -1;
+        if (row < hi) {
+            ex = load_id(p.ids, p.ids64, row);
+            if (ex < 0 || ex >= E) ex = -1;
+        }
+        const unsigned mask = __match_any_sync(0xffffffffu, ex);
+        int pos = 0;
+        if (ex >= 0) pos = my[ex] + __popc(mask & ((1u << lane) - 1u));
+        __syncwarp();
+        if (ex >= 0) {
+            p.order[pos] = static_cast<int32_t>(row);
+            if (lane == __ffs(mask) - 1) my[ex] += __popc(mask);
+        }
+        __syncwarp();
+    }
+    // 4. each token's slots in ascending expert id (stable by slot); dropped slots last as -1
+    const int K = p.top_k;
+    for (int64_t t = threadIdx.x; t < p.n_tokens; t += blockDim.x) {
+        int key[kMaxTopK], idx[kMaxTopK];
+        for (int k = 0; k < K; ++k) {
+            int ex = load_id(p.ids, p.ids64, t * K + k);
+            key[k] = (ex < 0 || ex >= E) ? INT32_MAX : ex;
+            idx[k] = k;
+        }
+        for (int a = 1; a < K; ++a) {
+            int kv = key[a], iv = idx[a], b = a - 1;
+            while (b >= 0 && key[b] > kv) {
+                key[b + 1] = key[b];
+                idx[b + 1] = idx[b];
+                --b;
+            }
+            key[b + 1] = kv;
+            idx[b + 1] = iv;
+        }
+        for (int k = 0; k < K; ++k)
+            p.slot_order[t * K + k] = key[k] == INT32_MAX ? -1 : static_cast<int32_t>(t * K + idx[k]);
+    }
+}
+
+// softmax -> top-k -> renormalise; one warp per token.
+template <int LD>
+__global__ void topk_softmax_kernel(const void* logits, int64_t row_stride, int64_t n_tokens,
+                                    int n_experts, int top_k, float* weights, int64_t* ids) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t = blockIdx.x * int64_t(blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t >= n_tokens) return;
+    auto val = [&](int e) -> float {
+        if constexpr (LD == VY_F32) return reinterpret_cast<const float*>(logits)[t * row_stride + e];
+        else if constexpr (LD == VY_BF16)
+            return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(logits)[t * row_stride + e]);
+        else return __half2float(reinterpret_cast<const __half*>(logits)[t * row_stride + e]);
+    };
+    float mx = -INFINITY;
+    for (int e = lane; e < n_experts; e += 32) mx = fmaxf(mx, val(e));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int e = lane; e < n_experts; e += 32) sum += expf(val(e) - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    // top-k by repeated arg-max over the probabilities (largest first, ties to the lower id)
+    float chosen_p[kMaxTopK];
+    int chosen_e[kMaxTopK];
+    float ksum = 0.f;
+    for (int k = 0; k < top_k; ++k) {
+        float best = -1.f;
+        int be = INT32_MAX;
+        for (int e = lane; e < n_experts; e += 32) {
+            bool taken = false;
+            for (int q = 0; q < k; ++q) taken |= (chosen_e[q] == e);
+            if (taken) continue;
+            float pv = expf(val(e) - mx) / sum;
+            if (pv > best || (pv == best && e < be)) {
+                best = pv;
+                be = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            int oe = __shfl_xor_sync(0xffffffffu, be, o);
+            if (ob > best || (ob == best && oe < be)) {
+                best = ob;
+                be = oe;
+            }
+        }
+        chosen_p[k] = best;
+        chosen_e[k] = be;
+    }
+    for (int k = 0; k < top_k; ++k) ksum += chosen_p[k];
+    if (lane == 0) {
+        for (int k = 0; k < top_k; ++k) {
+            weights[t * top_k + k] = chosen_p[k] / ksum;
+            ids[t * top_k + k] = chosen_e[k];
+        }
+    }
+}
+
+// out[t] = sum of contrib rows of token t in slot_order (ascending expert id, then slot).
+__global__ void combine_kernel(const float* __restrict__ contrib, const void* ids, bool ids64,
+                               int64_t n_tokens, int top_k, int64_t hidden, float* out,
+                               int64_t out_stride) {
+    const int64_t t = blockIdx.y;
+    int idx[kMaxTopK];
+    int key[kMaxTopK];
+    for (int k = 0; k < top_k; ++k) {
+        int e = load_id(ids, ids64, t * top_k + k);
+        key[k] = e < 0 ? INT32_MAX : e;
+        idx[k] = k;
+    }
+    for (int a = 1; a < top_k; ++a) {
+        int kv = key[a], iv = idx[a], b = a - 1;
+        while (b >= 0 && key[b] > kv) {
+            key[b + 1] = key[b];
+            idx[b + 1] = idx[b];
+            --b;
+        }
+        key[b + 1] = kv;
+        idx[b + 1] = iv;
+    }
+    for (int64_t c = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; c < hidden;
+         c += int64_t(gridDim.x) * blockDim.x) {
+        float acc = 0.f;
+        for (int k = 0; k < top_k; ++k)
+            if (key[k] != INT32_MAX) acc += contrib[(t * top_k + idx[k]) * hidden + c];
+        out[t * out_stride + c] = acc;
+    }
+}
+
+}  // namespace
+
+size_t plan_smem_bytes(int n_experts) {
+    return sizeof(int) * size_t(kPlanWarps) * size_t(n_experts);
+}
+
+int plan_validate(int64_t n_tokens, int top_k, int n_experts) {
+    if (n_tokens < 0 || top_k <= 0) return fail(VY_ERR_INVALID, "n_tokens %lld top_k %d", (long long)n_tokens, top_k);
+    if (top_k > kMaxTopK) return fail(VY_ERR_UNSUPPORTED, "top_k %d > %d", top_k, kMaxTopK);
+    if (n_experts <= 0 || n_experts > kMaxExperts)
+        return fail(VY_ERR_UNSUPPORTED, "n_experts %d (1..%d supported)", n_experts, kMaxExperts);
+    if (n_tokens * top_k > int64_t(kPlanWarps) * 65535)
+        return fail(VY_ERR_UNSUPPORTED, "%lld routed rows in one call (max %d)",
+                    (long long)(n_tokens * top_k), kPlanWarps * 65535);
+    return VY_OK;
+}
+
+int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream) {
+    size_t smem = plan_smem_bytes(p.n_experts);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(plan_smem_bytes(kMaxExperts)));
+        configured = true;
+    }
+    int perm_blocks = 0;
+    if (p.x_perm) {
+        int64_t groups = p.n_tokens * (p.hidden / 8);
+        int64_t b = (groups + kPlanThreads - 1) / kPlanThreads;
+        perm_blocks = static_cast<int>(b < 4 * sm_count ? b : 4 * sm_count);
+    }
+    plan_kernel<<<1 + perm_blocks, kPlanThreads, smem, stream>>>(p);
+    return check_launch("routing plan");
+}
+
+int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
+                   int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
+                   cudaStream_t stream) {
+    if (n_tokens == 0) return VY_OK;
+    int bx = static_cast<int>((hidden + 255) / 256);
+    if (bx > 8) bx = 8;
+    (void)sm_count;
+    dim3 grid(bx, static_cast<unsigned>(n_tokens));
+    combine_kernel<<<grid, 256, 0, stream>>>(contrib, ids, ids64, n_tokens, top_k, hidden, out, out_stride);
+    return check_launch("combine");
+}
+
+}  // namespace vy
+
+using namespace vy;
+
+extern "C" int vy_moe_route_permute(const void* ids, int32_t ids_dtype, int64_t n_tokens,
+                                    int32_t top_k, int32_t n_experts, int32_t* order,
+                                    int32_t* live_expert, int32_t* live_start,
+                                    int32_t* slot_order, int32_t* counters, void* stream) {
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if ((st = plan_validate(n_tokens, top_k, n_experts)) != VY_OK) return st;
+    if (ids_dtype != VY_I32 && ids_dtype != VY_I64) return fail(VY_ERR_UNSUPPORTED, "id dtype %d", ids_dtype);
+    if (!order || !live_expert || !live_start || !slot_order || !counters)
+        return fail(VY_ERR_INVALID, "null output");
+    if (n_tokens > 0 && !ids) return fail(VY_ERR_INVALID, "null ids");
+    PlanArgs p{};
+    p.ids = ids;
+    p.ids64 = ids_dtype == VY_I64;
+    p.n_tokens = n_tokens;
+    p.top_k = top_k;
+    p.n_experts = n_experts;
+    p.order = order;
+    p.live_expert = live_expert;
+    p.live_start = live_start;
+    p.slot_order = slot_order;
+    p.counters = counters;
+    p.unit_start = nullptr;
+    p.tok_per_unit = 0;
+    return launch_plan(p, dev->sm_count, as_stream(stream));
+}
+
+extern "C" int vy_moe_topk_softmax(const void* logits, int32_t logit_dtype, int64_t row_stride,
+                                   int64_t n_tokens, int32_t n_experts, int32_t top_k,
+                                   float* weights, int64_t* ids, void* stream) {
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if (n_tokens < 0 || n_experts <= 0 || top_k <= 0 || top_k > n_experts)
+        return fail(VY_ERR_INVALID, "n_tokens %lld n_experts %d top_k %d", (long long)n_tokens, n_experts, top_k);
+    if (top_k > kMaxTopK) return fail(VY_ERR_UNSUPPORTED, "top_k %d > %d", top_k, kMaxTopK);
+    if (n_tokens == 0) return ok();
+    if (!logits || !weights || !ids) return fail(VY_ERR_INVALID, "null pointer");
+    const int warps = 8;
+    const unsigned grid = static_cast<unsigned>((n_tokens + warps - 1) / warps);
+    cudaStream_t s = as_stream(stream);
+    switch (logit_dtype) {
+        case VY_F32: topk_softmax_kernel<VY_F32><<<grid, warps * 32, 0, s>>>(logits, row_stride, n_tokens, n_experts, top_k, weights, ids); break;
+        case VY_BF16: topk_softmax_kernel<VY_BF16><<<grid, warps * 32, 0, s>>>(logits, row_stride, n_tokens, n_experts, top_k, weights, ids); break;
+        case VY_F16: topk_softmax_kernel<VY_F16><<<grid, warps * 32, 0, s>>>(logits, row_stride, n_tokens, n_experts, top_k, weights, ids); break;
+        default: return fail(VY_ERR_UNSUPPORTED, "logit dtype %d", logit_dtype);
+    }
+    return check_launch("vy_moe_topk_softmax");
+}
+
+extern "C" int vy_moe_combine(const float* contrib, const void* expert_ids, int32_t ids_dtype,
+                              int64_t n_tokens, int32_t top_k, int64_t hidden, float* out,
+                              int64_t out_row_stride, void* stream) {
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if (n_tokens < 0 || top_k <= 0 || hidden < 0) return fail(VY_ERR_INVALID, "bad sizes");
+    if (top_k > kMaxTopK) return fail(VY_ERR_UNSUPPORTED, "top_k %d > %d", top_k, kMaxTopK);
+    if (ids_dtype != VY_I32 && ids_dtype != VY_I64) return fail(VY_ERR_UNSUPPORTED, "id dtype %d", ids_dtype);
+    if (n_tokens == 0 || hidden == 0) return ok();
+    if (!contrib || !expert_ids || !out) return fail(VY_ERR_INVALID, "null pointer");
+    return launch_combine(contrib, expert_ids, ids_dtype == VY_I64, n_tokens, top_k, hidden, out,
+                          out_row_stride, dev->sm_count, as_stream(stream));
+}
