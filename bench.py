@@ -214,6 +214,11 @@ def run_ours(args, rank, world, local):
     main_step = step_for(T)
     for i in range(args.warmup):
         main_step(i)
+    if args.profile:
+        # a short fixed loop of the main step for profilers: no sweep, e2e or CPU baseline
+        ms = time_steps(main_step, args.steps, device)
+        print(json.dumps({"profile": True, "ms_per_step": ms, "tokens": T, "layers": L}))
+        return
     barrier(world)
     with ClockSampler(local) as clocks:
         ms = time_steps(main_step, args.steps, device)
@@ -223,6 +228,9 @@ def run_ours(args, rank, world, local):
 
     # per-stage timing (serialised stages): the gate/up kernel's own duration for the roofline
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    for e in evs:
+        e.record()                      # torch creates the CUDA event on its first record
+    torch.cuda.synchronize(device)
     import ctypes
     handles = (ctypes.c_void_p * 4)(*[e.cuda_event for e in evs])
     stage = {"plan": [], "gate_up": [], "down": []}
@@ -395,6 +403,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--profile", action="store_true",
+                    help="only the timed loop of the main step (for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_setup()

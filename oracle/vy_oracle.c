@@ -231,11 +231,12 @@ static inline const void* scale_at(const void* base, int code, int64_t off) {
  *   table    [n_experts][3] addresses: packed int32 stream, scale stream, zero stream (or 0)
  *   h_out    optional [T*K, inter] act dtype: each row's SiLU(gate)*up
  *   y_out    optional [T*K, hidden] fp32: each row's weighted contribution
+ *   h_in     optional [T*K, inter] act dtype: use this h instead of computing it
  */
 int vyo_moe_layer(const vyo_geom* g, const void* x, int64_t x_stride, int32_t T,
                   const int64_t* eidx, int32_t K, const void* rw, const int32_t* w_index,
                   const int64_t* table, int32_t n_experts, float* out, int64_t out_stride,
-                  void* h_out, float* y_out, int32_t n_threads) {
+                  void* h_out, float* y_out, const void* h_in, int32_t n_threads) {
     const int64_t H = g->hidden, I = g->inter, n = (int64_t)T * K;
     const int act = g->act_code, bits = g->bits, gs = g->group_size;
     if (T < 0 || K <= 0 || H <= 0 || I <= 0 || bits <= 0 || 32 % bits || gs <= 0) return -1;
@@ -274,9 +275,12 @@ int vyo_moe_layer(const vyo_geom* g, const void* x, int64_t x_stride, int32_t T,
         for (int64_t k = 0; k < H; ++k)
             xf[t * H + k] = load_val((const char*)x, act, t * x_stride + k);
 
-    /* Phase 1: h = act(act(silu(act(x.Wg))) * act(x.Wu)) for every routed row. */
-#pragma omp parallel
-    {
+    /* Phase 1: h = act(act(silu(act(x.Wg))) * act(x.Wu)) for every routed row -- or, to check
+     * the down stage alone, the caller's h (h_in, act dtype [T*K, I]). */
+    if (h_in)
+        for (int64_t j = 0; j < n * I; ++j) hbuf[j] = load_val(h_in, act, j);
+#pragma omp parallel if (!h_in)
+    if (!h_in) {
         float* wg = (float*)malloc(sizeof(float) * (size_t)H);
         float* wu = (float*)malloc(sizeof(float) * (size_t)H);
 #pragma omp for schedule(dynamic, 4)

@@ -88,7 +88,8 @@ def oracle_expert(blob: dict) -> dict:
             "zero": None if "zero" not in f else to_np(f["zero"]).astype(np.int32)}
 
 
-def oracle_layer(blobs, x, eidx, rw, w_index=None, want_h=False, want_y=False, threads=0):
+def oracle_layer(blobs, x, eidx, rw, w_index=None, want_h=False, want_y=False, threads=0,
+                 h_in=None):
     """Oracle of one layer call: blobs indexed by expert id; eidx [T, K]; rw [T, K] (or flat
     with w_index)."""
     from oracle import oracle as O
@@ -98,7 +99,7 @@ def oracle_layer(blobs, x, eidx, rw, w_index=None, want_h=False, want_y=False, t
                       to_np(rw.reshape(-1)) if w_index is None else to_np(rw.reshape(-1)),
                       CODE[rw.dtype], sc,
                       w_index=None if w_index is None else np.asarray(w_index, np.int32),
-                      want_h=want_h, want_y=want_y, threads=threads)
+                      want_h=want_h, want_y=want_y, threads=threads, h_in=h_in)
     return res
 
 

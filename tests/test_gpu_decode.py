@@ -73,8 +73,10 @@ def test_each_rounding_point_matches_the_oracle(hid, inter, gs, k):
     table = pk.ExpertTable(blobs)
     vb.moe_forward(x, torch.arange(k, device="cuda").view(1, k), ones, table, contrib=contrib)
     torch.cuda.synchronize()
-    _o, h_ref, y_ref = _oracle(x, blobs, list(range(k)), ones, want_h=True, want_y=True)
+    _o, h_ref = _oracle(x, blobs, list(range(k)), ones, want_h=True)
     assert (T.to_np(h) == h_ref).mean() >= 0.99, "gate/up/SiLU/product stage"
+    # the down stage alone: the oracle is fed the kernel's own h
+    _o, y_ref = _oracle(x, blobs, list(range(k)), ones, want_y=True, h_in=T.to_np(h))
     assert (contrib.cpu().numpy() == y_ref).mean() >= 0.99, "down stage"
 
 

@@ -217,6 +217,14 @@ __global__ void __launch_bounds__(kWarps * 32) gate_up_kernel(GateUpParams p) {
             const int kx = ks * kStageK + tig * 32;
             const uint32_t wgw0[4] = {wg0.x, wg0.y, wg0.z, wg0.w}, wgw8[4] = {wg8.x, wg8.y, wg8.z, wg8.w};
             const uint32_t wuw0[4] = {wu0.x, wu0.y, wu0.z, wu0.w}, wuw8[4] = {wu8.x, wu8.y, wu8.z, wu8.w};
+            // The stage's 128-term partial dots start from zero and join the running sums with
+            // round-to-nearest fp32 adds: the tensor core's own accumulate truncates against the
+            // accumulator's magnitude, so a long chain inside it drifts (biased) from the fp32 sum.
+            float sg[NB][4], su[NB][4];
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sg[cb][i] = su[cb][i] = 0.f;
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
                 uint32_t ag0[4], ag8[4], au0[4], au8[4];
@@ -231,12 +239,19 @@ __global__ void __launch_bounds__(kWarps * 32) gate_up_kernel(GateUpParams p) {
                 for (int cb = 0; cb < NB; ++cb) {
                     uint4 xv = make_uint4(0u, 0u, 0u, 0u);
                     if (xoff[cb] >= 0) xv = ld_nc_v4(p.x_perm + xoff[cb] + kx + wi * 8);
-                    mma_16816<ACT>(acc_g[cb], ag0[0], ag8[0], ag0[1], ag8[1], xv.x, xv.y);
-                    mma_16816<ACT>(acc_g[cb], ag0[2], ag8[2], ag0[3], ag8[3], xv.z, xv.w);
-                    mma_16816<ACT>(acc_u[cb], au0[0], au8[0], au0[1], au8[1], xv.x, xv.y);
-                    mma_16816<ACT>(acc_u[cb], au0[2], au8[2], au0[3], au8[3], xv.z, xv.w);
+                    mma_16816<ACT>(sg[cb], ag0[0], ag8[0], ag0[1], ag8[1], xv.x, xv.y);
+                    mma_16816<ACT>(sg[cb], ag0[2], ag8[2], ag0[3], ag8[3], xv.z, xv.w);
+                    mma_16816<ACT>(su[cb], au0[0], au8[0], au0[1], au8[1], xv.x, xv.y);
+                    mma_16816<ACT>(su[cb], au0[2], au8[2], au0[3], au8[3], xv.z, xv.w);
                 }
             }
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc_g[cb][i] = __fadd_rn(acc_g[cb][i], sg[cb][i]);
+                    acc_u[cb][i] = __fadd_rn(acc_u[cb][i], su[cb][i]);
+                }
         }
         if (ks == spu - 1) {
             if (cunit.ok) {
@@ -377,6 +392,11 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
             load_scale_bias<ACT, SC, ZERO>(csc, czp, p.s_off, p.z_off, row + 8, groups, grp, s8, b8);
             const int kh = cc.ks * kStageK + tig * 32;
             const uint32_t ww0[4] = {w0.x, w0.y, w0.z, w0.w}, ww8[4] = {w8.x, w8.y, w8.z, w8.w};
+            float sp[NB][4];   // the stage's partial dots (see gate_up_kernel)
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sp[cb][i] = 0.f;
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
                 uint32_t a0[4], a8[4];
@@ -389,10 +409,14 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
                 for (int cb = 0; cb < NB; ++cb) {
                     uint4 hv = make_uint4(0u, 0u, 0u, 0u);
                     if (hoff[cb] >= 0) hv = ld_nc_v4(p.h_perm + hoff[cb] + kh + wi * 8);
-                    mma_16816<ACT>(acc[cb], a0[0], a8[0], a0[1], a8[1], hv.x, hv.y);
-                    mma_16816<ACT>(acc[cb], a0[2], a8[2], a0[3], a8[3], hv.z, hv.w);
+                    mma_16816<ACT>(sp[cb], a0[0], a8[0], a0[1], a8[1], hv.x, hv.y);
+                    mma_16816<ACT>(sp[cb], a0[2], a8[2], a0[3], a8[3], hv.z, hv.w);
                 }
             }
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[cb][i] = __fadd_rn(acc[cb][i], sp[cb][i]);
         }
         if (cc.ks == spu - 1) {
             if (cok) {
@@ -635,7 +659,8 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     pa.x_perm = L.x_perm;
     cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
     const bool timed = ev != nullptr && c->n_stage_events >= 4;
-    if (timed) cudaEventRecord(ev[0], s);
+    if (timed && cudaEventRecord(ev[0], s) != cudaSuccess)
+        return fail(VY_ERR_INVALID, "stage_events[0] is not a usable cudaEvent_t");
     if ((st = launch_plan(pa, dev->sm_count, s)) != VY_OK) return st;
     if (timed) cudaEventRecord(ev[1], s);
 
