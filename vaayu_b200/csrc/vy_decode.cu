@@ -27,10 +27,16 @@
 namespace vy {
 namespace {
 
+#ifndef VY_GU_DEPTH
+#define VY_GU_DEPTH 6
+#endif
+#ifndef VY_DN_DEPTH
+#define VY_DN_DEPTH 8
+#endif
 constexpr int kWarps = 8;
-constexpr int kStageK = 128;    // K elements of one row per pipeline stage (64 bytes of codes)
-constexpr int kGuDepth = 6;     // gate/up ring: stages in flight per warp (2 KB each)
-constexpr int kDnDepth = 8;     // down ring: stages in flight per warp (1 KB each)
+constexpr int kStageK = 128;             // K elements of one row per pipeline stage (64 bytes of codes)
+constexpr int kGuDepth = VY_GU_DEPTH;    // gate/up ring: stages in flight per warp (2 KB each)
+constexpr int kDnDepth = VY_DN_DEPTH;    // down ring: stages in flight per warp (1 KB each)
 constexpr int kTileRows = 16;
 
 struct GateUpParams {
@@ -65,7 +71,10 @@ struct DownParams {
     const int32_t* w_index;
     float* out;
     int64_t out_stride;
-    float* ybuf_g;      // non-null: contributions to global [n][hidden], no in-CTA combine
+    float* ybuf_g;      // non-null: contributions to global [n][hidden] instead of shared memory
+    bool global_combine;  // with ybuf_g: the last CTA of each row tile sums it into `out`
+    int n_chunks;       // CTAs sharing one row tile (its live experts interleaved over them)
+    int32_t* tile_done; // [hidden / 16] tickets, zeroed by the plan kernel of the same call
 };
 
 // Everything a warp needs about the unit (expert, 16-row tile, token pass) it works on.
@@ -132,7 +141,7 @@ __device__ __forceinline__ void dequant4(const uint4& w, uint32_t bias, uint32_t
 }
 
 template <int ACT, int SC, bool ZERO, int NB>
-__global__ void __launch_bounds__(kWarps * 32) gate_up_kernel(GateUpParams p) {
+__global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(GateUpParams p) {
     extern __shared__ uint4 ring[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
@@ -237,6 +246,7 @@ __global__ void __launch_bounds__(kWarps * 32) gate_up_kernel(GateUpParams p) {
                 }
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
+                    if (cb * 8 >= cunit.ncols) break;     // warp-uniform: no tokens left
                     uint4 xv = make_uint4(0u, 0u, 0u, 0u);
                     if (xoff[cb] >= 0) xv = ld_nc_v4(p.x_perm + xoff[cb] + kx + wi * 8);
                     mma_16816<ACT>(sg[cb], ag0[0], ag8[0], ag0[1], ag8[1], xv.x, xv.y);
@@ -246,12 +256,14 @@ __global__ void __launch_bounds__(kWarps * 32) gate_up_kernel(GateUpParams p) {
                 }
             }
 #pragma unroll
-            for (int cb = 0; cb < NB; ++cb)
+            for (int cb = 0; cb < NB; ++cb) {
+                if (cb * 8 >= cunit.ncols) break;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     acc_g[cb][i] = __fadd_rn(acc_g[cb][i], sg[cb][i]);
                     acc_u[cb][i] = __fadd_rn(acc_u[cb][i], su[cb][i]);
                 }
+            }
         }
         if (ks == spu - 1) {
             if (cunit.ok) {
@@ -283,13 +295,15 @@ __global__ void __launch_bounds__(kWarps * 32) gate_up_kernel(GateUpParams p) {
 }
 
 template <int ACT, int SC, bool ZERO, int NB>
-__global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
+__global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) down_kernel(DownParams p) {
     extern __shared__ uint4 ring[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
     uint4* my_ring = ring + warp * (kDnDepth * 2 * 32);
     float* ybuf = reinterpret_cast<float*>(ring + kWarps * kDnDepth * 2 * 32);
-    const int tile = blockIdx.x;
+    const int n_tiles = p.hidden / kTileRows;
+    const int tile = blockIdx.x % n_tiles, chunk = blockIdx.x / n_tiles;
+    const int wstride = kWarps * p.n_chunks;     // live experts: li = chunk*kWarps + warp + q*wstride
 
     grid_dependency_wait();
 
@@ -314,12 +328,13 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
             c.ks = 0;
             if (++c.pass == c.npass) {
                 c.pass = 0;
-                c.li += kWarps;
+                c.li += wstride;
                 c.npass = npass_of(c.li);
             }
         }
     };
-    Cursor ic{warp, 0, npass_of(warp), 0};
+    const int li0 = chunk * kWarps + warp;
+    Cursor ic{li0, 0, npass_of(li0), 0};
     int ic_li = -1;
     const int32_t* ipk = nullptr;
     bool iok = false;
@@ -347,7 +362,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
 #pragma unroll
     for (int s = 0; s < kDnDepth - 1; ++s) issue();
 
-    Cursor cc{warp, 0, npass_of(warp), 0};
+    Cursor cc{li0, 0, npass_of(li0), 0};
     int cc_li = -1;
     const void* csc = nullptr;
     const int32_t* czp = nullptr;
@@ -407,6 +422,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
                 }
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
+                    if (cb * 8 >= ncols) break;            // warp-uniform: no tokens left
                     uint4 hv = make_uint4(0u, 0u, 0u, 0u);
                     if (hoff[cb] >= 0) hv = ld_nc_v4(p.h_perm + hoff[cb] + kh + wi * 8);
                     mma_16816<ACT>(sp[cb], a0[0], a8[0], a0[1], a8[1], hv.x, hv.y);
@@ -414,9 +430,11 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
                 }
             }
 #pragma unroll
-            for (int cb = 0; cb < NB; ++cb)
+            for (int cb = 0; cb < NB; ++cb) {
+                if (cb * 8 >= ncols) break;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[cb][i] = __fadd_rn(acc[cb][i], sp[cb][i]);
+            }
         }
         if (cc.ks == spu - 1) {
             if (cok) {
@@ -449,8 +467,21 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
         advance(cc);
     }
     cp_async_wait<0>();
-    if (p.ybuf_g) return;
-    __syncthreads();
+    if (p.ybuf_g && !p.global_combine) return;   // per-row contributions only (expert parallel)
+    __shared__ int s_last;
+    if (p.ybuf_g) {
+        // the last CTA of this row tile to finish sums it: publish, then take a ticket
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            __threadfence();
+            s_last = atomicAdd(p.tile_done + tile, 1) == p.n_chunks - 1;
+        }
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+    } else {
+        __syncthreads();
+    }
     // each token's 16 columns: contributions in ascending expert id, then slot
     const int K = p.top_k;
     for (int64_t idx = threadIdx.x; idx < p.n_tokens * kTileRows; idx += blockDim.x) {
@@ -459,7 +490,9 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(DownParams p) {
         float a = 0.f;
         for (int k = 0; k < K; ++k) {
             const int rowid = p.slot_order[t * K + k];
-            if (rowid >= 0) a += ybuf[rowid * kTileRows + r];
+            if (rowid < 0) continue;
+            a += p.ybuf_g ? __ldcg(p.ybuf_g + int64_t(rowid) * p.hidden + tile * kTileRows + r)
+                          : ybuf[rowid * kTileRows + r];
         }
         p.out[t * p.out_stride + tile * kTileRows + r] = a;
     }
@@ -508,7 +541,7 @@ int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, size_
     cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_grid, gu_smem(), s, gu);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
     if (timed) cudaEventRecord(ev[2], s);
-    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn.hidden / kTileRows, dn_smem, s, dn);
+    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, (dn.hidden / kTileRows) * dn.n_chunks, dn_smem, s, dn);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "down launch: %s", cudaGetErrorString(e));
     return check_launch("vy_moe_decode");
 }
@@ -539,16 +572,31 @@ int dispatch_sc(int sc, bool zero, int nb, const GateUpParams& gu, const DownPar
 }
 
 struct DecodeLayout {
-    int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters;
+    int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters, *tile_done;
     uint16_t *x_perm, *h_perm;
     float* ybuf_g;
     size_t bytes;
     bool combine_in_cta;
+    int n_chunks;
 };
 
-int nb_for(int64_t n_tokens) { return n_tokens <= 8 ? 1 : (n_tokens <= 16 ? 2 : 4); }
+// Column blocks (8 tokens each) one pass of a unit holds: the largest token count an expert
+// can have is n_tokens; empty blocks are skipped at run time, so NB only costs registers.
+int nb_for(int64_t n_tokens) { return n_tokens <= 16 ? 1 : (n_tokens <= 64 ? 2 : 4); }
 
-DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
+// CTAs per down-projection row tile: enough for ~2 resident CTAs per SM, but no more chunks
+// than the call can have live experts per warp.
+int down_chunks(const vy_moe_call* c, int sm_count) {
+    const int64_t n = c->n_tokens * c->top_k;
+    const int n_tiles = c->geom->hidden / kTileRows;
+    const int64_t max_live = n < c->n_experts ? n : c->n_experts;
+    int chunks = (2 * sm_count + n_tiles - 1) / n_tiles;
+    const int cap = static_cast<int>((max_live + kWarps - 1) / kWarps);
+    if (chunks > cap) chunks = cap;
+    return chunks < 1 ? 1 : chunks;
+}
+
+DecodeLayout decode_layout(const vy_moe_call* c, void* base, int sm_count) {
     const int64_t n = c->n_tokens * c->top_k;
     const int E = c->n_experts;
     const int64_t H = c->geom->hidden, I = c->geom->inter;
@@ -560,10 +608,13 @@ DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
     L.unit_start = cv.take<int32_t>(E + 1);
     L.slot_order = cv.take<int32_t>(n);
     L.counters = cv.take<int32_t>(4);
+    L.tile_done = cv.take<int32_t>(H / kTileRows);
     L.x_perm = cv.take<uint16_t>(c->n_tokens * H);
     L.h_perm = cv.take<uint16_t>(n * I);
+    L.n_chunks = down_chunks(c, sm_count);
     const size_t ybuf_bytes = size_t(n) * kTileRows * sizeof(float);
-    L.combine_in_cta = (c->contrib == nullptr) && (dn_ring_smem() + ybuf_bytes <= kDnSmemCap);
+    L.combine_in_cta = (c->contrib == nullptr) && L.n_chunks == 1 &&
+                       (dn_ring_smem() + ybuf_bytes <= kDnSmemCap);
     L.ybuf_g = nullptr;
     if (c->contrib == nullptr && !L.combine_in_cta) L.ybuf_g = cv.take<float>(n * H);
     L.bytes = cv.used;
@@ -621,7 +672,8 @@ using namespace vy;
 extern "C" size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path) {
     if (!call || !call->geom) return 0;
     if (path == 1) return prefill_workspace_bytes(call);
-    return decode_layout(call, nullptr).bytes + 256;
+    // the layout depends on the SM count only through the chunk count; size for the largest
+    return decode_layout(call, nullptr, 1 << 20).bytes + 256;
 }
 
 extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
@@ -630,11 +682,11 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     if (!dev) return st;
     if ((st = validate_call(c)) != VY_OK) return st;
     if (c->n_tokens == 0) return ok();
-    DecodeLayout L = decode_layout(c, nullptr);
+    DecodeLayout L = decode_layout(c, nullptr, dev->sm_count);
     if (!c->workspace || c->workspace_bytes < L.bytes + 256)
         return fail(VY_ERR_WORKSPACE, "workspace %zu bytes, %zu needed", c->workspace_bytes, L.bytes + 256);
     char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 255) & ~uintptr_t(255));
-    L = decode_layout(c, base);
+    L = decode_layout(c, base, dev->sm_count);
     const vy_expert_geom& g = *c->geom;
     cudaStream_t s = as_stream(stream);
     const int nb = nb_for(c->n_tokens);
@@ -657,6 +709,8 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     pa.x_vec = aligned16(c->x) && (c->x_row_stride % 8 == 0);
     pa.hidden = g.hidden;
     pa.x_perm = L.x_perm;
+    pa.zero_ints = L.tile_done;
+    pa.zero_count = g.hidden / kTileRows;
     cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
     const bool timed = ev != nullptr && c->n_stage_events >= 4;
     if (timed && cudaEventRecord(ev[0], s) != cudaSuccess)
@@ -710,16 +764,15 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     dn.out = c->out;
     dn.out_stride = c->out_row_stride;
     dn.ybuf_g = c->contrib ? c->contrib : L.ybuf_g;
+    dn.global_combine = c->contrib == nullptr && !L.combine_in_cta;
+    dn.n_chunks = L.n_chunks;
+    dn.tile_done = L.tile_done;
 
     const int sm_count = dev->sm_count;
     const size_t dn_smem = dn_ring_smem() + (L.combine_in_cta ? size_t(c->n_tokens * c->top_k) * kTileRows * sizeof(float) : 0);
     const bool zero = g.has_zero != 0;
     st = c->act_dtype == VY_BF16 ? dispatch_sc<VY_BF16>(g.scale_dtype, zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed)
                                  : dispatch_sc<VY_F16>(g.scale_dtype, zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
-    if (st != VY_OK) return st;
-    if (!c->contrib && !L.combine_in_cta)
-        st = launch_combine(L.ybuf_g, c->expert_ids, c->ids_dtype == VY_I64, c->n_tokens, c->top_k,
-                            g.hidden, c->out, c->out_row_stride, dev->sm_count, s);
     if (st != VY_OK) return st;
     if (timed) cudaEventRecord(ev[3], s);
     return ok();

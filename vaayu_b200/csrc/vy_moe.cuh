@@ -28,6 +28,9 @@ struct PlanArgs {
     bool x_vec;
     int64_t hidden;
     uint16_t* x_perm;
+    // an int array the plan zeroes before anything else of the call runs (per-tile tickets)
+    int32_t* zero_ints;
+    int zero_count;
 };
 
 size_t plan_smem_bytes(int n_experts);

@@ -10,7 +10,6 @@ namespace {
 
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanWarps = kPlanThreads / 32;
-constexpr int kPermThreads = 256;
 
 __device__ __forceinline__ int load_id(const void* ids, bool ids64, int64_t j) {
     if (ids64) {
@@ -50,6 +49,91 @@ __device__ int block_exclusive_scan(int v, int* scratch, int* total) {
     return excl;
 }
 
+// The plan of a decode-sized call (n <= kSmallPlan rows, one row per thread): every position
+// is a count over the call's ids held in shared memory -- the stable sorted position of row j
+// is #{i : e_i < e_j or (e_i == e_j and i < j)} -- so the whole plan takes two barriers.
+constexpr int kSmallPlan = kPlanThreads;
+
+__device__ void plan_small(const PlanArgs& p) {
+    __shared__ int ids[kSmallPlan];
+    __shared__ int first[kSmallPlan];
+    __shared__ int cnt_of[kSmallPlan];
+    __shared__ int n_live_s, dropped_s;
+    const int n = static_cast<int>(p.n_tokens * p.top_k), j = threadIdx.x, E = p.n_experts;
+    if (j == 0) {
+        n_live_s = 0;
+        dropped_s = 0;
+    }
+    int e = -1;
+    if (j < n) {
+        e = load_id(p.ids, p.ids64, j);
+        if (e < 0 || e >= E) e = -1;
+        ids[j] = e;
+    }
+    __syncthreads();
+    int less = 0, same_before = 0, same = 0, dropped = 0;
+    if (j < n && e >= 0) {
+        for (int i = 0; i < n; ++i) {
+            const int v = ids[i];
+            if (v < 0) continue;
+            less += v < e;
+            same += v == e;
+            same_before += (v == e) & (i < j);
+        }
+        p.order[less + same_before] = j;
+    }
+    if (j < n && e < 0) dropped = 1;
+    const bool is_first = j < n && e >= 0 && same_before == 0;
+    if (j < n) {
+        first[j] = is_first;
+        cnt_of[j] = same;
+    }
+    if (dropped) atomicAdd(&dropped_s, 1);
+    __syncthreads();
+    if (is_first) {
+        int live_idx = 0, units = 0;
+        const int tpu = p.tok_per_unit;
+        for (int i = 0; i < n; ++i) {
+            if (!first[i] || ids[i] >= e) continue;
+            ++live_idx;
+            if (tpu > 0) units += (cnt_of[i] + tpu - 1) / tpu;
+        }
+        p.live_expert[live_idx] = e;
+        p.live_start[live_idx] = less;
+        if (p.unit_start) p.unit_start[live_idx] = units;
+        atomicAdd(&n_live_s, 1);
+    }
+    // each row's place among its token's slots: ascending id, then slot; dropped rows last
+    if (j < n) {
+        const int K = p.top_k, t = j / K, k = j - t * K;
+        int pos = 0;
+        for (int q = 0; q < K; ++q) {
+            const int v = ids[t * K + q];
+            const bool before = (e >= 0) ? (v >= 0 && (v < e || (v == e && q < k)))
+                                         : (v >= 0 || q < k);
+            pos += before;
+        }
+        p.slot_order[t * K + pos] = e >= 0 ? j : -1;
+    }
+    __syncthreads();
+    if (j == 0) {
+        const int nl = n_live_s;
+        int rows = 0, units = 0;
+        const int tpu = p.tok_per_unit;
+        for (int i = 0; i < n; ++i)
+            if (ids[i] >= 0) {
+                ++rows;
+                if (tpu > 0 && first[i]) units += (cnt_of[i] + tpu - 1) / tpu;
+            }
+        p.live_start[nl] = rows;
+        if (p.unit_start) p.unit_start[nl] = units;
+        p.counters[0] = nl;
+        p.counters[1] = dropped_s;
+        p.counters[2] = 0;
+        p.counters[3] = 0;
+    }
+}
+
 // Block 0: the plan.  Blocks >= 1: the activation permutation (x -> x_perm).
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
     if (blockIdx.x > 0) {
@@ -74,6 +158,12 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
             o.w = v[3] | (uint32_t(v[7]) << 16);
             *reinterpret_cast<uint4*>(p.x_perm + t * p.hidden + c) = o;
         }
+        return;
+    }
+    for (int i = threadIdx.x; i < p.zero_count; i += blockDim.x) p.zero_ints[i] = 0;
+    const int64_t n_rows_all = p.n_tokens * p.top_k;
+    if (n_rows_all <= kSmallPlan) {
+        plan_small(p);
         return;
     }
     extern __shared__ int cnt[];                            // [kPlanWarps][n_experts]
