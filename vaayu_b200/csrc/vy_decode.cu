@@ -40,27 +40,22 @@ constexpr int kDnDepth = VY_DN_DEPTH;    // down ring: stages in flight per warp
 constexpr int kTileRows = 16;
 
 struct GateUpParams {
-    int hidden, inter, gs, top_k;
-    const int64_t* table;
+    int hidden, inter, gs_shift, top_k;
     int64_t w_off[2], s_off[2], z_off[2];   // gate, up
-    const int32_t* order;
-    const int32_t* live_expert;
-    const int32_t* live_start;
-    const int32_t* unit_start;
-    int32_t* counters;
+    const PassEntry* passes;
+    const int32_t* unit_start;               // unit_start[n_live] = number of passes
+    int32_t* counters;                       // [0] n_live, [2] error flags
     const uint16_t* x_perm;
     uint16_t* h_perm;
     uint16_t* h_out;
 };
 
 struct DownParams {
-    int hidden, inter, gs, top_k;
+    int hidden, inter, gs_shift, top_k;
     int64_t n_tokens;
-    const int64_t* table;
     int64_t w_off, s_off, z_off;
-    const int32_t* order;
-    const int32_t* live_expert;
-    const int32_t* live_start;
+    const PassEntry* passes;
+    const int32_t* unit_start;
     const int32_t* slot_order;
     int32_t* counters;
     const uint16_t* h_perm;
@@ -71,73 +66,109 @@ struct DownParams {
     const int32_t* w_index;
     float* out;
     int64_t out_stride;
-    float* ybuf_g;      // non-null: contributions to global [n][hidden] instead of shared memory
+    float* ybuf_g;        // non-null: contributions to global [n][hidden] instead of shared memory
     bool global_combine;  // with ybuf_g: the last CTA of each row tile sums it into `out`
-    int n_chunks;       // CTAs sharing one row tile (its live experts interleaved over them)
-    int32_t* tile_done; // [hidden / 16] tickets, zeroed by the plan kernel of the same call
+    int n_chunks;         // CTAs sharing one row tile (its expert passes interleaved over them)
+    int32_t* tile_done;   // [hidden / 16] tickets, zeroed by the plan kernel of the same call
 };
 
-// Everything a warp needs about the unit (expert, 16-row tile, token pass) it works on.
-struct Unit {
+// What a warp needs about one unit of work: a pass of a live expert (and, for gate/up, a 16-row
+// tile of it).  Loaded one unit ahead of its use, so its latency hides behind the current unit.
+template <int NB>
+struct UnitInfo {
     const int32_t* pk;
     const void* sc;
     const int32_t* zp;
-    int tile, row0, ncols;   // row0 = first row of this pass in `order`
+    int ncols;
+    int tile;
+    int col_row[NB];   // row id of this lane's column (cb * 8 + g) in each block, -1 if none
     bool ok;
 };
 
-__device__ __forceinline__ int find_live(const int32_t* unit_start, int n_live, int pass_global) {
-    int lo = 0, hi = n_live - 1;
-    while (lo < hi) {
-        int mid = (lo + hi + 1) >> 1;
-        if (unit_start[mid] <= pass_global) lo = mid;
-        else hi = mid - 1;
+// The per-warp hand-off of unit descriptions from the issue side to the consuming side: the
+// warp-uniform part once, the row ids per column.  Q slots cover the issue side's lookahead
+// (kDepth - 1 stages, so at most kDepth - 1 units when a unit has a single stage).
+template <int NB, int Q>
+struct UnitQueue {
+    struct Head {
+        const int32_t* pk;
+        const void* sc;
+        const int32_t* zp;
+        int ncols, tile, ok;
+    } head[kWarps][Q];
+    int rows[kWarps][Q][NB * 8];
+
+    __device__ __forceinline__ void put(int warp, int slot, int lane, int g, const UnitInfo<NB>& u) {
+        if (lane == 0) head[warp][slot] = Head{u.pk, u.sc, u.zp, u.ncols, u.tile, u.ok};
+        if ((lane & 3) == 0)
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb) rows[warp][slot][cb * 8 + g] = u.col_row[cb];
     }
-    return lo;
-}
+    __device__ __forceinline__ UnitInfo<NB> get(int warp, int slot, int g) const {
+        const Head& h = head[warp][slot];
+        UnitInfo<NB> u;
+        u.pk = h.pk;
+        u.sc = h.sc;
+        u.zp = h.zp;
+        u.ncols = h.ncols;
+        u.tile = h.tile;
+        u.ok = h.ok;
+#pragma unroll
+        for (int cb = 0; cb < NB; ++cb) u.col_row[cb] = rows[warp][slot][cb * 8 + g];
+        return u;
+    }
+};
 
 template <int NB>
-__device__ __forceinline__ Unit resolve_gu(const GateUpParams& p, int n_live, int tiles, int u) {
-    Unit un;
-    const int pass_global = u / tiles;
-    un.tile = u - pass_global * tiles;
-    const int li = find_live(p.unit_start, n_live, pass_global);
-    const int pass = pass_global - p.unit_start[li];
-    const int e = p.live_expert[li];
-    const int first = p.live_start[li], count = p.live_start[li + 1] - first;
-    un.row0 = first + pass * NB * 8;
-    un.ncols = min(NB * 8, count - pass * NB * 8);
-    un.pk = reinterpret_cast<const int32_t*>(p.table[3 * e]);
-    un.sc = reinterpret_cast<const void*>(p.table[3 * e + 1]);
-    un.zp = reinterpret_cast<const int32_t*>(p.table[3 * e + 2]);
-    un.ok = ((reinterpret_cast<uintptr_t>(un.pk) & 15u) == 0) && un.pk != nullptr && un.sc != nullptr;
-    return un;
-}
-
-template <int ACT, int SC, bool ZERO>
-__device__ __forceinline__ void load_scale_bias(const void* sc, const int32_t* zp, int64_t s_off,
-                                                int64_t z_off, int row, int groups, int grp,
-                                                uint32_t& s_pair, uint32_t& b_pair) {
-    const float s = round_act<ACT>(load_scale<SC>(sc, s_off + int64_t(row) * groups + grp));
-    const uint32_t sb = act_bits<ACT>(s);
-    s_pair = sb | (sb << 16);
-    uint32_t z = 8u;
-    if constexpr (ZERO) {
-        const uint32_t zw = static_cast<uint32_t>(__ldg(zp + z_off + int64_t(row >> 3) * groups + grp));
-        z = (zw >> (4 * (row & 7))) & 15u;
+__device__ __forceinline__ UnitInfo<NB> load_unit(const PassEntry* passes, int pg, int tile, int g) {
+    UnitInfo<NB> u;
+    const PassEntry& pe = passes[pg];
+    u.pk = reinterpret_cast<const int32_t*>(pe.pk);
+    u.sc = reinterpret_cast<const void*>(pe.sc);
+    u.zp = reinterpret_cast<const int32_t*>(pe.zp);
+    u.ncols = pe.ncols;
+    u.tile = tile;
+#pragma unroll
+    for (int cb = 0; cb < NB; ++cb) {
+        const int col = cb * 8 + g;
+        u.col_row[cb] = col < u.ncols ? pe.rows[col] : -1;
     }
-    b_pair = int4_bias_pair<ACT>(z);
+    u.ok = u.pk != nullptr && u.sc != nullptr && (reinterpret_cast<uintptr_t>(u.pk) & 15u) == 0;
+    return u;
 }
 
+// Activation-dtype bits of one scale, duplicated into both halves of a pair register.
+template <int ACT, int SC>
+__device__ __forceinline__ uint32_t scale_pair(const void* base, int64_t idx) {
+    uint32_t b;
+    if constexpr (SC == ACT) {
+        b = __ldg(reinterpret_cast<const unsigned short*>(base) + idx);
+    } else {
+        b = act_bits<ACT>(load_scale<SC>(base, idx));
+    }
+    return __byte_perm(b, 0, 0x1010);
+}
+
+template <int ACT, bool ZERO>
+__device__ __forceinline__ uint32_t bias_pair(const int32_t* zp, int64_t idx, int nib) {
+    if constexpr (ZERO) {
+        const uint32_t zw = static_cast<uint32_t>(__ldg(zp + idx));
+        return int4_bias_pair<ACT>((zw >> (4 * nib)) & 15u);
+    } else {
+        return int4_bias_pair<ACT>(8u);
+    }
+}
+
+// One 16-byte chunk (4 words = 32 codes) of one row, dequantised to 4 x 4 activation pairs.
 template <int ACT>
-__device__ __forceinline__ void dequant4(const uint4& w, uint32_t bias, uint32_t scale,
-                                         uint32_t (&out)[4][4]) {
+__device__ __forceinline__ void dequant_chunk(const uint4& w, uint32_t bias, uint32_t scale,
+                                              uint32_t (&a)[4][4]) {
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int wi = 0; wi < 4; ++wi)
 #pragma unroll
         for (int j = 0; j < 4; ++j)
-            out[wi][j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[wi], j), bias), scale);
+            a[wi][j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[wi], j), bias), scale);
 }
 
 template <int ACT, int SC, bool ZERO, int NB>
@@ -146,6 +177,7 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
     uint4* my_ring = ring + warp * (kGuDepth * 4 * 32);
+    __shared__ UnitQueue<NB, kGuDepth> queue;
 
     grid_dependency_wait();
     grid_dependents_launch();
@@ -158,74 +190,102 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
     if (gw >= total_units) return;
     const int my_units = (total_units - gw + nw - 1) / nw;
     const int spu = p.hidden / kStageK;
-    const int total_stages = my_units * spu;
     const int wpr = p.hidden / 8;
-    const int groups = p.hidden / p.gs;
+    const int groups = p.hidden >> p.gs_shift;
 
-    // issue cursor
-    int iu = -1;
-    Unit iunit{};
-    auto issue = [&](int s) {
-        if (s < total_stages) {
-            const int ui = s / spu, ks = s - ui * spu;
-            if (ui != iu) {
-                iu = ui;
-                iunit = resolve_gu<NB>(p, n_live, tiles, gw + ui * nw);
-            }
-            if (iunit.ok) {
-                const int slot = s % kGuDepth;
-                const int64_t rg = int64_t(iunit.tile * kTileRows + g) * wpr + ks * 16 + tig * 4;
-                const int32_t* src_g = iunit.pk + p.w_off[0] + rg;
-                const int32_t* src_u = iunit.pk + p.w_off[1] + rg;
-                uint4* dst = my_ring + slot * 128 + lane;
-                cp_async16(dst, src_g);
-                cp_async16(dst + 32, src_g + 8 * wpr);
-                cp_async16(dst + 64, src_u);
-                cp_async16(dst + 96, src_u + 8 * wpr);
-            }
-        }
-        cp_async_commit();
+    auto unit_at = [&](int i) {
+        const int u = gw + i * nw;
+        const int pg = u / tiles;
+        return load_unit<NB>(p.passes, pg, u - pg * tiles, g);
     };
 
+    // ── issue side: kGuDepth - 1 stages ahead of the consuming side ─────────────────────────
+    int i_ui = 0, i_ks = 0, i_slot = 0, i_left = my_units * spu;
+    UnitInfo<NB> i_nxt = unit_at(0);
+    const int32_t* i_src_g = nullptr;
+    const int32_t* i_src_u = nullptr;
+    bool i_ok = false;
+    auto issue = [&]() {
+        if (i_left > 0) {
+            if (i_ks == 0) {
+                const UnitInfo<NB> cur = i_nxt;
+                queue.put(warp, i_ui % kGuDepth, lane, g, cur);
+                if (i_ui + 1 < my_units) i_nxt = unit_at(i_ui + 1);
+                i_ok = cur.ok;
+                const int64_t row_off = int64_t(cur.tile * kTileRows + g) * wpr + tig * 4;
+                i_src_g = cur.pk + p.w_off[0] + row_off;
+                i_src_u = cur.pk + p.w_off[1] + row_off;
+            }
+            if (i_ok) {
+                uint4* dst = my_ring + i_slot * 128 + lane;
+                cp_async16(dst, i_src_g);
+                cp_async16(dst + 32, i_src_g + 8 * wpr);
+                cp_async16(dst + 64, i_src_u);
+                cp_async16(dst + 96, i_src_u + 8 * wpr);
+            }
+            i_src_g += 16;
+            i_src_u += 16;
+            if (++i_ks == spu) {
+                i_ks = 0;
+                ++i_ui;
+            }
+            --i_left;
+        }
+        cp_async_commit();
+        if (++i_slot == kGuDepth) i_slot = 0;
+    };
 #pragma unroll
-    for (int s = 0; s < kGuDepth - 1; ++s) issue(s);
+    for (int s = 0; s < kGuDepth - 1; ++s) issue();
 
+    // ── consuming side ───────────────────────────────────────────────────────────────────
     float acc_g[NB][4], acc_u[NB][4];
 #pragma unroll
     for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc_g[cb][i] = acc_u[cb][i] = 0.f;
-
-    int cu = -1;
-    Unit cunit{};
+    UnitInfo<NB> cu{};
+    int c_ui = 0, c_ks = 0, c_slot = 0;
     int xoff[NB];
-    for (int s = 0; s < total_stages; ++s) {
-        issue(s + kGuDepth - 1);
-        const int ui = s / spu, ks = s - ui * spu;
-        if (ui != cu) {
-            cu = ui;
-            cunit = resolve_gu<NB>(p, n_live, tiles, gw + ui * nw);
+    int sidx[4];      // scale element index of rows g, g+8 of gate, up at this thread's K offset
+    int zidx[2];      // zero word index (rows g and g+8 share a nibble position) of gate, up
+    const int kfirst = tig * 32;
+    for (int s = my_units * spu; s > 0; --s) {
+        issue();
+        if (c_ks == 0) {
+            __syncwarp();
+            cu = queue.get(warp, c_ui % kGuDepth, g);
+            const int row = cu.tile * kTileRows + g;
 #pragma unroll
-            for (int cb = 0; cb < NB; ++cb) {
-                const int col = cb * 8 + g;
-                xoff[cb] = col < cunit.ncols ? (p.order[cunit.row0 + col] / p.top_k) * p.hidden : -1;
+            for (int m = 0; m < 2; ++m) {
+                sidx[2 * m] = static_cast<int>(p.s_off[m]) + row * groups;
+                sidx[2 * m + 1] = sidx[2 * m] + 8 * groups;
+                zidx[m] = static_cast<int>(p.z_off[m]) + (row >> 3) * groups;
             }
-            if (!cunit.ok && lane == 0) atomicOr(p.counters + 2, 1);
+#pragma unroll
+            for (int cb = 0; cb < NB; ++cb)
+                xoff[cb] = cu.col_row[cb] >= 0 ? (cu.col_row[cb] / p.top_k) * p.hidden + kfirst : -1;
+            if (!cu.ok && lane == 0) atomicOr(p.counters + 2, 1);
         }
         cp_async_wait<kGuDepth - 1>();
-        if (cunit.ok) {
-            const uint4* st = my_ring + (s % kGuDepth) * 128 + lane;
+        if (cu.ok) {
+            const int kx = c_ks * kStageK;
+            // the first token block's activations first: their L2 latency hides behind the
+            // dequant work below (further blocks, rarely populated at decode sizes, load in line)
+            uint4 xv0[4];
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi)
+                xv0[wi] = xoff[0] >= 0 ? ld_nc_v4(p.x_perm + xoff[0] + kx + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
+            const uint4* st = my_ring + c_slot * 128 + lane;
             const uint4 wg0 = st[0], wg8 = st[32], wu0 = st[64], wu8 = st[96];
-            const int row = cunit.tile * kTileRows + g;
-            const int grp = (ks * kStageK + tig * 32) / p.gs;
-            uint32_t sg0, bg0, sg8, bg8, su0, bu0, su8, bu8;
-            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[0], p.z_off[0], row, groups, grp, sg0, bg0);
-            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[0], p.z_off[0], row + 8, groups, grp, sg8, bg8);
-            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[1], p.z_off[1], row, groups, grp, su0, bu0);
-            load_scale_bias<ACT, SC, ZERO>(cunit.sc, cunit.zp, p.s_off[1], p.z_off[1], row + 8, groups, grp, su8, bu8);
-            const int kx = ks * kStageK + tig * 32;
-            const uint32_t wgw0[4] = {wg0.x, wg0.y, wg0.z, wg0.w}, wgw8[4] = {wg8.x, wg8.y, wg8.z, wg8.w};
-            const uint32_t wuw0[4] = {wu0.x, wu0.y, wu0.z, wu0.w}, wuw8[4] = {wu8.x, wu8.y, wu8.z, wu8.w};
+            const int grp = (kx + kfirst) >> p.gs_shift;
+            const uint32_t sg0 = scale_pair<ACT, SC>(cu.sc, sidx[0] + grp);
+            const uint32_t sg8 = scale_pair<ACT, SC>(cu.sc, sidx[1] + grp);
+            const uint32_t su0 = scale_pair<ACT, SC>(cu.sc, sidx[2] + grp);
+            const uint32_t su8 = scale_pair<ACT, SC>(cu.sc, sidx[3] + grp);
+            const uint32_t bg0 = bias_pair<ACT, ZERO>(cu.zp, zidx[0] + grp, g);
+            const uint32_t bg8 = bias_pair<ACT, ZERO>(cu.zp, zidx[0] + groups + grp, g);
+            const uint32_t bu0 = bias_pair<ACT, ZERO>(cu.zp, zidx[1] + grp, g);
+            const uint32_t bu8 = bias_pair<ACT, ZERO>(cu.zp, zidx[1] + groups + grp, g);
             // The stage's 128-term partial dots start from zero and join the running sums with
             // round-to-nearest fp32 adds: the tensor core's own accumulate truncates against the
             // accumulator's magnitude, so a long chain inside it drifts (biased) from the fp32 sum.
@@ -234,6 +294,8 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
             for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) sg[cb][i] = su[cb][i] = 0.f;
+            const uint32_t wgw0[4] = {wg0.x, wg0.y, wg0.z, wg0.w}, wgw8[4] = {wg8.x, wg8.y, wg8.z, wg8.w};
+            const uint32_t wuw0[4] = {wu0.x, wu0.y, wu0.z, wu0.w}, wuw8[4] = {wu8.x, wu8.y, wu8.z, wu8.w};
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
                 uint32_t ag0[4], ag8[4], au0[4], au8[4];
@@ -246,9 +308,10 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
                 }
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
-                    if (cb * 8 >= cunit.ncols) break;     // warp-uniform: no tokens left
-                    uint4 xv = make_uint4(0u, 0u, 0u, 0u);
-                    if (xoff[cb] >= 0) xv = ld_nc_v4(p.x_perm + xoff[cb] + kx + wi * 8);
+                    if (cb * 8 >= cu.ncols) break;     // warp-uniform: no tokens left
+                    uint4 xv = xv0[wi];
+                    if (cb > 0)
+                        xv = xoff[cb] >= 0 ? ld_nc_v4(p.x_perm + xoff[cb] + kx + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
                     mma_16816<ACT>(sg[cb], ag0[0], ag8[0], ag0[1], ag8[1], xv.x, xv.y);
                     mma_16816<ACT>(sg[cb], ag0[2], ag8[2], ag0[3], ag8[3], xv.z, xv.w);
                     mma_16816<ACT>(su[cb], au0[0], au8[0], au0[1], au8[1], xv.x, xv.y);
@@ -257,7 +320,7 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
             }
 #pragma unroll
             for (int cb = 0; cb < NB; ++cb) {
-                if (cb * 8 >= cunit.ncols) break;
+                if (cb * 8 >= cu.ncols) break;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     acc_g[cb][i] = __fadd_rn(acc_g[cb][i], sg[cb][i]);
@@ -265,16 +328,18 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
                 }
             }
         }
-        if (ks == spu - 1) {
-            if (cunit.ok) {
+        if (++c_slot == kGuDepth) c_slot = 0;
+        if (++c_ks == spu) {
+            if (cu.ok) {
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int col = cb * 8 + 2 * tig + (i & 1);
-                        if (col < cunit.ncols) {
-                            const int r = cunit.tile * kTileRows + g + 8 * (i >> 1);
-                            const int rowid = p.order[cunit.row0 + col];
+                        // every lane takes part in the shuffle; only live columns store
+                        const int rowid = __shfl_sync(0xffffffffu, cu.col_row[cb], (col - cb * 8) * 4);
+                        if (col < cu.ncols) {
+                            const int r = cu.tile * kTileRows + g + 8 * (i >> 1);
                             const float gv = round_act<ACT>(acc_g[cb][i]);
                             const float uv = round_act<ACT>(acc_u[cb][i]);
                             const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
@@ -289,6 +354,8 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
             for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc_g[cb][i] = acc_u[cb][i] = 0.f;
+            c_ks = 0;
+            ++c_ui;
         }
     }
     cp_async_wait<0>();
@@ -300,118 +367,97 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) down_kernel(Down
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
     uint4* my_ring = ring + warp * (kDnDepth * 2 * 32);
+    __shared__ UnitQueue<NB, kDnDepth> queue;
     float* ybuf = reinterpret_cast<float*>(ring + kWarps * kDnDepth * 2 * 32);
     const int n_tiles = p.hidden / kTileRows;
     const int tile = blockIdx.x % n_tiles, chunk = blockIdx.x / n_tiles;
-    const int wstride = kWarps * p.n_chunks;     // live experts: li = chunk*kWarps + warp + q*wstride
+    const int wstride = kWarps * p.n_chunks;   // passes: pg = chunk*kWarps + warp + q*wstride
 
     grid_dependency_wait();
 
     const int n_live = p.counters[0];
+    const int n_pass = n_live > 0 ? p.unit_start[n_live] : 0;
+    const int pg0 = chunk * kWarps + warp;
+    const int my_units = pg0 < n_pass ? (n_pass - pg0 + wstride - 1) / wstride : 0;
     const int spu = p.inter / kStageK;
     const int wpr = p.inter / 8;
-    const int groups = p.inter / p.gs;
-    constexpr int kCols = NB * 8;
+    const int groups = p.inter >> p.gs_shift;
+    auto unit_at = [&](int i) { return load_unit<NB>(p.passes, pg0 + i * wstride, tile, g); };
 
-    // The warp's work: experts li = warp, warp + kWarps, ...; each in ceil(count / kCols) passes.
-    // Cursor over (li, pass, ks).
-    struct Cursor {
-        int li, pass, npass, ks;
-    };
-    auto npass_of = [&](int li) -> int {
-        if (li >= n_live) return 0;
-        const int c = p.live_start[li + 1] - p.live_start[li];
-        return (c + kCols - 1) / kCols;
-    };
-    auto advance = [&](Cursor& c) {
-        if (++c.ks == spu) {
-            c.ks = 0;
-            if (++c.pass == c.npass) {
-                c.pass = 0;
-                c.li += wstride;
-                c.npass = npass_of(c.li);
-            }
-        }
-    };
-    const int li0 = chunk * kWarps + warp;
-    Cursor ic{li0, 0, npass_of(li0), 0};
-    int ic_li = -1;
-    const int32_t* ipk = nullptr;
-    bool iok = false;
-    int s_issue = 0;
+    int i_ui = 0, i_ks = 0, i_slot = 0, i_left = my_units * spu;
+    UnitInfo<NB> i_nxt{};
+    if (my_units > 0) i_nxt = unit_at(0);
+    const int32_t* i_src = nullptr;
+    bool i_ok = false;
     auto issue = [&]() {
-        if (ic.li < n_live) {
-            if (ic.li != ic_li) {
-                ic_li = ic.li;
-                const int e = p.live_expert[ic.li];
-                ipk = reinterpret_cast<const int32_t*>(p.table[3 * e]);
-                iok = ipk != nullptr && (reinterpret_cast<uintptr_t>(ipk) & 15u) == 0;
+        if (i_left > 0) {
+            if (i_ks == 0) {
+                const UnitInfo<NB> cur = i_nxt;
+                queue.put(warp, i_ui % kDnDepth, lane, g, cur);
+                if (i_ui + 1 < my_units) i_nxt = unit_at(i_ui + 1);
+                i_ok = cur.ok;
+                i_src = cur.pk + p.w_off + int64_t(tile * kTileRows + g) * wpr + tig * 4;
             }
-            if (iok) {
-                const int slot = s_issue % kDnDepth;
-                const int32_t* src = ipk + p.w_off + int64_t(tile * kTileRows + g) * wpr + ic.ks * 16 + tig * 4;
-                uint4* dst = my_ring + slot * 64 + lane;
-                cp_async16(dst, src);
-                cp_async16(dst + 32, src + 8 * wpr);
+            if (i_ok) {
+                uint4* dst = my_ring + i_slot * 64 + lane;
+                cp_async16(dst, i_src);
+                cp_async16(dst + 32, i_src + 8 * wpr);
             }
-            advance(ic);
+            i_src += 16;
+            if (++i_ks == spu) {
+                i_ks = 0;
+                ++i_ui;
+            }
+            --i_left;
         }
-        ++s_issue;
         cp_async_commit();
+        if (++i_slot == kDnDepth) i_slot = 0;
     };
 #pragma unroll
     for (int s = 0; s < kDnDepth - 1; ++s) issue();
 
-    Cursor cc{li0, 0, npass_of(li0), 0};
-    int cc_li = -1;
-    const void* csc = nullptr;
-    const int32_t* czp = nullptr;
-    bool cok = false;
-    int hoff[NB];
-    int row0 = 0, ncols = 0;
     float acc[NB][4];
 #pragma unroll
     for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[cb][i] = 0.f;
-
-    for (int s = 0; cc.li < n_live; ++s) {
+    UnitInfo<NB> cu{};
+    int c_ui = 0, c_ks = 0, c_slot = 0;
+    int hoff[NB];
+    const int row = tile * kTileRows + g;
+    const int sidx0 = static_cast<int>(p.s_off) + row * groups, sidx8 = sidx0 + 8 * groups;
+    const int zidx = static_cast<int>(p.z_off) + (row >> 3) * groups;
+    const int kfirst = tig * 32;
+    for (int s = my_units * spu; s > 0; --s) {
         issue();
-        if (cc.ks == 0) {
-            if (cc.li != cc_li) {
-                cc_li = cc.li;
-                const int e = p.live_expert[cc.li];
-                const int32_t* pk = reinterpret_cast<const int32_t*>(p.table[3 * e]);
-                csc = reinterpret_cast<const void*>(p.table[3 * e + 1]);
-                czp = reinterpret_cast<const int32_t*>(p.table[3 * e + 2]);
-                cok = pk != nullptr && csc != nullptr && (reinterpret_cast<uintptr_t>(pk) & 15u) == 0;
-                if (!cok && lane == 0) atomicOr(p.counters + 2, 1);
-            }
-            const int first = p.live_start[cc.li], count = p.live_start[cc.li + 1] - first;
-            row0 = first + cc.pass * kCols;
-            ncols = min(kCols, count - cc.pass * kCols);
+        if (c_ks == 0) {
+            __syncwarp();
+            cu = queue.get(warp, c_ui % kDnDepth, g);
 #pragma unroll
-            for (int cb = 0; cb < NB; ++cb) {
-                const int col = cb * 8 + g;
-                hoff[cb] = col < ncols ? p.order[row0 + col] * p.inter : -1;
-            }
+            for (int cb = 0; cb < NB; ++cb)
+                hoff[cb] = cu.col_row[cb] >= 0 ? cu.col_row[cb] * p.inter + kfirst : -1;
+            if (!cu.ok && lane == 0) atomicOr(p.counters + 2, 1);
         }
         cp_async_wait<kDnDepth - 1>();
-        if (cok) {
-            const uint4* st = my_ring + (s % kDnDepth) * 64 + lane;
+        if (cu.ok) {
+            const int kh = c_ks * kStageK;
+            uint4 hv0[4];
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi)
+                hv0[wi] = hoff[0] >= 0 ? ld_nc_v4(p.h_perm + hoff[0] + kh + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
+            const uint4* st = my_ring + c_slot * 64 + lane;
             const uint4 w0 = st[0], w8 = st[32];
-            const int row = tile * kTileRows + g;
-            const int grp = (cc.ks * kStageK + tig * 32) / p.gs;
-            uint32_t s0, b0, s8, b8;
-            load_scale_bias<ACT, SC, ZERO>(csc, czp, p.s_off, p.z_off, row, groups, grp, s0, b0);
-            load_scale_bias<ACT, SC, ZERO>(csc, czp, p.s_off, p.z_off, row + 8, groups, grp, s8, b8);
-            const int kh = cc.ks * kStageK + tig * 32;
-            const uint32_t ww0[4] = {w0.x, w0.y, w0.z, w0.w}, ww8[4] = {w8.x, w8.y, w8.z, w8.w};
+            const int grp = (kh + kfirst) >> p.gs_shift;
+            const uint32_t s0 = scale_pair<ACT, SC>(cu.sc, sidx0 + grp);
+            const uint32_t s8 = scale_pair<ACT, SC>(cu.sc, sidx8 + grp);
+            const uint32_t b0 = bias_pair<ACT, ZERO>(cu.zp, zidx + grp, g);
+            const uint32_t b8 = bias_pair<ACT, ZERO>(cu.zp, zidx + groups + grp, g);
             float sp[NB][4];   // the stage's partial dots (see gate_up_kernel)
 #pragma unroll
             for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) sp[cb][i] = 0.f;
+            const uint32_t ww0[4] = {w0.x, w0.y, w0.z, w0.w}, ww8[4] = {w8.x, w8.y, w8.z, w8.w};
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {
                 uint32_t a0[4], a8[4];
@@ -422,30 +468,32 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) down_kernel(Down
                 }
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
-                    if (cb * 8 >= ncols) break;            // warp-uniform: no tokens left
-                    uint4 hv = make_uint4(0u, 0u, 0u, 0u);
-                    if (hoff[cb] >= 0) hv = ld_nc_v4(p.h_perm + hoff[cb] + kh + wi * 8);
+                    if (cb * 8 >= cu.ncols) break;     // warp-uniform: no tokens left
+                    uint4 hv = hv0[wi];
+                    if (cb > 0)
+                        hv = hoff[cb] >= 0 ? ld_nc_v4(p.h_perm + hoff[cb] + kh + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
                     mma_16816<ACT>(sp[cb], a0[0], a8[0], a0[1], a8[1], hv.x, hv.y);
                     mma_16816<ACT>(sp[cb], a0[2], a8[2], a0[3], a8[3], hv.z, hv.w);
                 }
             }
 #pragma unroll
             for (int cb = 0; cb < NB; ++cb) {
-                if (cb * 8 >= ncols) break;
+                if (cb * 8 >= cu.ncols) break;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[cb][i] = __fadd_rn(acc[cb][i], sp[cb][i]);
             }
         }
-        if (cc.ks == spu - 1) {
-            if (cok) {
+        if (++c_slot == kDnDepth) c_slot = 0;
+        if (++c_ks == spu) {
+            if (cu.ok) {
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const int col = cb * 8 + 2 * tig + (i & 1);
-                        if (col < ncols) {
+                        const int rowid = __shfl_sync(0xffffffffu, cu.col_row[cb], (col - cb * 8) * 4);
+                        if (col < cu.ncols) {
                             const int r = g + 8 * (i >> 1);
-                            const int rowid = p.order[row0 + col];
                             const int64_t t = rowid / p.top_k;
                             const int k = rowid - int(t) * p.top_k;
                             const int widx = p.w_index ? p.w_index[rowid] : k;
@@ -463,8 +511,9 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) down_kernel(Down
             for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[cb][i] = 0.f;
+            c_ks = 0;
+            ++c_ui;
         }
-        advance(cc);
     }
     cp_async_wait<0>();
     if (p.ybuf_g && !p.global_combine) return;   // per-row contributions only (expert parallel)
@@ -573,6 +622,7 @@ int dispatch_sc(int sc, bool zero, int nb, const GateUpParams& gu, const DownPar
 
 struct DecodeLayout {
     int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters, *tile_done;
+    PassEntry* passes;
     uint16_t *x_perm, *h_perm;
     float* ybuf_g;
     size_t bytes;
@@ -582,7 +632,7 @@ struct DecodeLayout {
 
 // Column blocks (8 tokens each) one pass of a unit holds: the largest token count an expert
 // can have is n_tokens; empty blocks are skipped at run time, so NB only costs registers.
-int nb_for(int64_t n_tokens) { return n_tokens <= 16 ? 1 : (n_tokens <= 64 ? 2 : 4); }
+int nb_for(int64_t n_tokens) { return n_tokens <= 32 ? 1 : (n_tokens <= 64 ? 2 : 4); }
 
 // CTAs per down-projection row tile: enough for ~2 resident CTAs per SM, but no more chunks
 // than the call can have live experts per warp.
@@ -609,6 +659,10 @@ DecodeLayout decode_layout(const vy_moe_call* c, void* base, int sm_count) {
     L.slot_order = cv.take<int32_t>(n);
     L.counters = cv.take<int32_t>(4);
     L.tile_done = cv.take<int32_t>(H / kTileRows);
+    {
+        const int64_t tpu = nb_for(c->n_tokens) * 8, max_live = n < E ? n : E;
+        L.passes = cv.take<PassEntry>(n / tpu + max_live + 1);
+    }
     L.x_perm = cv.take<uint16_t>(c->n_tokens * H);
     L.h_perm = cv.take<uint16_t>(n * I);
     L.n_chunks = down_chunks(c, sm_count);
@@ -711,6 +765,8 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     pa.x_perm = L.x_perm;
     pa.zero_ints = L.tile_done;
     pa.zero_count = g.hidden / kTileRows;
+    pa.expert_table = c->expert_table;
+    pa.passes = L.passes;
     cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
     const bool timed = ev != nullptr && c->n_stage_events >= 4;
     if (timed && cudaEventRecord(ev[0], s) != cudaSuccess)
@@ -718,21 +774,21 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     if ((st = launch_plan(pa, dev->sm_count, s)) != VY_OK) return st;
     if (timed) cudaEventRecord(ev[1], s);
 
+    int gs_shift = 0;
+    while ((1 << gs_shift) < g.group_size) ++gs_shift;
+
     GateUpParams gu{};
     gu.hidden = g.hidden;
     gu.inter = g.inter;
-    gu.gs = g.group_size;
+    gu.gs_shift = gs_shift;
     gu.top_k = c->top_k;
-    gu.table = c->expert_table;
     gu.w_off[0] = g.word_off[0];
     gu.w_off[1] = g.word_off[1];
     gu.s_off[0] = g.scale_off[0];
     gu.s_off[1] = g.scale_off[1];
     gu.z_off[0] = g.zero_off[0];
     gu.z_off[1] = g.zero_off[1];
-    gu.order = L.order;
-    gu.live_expert = L.live_expert;
-    gu.live_start = L.live_start;
+    gu.passes = L.passes;
     gu.unit_start = L.unit_start;
     gu.counters = L.counters;
     gu.x_perm = L.x_perm;
@@ -742,16 +798,14 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     DownParams dn{};
     dn.hidden = g.hidden;
     dn.inter = g.inter;
-    dn.gs = g.group_size;
+    dn.gs_shift = gs_shift;
     dn.top_k = c->top_k;
     dn.n_tokens = c->n_tokens;
-    dn.table = c->expert_table;
     dn.w_off = g.word_off[2];
     dn.s_off = g.scale_off[2];
     dn.z_off = g.zero_off[2];
-    dn.order = L.order;
-    dn.live_expert = L.live_expert;
-    dn.live_start = L.live_start;
+    dn.passes = L.passes;
+    dn.unit_start = L.unit_start;
     dn.slot_order = L.slot_order;
     dn.counters = L.counters;
     dn.h_perm = L.h_perm;

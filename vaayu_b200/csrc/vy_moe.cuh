@@ -7,6 +7,16 @@ namespace vy {
 
 constexpr int kMaxTopK = 32;
 constexpr int kMaxExperts = 1024;
+constexpr int kMaxPassCols = 32;   // tokens one pass of an expert carries (8 per column block)
+
+// One pass of one live expert: the unit of work of the GEMV kernels, fully resolved by the
+// routing plan so a kernel fetches it with independent loads (no dependent pointer chase).
+struct __align__(16) PassEntry {
+    int64_t pk, sc, zp;            // the expert's packed / scale / zero streams
+    int32_t row0;                  // first position of this pass in `order`
+    int32_t ncols;                 // routed rows in this pass (<= tok_per_unit)
+    int32_t rows[kMaxPassCols];    // their row ids (token * top_k + slot)
+};
 
 // Arguments of the routing plan kernel (block 0) and the activation permutation (blocks >= 1).
 struct PlanArgs {
@@ -31,6 +41,9 @@ struct PlanArgs {
     // an int array the plan zeroes before anything else of the call runs (per-tile tickets)
     int32_t* zero_ints;
     int zero_count;
+    // optional pass table (needs unit_start and tok_per_unit): one PassEntry per expert pass
+    const int64_t* expert_table;
+    PassEntry* passes;
 };
 
 size_t plan_smem_bytes(int n_experts);

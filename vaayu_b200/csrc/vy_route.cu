@@ -49,89 +49,162 @@ __device__ int block_exclusive_scan(int v, int* scratch, int* total) {
     return excl;
 }
 
-// The plan of a decode-sized call (n <= kSmallPlan rows, one row per thread): every position
-// is a count over the call's ids held in shared memory -- the stable sorted position of row j
-// is #{i : e_i < e_j or (e_i == e_j and i < j)} -- so the whole plan takes two barriers.
+// The plan of a decode-sized call (n <= kSmallPlan rows): a bitonic sort of the keys
+// (expert id << 10 | row) -- unique, so the sort is stable by construction -- with warp shuffles
+// for the exchanges inside a warp and shared memory above that, then the run boundaries of the
+// sorted keys give the live experts.  n <= 32 stays in one warp with no barrier at all.
 constexpr int kSmallPlan = kPlanThreads;
+constexpr int kKeyNone = 0x7FFFFFFF;
+
+__device__ __forceinline__ int warp_sort_step(int key, int lane_id, int k, int j) {
+    const int other = __shfl_xor_sync(0xffffffffu, key, j);
+    const bool up = (lane_id & k) == 0, lower = (lane_id & j) == 0;
+    return (lower == up) ? min(key, other) : max(key, other);
+}
+
+// Each row's place among its token's slots (ascending id, then slot; dropped rows last).
+__device__ __forceinline__ void write_slot_order(const PlanArgs& p, const int* ids, int j, int n) {
+    if (j >= n) return;
+    const int K = p.top_k, t = j / K, k = j - t * K, e = ids[j];
+    int pos = 0;
+    for (int q = 0; q < K; ++q) {
+        const int v = ids[t * K + q];
+        pos += (e >= 0) ? (v >= 0 && (v < e || (v == e && q < k))) : (v >= 0 || q < k);
+    }
+    p.slot_order[t * K + pos] = e >= 0 ? j : -1;
+}
+
+// Sorted position `pos` of a live expert's run (run start `ls`, length `count`, first pass
+// `ustart`, expert `e`) holds row `row`: file it in the pass table.
+__device__ __forceinline__ void file_pass_row(const PlanArgs& p, int e, int ls, int count, int ustart,
+                                              int pos, int row) {
+    if (!p.passes) return;
+    const int tpu = p.tok_per_unit, r = pos - ls, q = r / tpu, col = r - q * tpu;
+    PassEntry& pe = p.passes[ustart + q];
+    pe.rows[col] = row;
+    if (col == 0) {
+        pe.pk = p.expert_table[3 * e];
+        pe.sc = p.expert_table[3 * e + 1];
+        pe.zp = p.expert_table[3 * e + 2];
+        pe.row0 = pos;
+        pe.ncols = min(tpu, count - q * tpu);
+    }
+}
 
 __device__ void plan_small(const PlanArgs& p) {
     __shared__ int ids[kSmallPlan];
-    __shared__ int first[kSmallPlan];
-    __shared__ int cnt_of[kSmallPlan];
-    __shared__ int n_live_s, dropped_s;
-    const int n = static_cast<int>(p.n_tokens * p.top_k), j = threadIdx.x, E = p.n_experts;
-    if (j == 0) {
-        n_live_s = 0;
-        dropped_s = 0;
-    }
+    __shared__ int keys[kSmallPlan];
+    __shared__ int ls[kSmallPlan + 1];
+    __shared__ int scratch[kPlanWarps + 1];
+    const int n = static_cast<int>(p.n_tokens * p.top_k), tid = threadIdx.x, E = p.n_experts;
+    const int lane = tid & 31;
     int e = -1;
-    if (j < n) {
-        e = load_id(p.ids, p.ids64, j);
+    if (tid < n) {
+        e = load_id(p.ids, p.ids64, tid);
         if (e < 0 || e >= E) e = -1;
-        ids[j] = e;
+        ids[tid] = e;
     }
-    __syncthreads();
-    int less = 0, same_before = 0, same = 0, dropped = 0;
-    if (j < n && e >= 0) {
-        for (int i = 0; i < n; ++i) {
-            const int v = ids[i];
-            if (v < 0) continue;
-            less += v < e;
-            same += v == e;
-            same_before += (v == e) & (i < j);
+    int key = (tid < n && e >= 0) ? ((e << 10) | tid) : kKeyNone;
+    const int tpu = p.tok_per_unit;
+    if (n <= 32) {
+        if (tid >= 32) return;
+        __syncwarp();
+        for (int k = 2; k <= 32; k <<= 1)
+            for (int j = k >> 1; j > 0; j >>= 1) key = warp_sort_step(key, lane, k, j);
+        const bool valid = key != kKeyNone;
+        const int ek = valid ? (key >> 10) : -1;
+        const int prev = __shfl_up_sync(0xffffffffu, ek, 1);
+        const bool first = valid && (lane == 0 || prev != ek);
+        const unsigned fm = __ballot_sync(0xffffffffu, first);
+        const int n_valid = __popc(__ballot_sync(0xffffffffu, valid));
+        const int li = __popc(fm & ((1u << lane) - 1u));
+        // run end = next first position (or n_valid); units prefix over the live runs
+        const unsigned later = fm & ~((2u << lane) - 1u);
+        const int run_end = later ? (__ffs(later) - 1) : n_valid;
+        int units = (first && tpu > 0) ? (run_end - lane + tpu - 1) / tpu : 0;
+        int incl = units;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
         }
-        p.order[less + same_before] = j;
-    }
-    if (j < n && e < 0) dropped = 1;
-    const bool is_first = j < n && e >= 0 && same_before == 0;
-    if (j < n) {
-        first[j] = is_first;
-        cnt_of[j] = same;
-    }
-    if (dropped) atomicAdd(&dropped_s, 1);
-    __syncthreads();
-    if (is_first) {
-        int live_idx = 0, units = 0;
-        const int tpu = p.tok_per_unit;
-        for (int i = 0; i < n; ++i) {
-            if (!first[i] || ids[i] >= e) continue;
-            ++live_idx;
-            if (tpu > 0) units += (cnt_of[i] + tpu - 1) / tpu;
+        if (valid) p.order[lane] = key & 1023;
+        if (first) {
+            p.live_expert[li] = ek;
+            p.live_start[li] = lane;
+            if (p.unit_start) p.unit_start[li] = incl - units;
         }
-        p.live_expert[live_idx] = e;
-        p.live_start[live_idx] = less;
-        if (p.unit_start) p.unit_start[live_idx] = units;
-        atomicAdd(&n_live_s, 1);
-    }
-    // each row's place among its token's slots: ascending id, then slot; dropped rows last
-    if (j < n) {
-        const int K = p.top_k, t = j / K, k = j - t * K;
-        int pos = 0;
-        for (int q = 0; q < K; ++q) {
-            const int v = ids[t * K + q];
-            const bool before = (e >= 0) ? (v >= 0 && (v < e || (v == e && q < k)))
-                                         : (v >= 0 || q < k);
-            pos += before;
+        if (p.passes) {
+            // every position learns its run: the start (last first-flag at or before it)
+            const unsigned upto = fm & ((2u << lane) - 1u);
+            const int run_start = valid ? (31 - __clz(upto)) : 0;
+            const int rend = __shfl_sync(0xffffffffu, run_end, run_start);
+            const int ust = __shfl_sync(0xffffffffu, incl - units, run_start);
+            if (valid) file_pass_row(p, ek, run_start, rend - run_start, ust, lane, key & 1023);
         }
-        p.slot_order[t * K + pos] = e >= 0 ? j : -1;
+        const int n_live = __popc(fm), total_units = __shfl_sync(0xffffffffu, incl, 31);
+        if (lane == 0) {
+            p.live_start[n_live] = n_valid;
+            if (p.unit_start) p.unit_start[n_live] = total_units;
+            p.counters[0] = n_live;
+            p.counters[1] = n - n_valid;
+            p.counters[2] = 0;
+            p.counters[3] = 0;
+        }
+        write_slot_order(p, ids, lane, n);
+        return;
     }
-    __syncthreads();
-    if (j == 0) {
-        const int nl = n_live_s;
-        int rows = 0, units = 0;
-        const int tpu = p.tok_per_unit;
-        for (int i = 0; i < n; ++i)
-            if (ids[i] >= 0) {
-                ++rows;
-                if (tpu > 0 && first[i]) units += (cnt_of[i] + tpu - 1) / tpu;
+    // block-wide bitonic sort over the next power of two >= n
+    int N = 64;
+    while (N < n) N <<= 1;
+    for (int k = 2; k <= N; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= 32) {
+                keys[tid] = key;
+                __syncthreads();
+                const int other = keys[tid ^ j];
+                __syncthreads();
+                const bool up = (tid & k) == 0, lower = (tid & j) == 0;
+                key = (lower == up) ? min(key, other) : max(key, other);
+            } else {
+                key = warp_sort_step(key, tid, k, j);
             }
-        p.live_start[nl] = rows;
-        if (p.unit_start) p.unit_start[nl] = units;
-        p.counters[0] = nl;
-        p.counters[1] = dropped_s;
+        }
+    }
+    keys[tid] = key;
+    __syncthreads();
+    const bool valid = tid < N && key != kKeyNone;
+    const int ek = valid ? (key >> 10) : -1;
+    const bool first = valid && (tid == 0 || (keys[tid - 1] >> 10) != ek);
+    int n_live, n_valid;
+    const int li = block_exclusive_scan(first ? 1 : 0, scratch, &n_live);
+    block_exclusive_scan(valid ? 1 : 0, scratch, &n_valid);
+    if (valid) p.order[tid] = key & 1023;
+    if (first) {
+        p.live_expert[li] = ek;
+        ls[li] = tid;
+    }
+    if (tid == 0) ls[n_live] = n_valid;
+    __syncthreads();
+    const int units = (tid < n_live && tpu > 0) ? (ls[tid + 1] - ls[tid] + tpu - 1) / tpu : 0;
+    int total_units;
+    const int ustart = block_exclusive_scan(units, scratch, &total_units);
+    if (tid <= n_live) {
+        p.live_start[tid] = ls[tid];
+        if (p.unit_start) p.unit_start[tid] = tid < n_live ? ustart : total_units;
+    }
+    if (p.passes) {
+        keys[tid] = ustart;                       // keys[] is free now: per-live-expert first pass
+        __syncthreads();
+        const int run = li + (first ? 1 : 0) - 1; // this position's live index
+        if (valid) file_pass_row(p, ek, ls[run], ls[run + 1] - ls[run], keys[run], tid, key & 1023);
+    }
+    if (tid == 0) {
+        p.counters[0] = n_live;
+        p.counters[1] = n - n_valid;
         p.counters[2] = 0;
         p.counters[3] = 0;
     }
+    write_slot_order(p, ids, tid, n);
 }
 
 // Block 0: the plan.  Blocks >= 1: the activation permutation (x -> x_perm).
@@ -243,6 +316,22 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
             if (lane == __ffs(mask) - 1) my[ex] += __popc(mask);
         }
         __syncwarp();
+    }
+    // 3b. the pass table: each sorted position finds its live run by binary search
+    if (p.passes) {
+        __syncthreads();
+        __threadfence_block();
+        for (int64_t pos = threadIdx.x; pos < n_rows; pos += blockDim.x) {
+            int lo = 0, hi = n_live - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (p.live_start[mid] <= pos) lo = mid;
+                else hi = mid - 1;
+            }
+            const int ls0 = p.live_start[lo];
+            file_pass_row(p, p.live_expert[lo], ls0, p.live_start[lo + 1] - ls0, p.unit_start[lo],
+                          static_cast<int>(pos), p.order[pos]);
+        }
     }
     // 4. each token's slots in ascending expert id (stable by slot); dropped slots last as -1
     const int K = p.top_k;
