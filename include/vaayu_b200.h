@@ -232,6 +232,26 @@ int vy_moe_decode(const vy_moe_call* call, void* stream);
 int vy_moe_prefill(const vy_moe_call* call, void* stream);
 
 /*
+ * Bytes of the scratch array compiled into the library for vy_moe_decode_static.  Every GPU that
+ * loads the library holds this much device memory until the process exits.
+ */
+#define VY_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
+
+/*
+ * vy_moe_decode with no workspace from the caller and no allocation: the scratch is a fixed array
+ * of VY_DECODE_STATIC_SCRATCH_BYTES inside the library (call->workspace and workspace_bytes are
+ * ignored).  This entry point has no counterpart in the reference.  It is for hosts that cannot
+ * call cudaMalloc -- a binding that only receives pointers from a runtime owning all device
+ * memory, an engine whose memory plan has no room left, code that must not allocate while it runs
+ * -- and so cannot supply vy_moe_decode's workspace.  A call whose vy_moe_workspace_size (path 0)
+ * exceeds the array is rejected with VY_ERR_UNSUPPORTED.  The first call on each device looks the
+ * array's device address up (once, with that device current); make that first call before any
+ * stream capture.  All calls share the array: calls whose kernels overlap on the GPU race on it
+ * and must be ordered on one stream.  Results are bit-identical to vy_moe_decode's.
+ */
+int vy_moe_decode_static(const vy_moe_call* call, void* stream);
+
+/*
  * out[t] = sum of contrib[t * top_k + k] over the token's slots in ascending expert id, then
  * slot (fp32), for contributions gathered back from other ranks.  Replaces
  * vaayu/packed_expert_kernels.py:249-260 `_reduce_kernel` with the order

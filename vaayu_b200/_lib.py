@@ -56,6 +56,7 @@ SIGNATURES = {
     "vy_moe_route_permute": (ctypes.c_int, [P, I32T, I64T, I32T, I32T, P, P, P, P, P, P]),
     "vy_moe_workspace_size": (SZ, [ctypes.POINTER(MoeCall), I32T]),
     "vy_moe_decode": (ctypes.c_int, [ctypes.POINTER(MoeCall), P]),
+    "vy_moe_decode_static": (ctypes.c_int, [ctypes.POINTER(MoeCall), P]),
     "vy_moe_prefill": (ctypes.c_int, [ctypes.POINTER(MoeCall), P]),
     "vy_moe_combine": (ctypes.c_int, [P, P, I32T, I64T, I32T, I64T, P, I64T, P]),
 }
