@@ -1,17 +1,688 @@
-// vy_prefill.cu -- the tensor-core (tcgen05 / TMEM) grouped-GEMM expert layer for prefill.
+// vy_prefill.cu -- the prefill expert layer as tcgen05 grouped GEMMs (accumulators in TMEM).
+//
+//   plan (vy_route.cu)   rows grouped by expert; the pass table holds one entry per 128-row
+//                        M-tile of a live expert (stream pointers, first sorted row, row count)
+//   gather_kernel        x rows in sorted order -> x_sorted, 8-element groups permuted the way the
+//                        dequantised pairs come out (code j pairs with code j + 4), so A and B
+//                        share one consistent K order
+//   gemm_kernel<2>       h = act(act(silu(act(x Wg^T))) * act(x Wu^T)) per M-tile x 128 columns
+//   gemm_kernel<1>       c = act(h Wd^T) * w (one fp32 rounding), scattered to the row ids
+//   combine (vy_route)   each token's contributions in ascending expert id, then slot
+//
+// A GEMM CTA: 4 dequant warps + 1 control warp.  Each dequant thread owns one row of the 128-row
+// weight tile: it copies that row's packed codes into a private cp.async ring, dequantises them
+// (the reference's exact rounding of every weight: sub.rn then mul.rn on activation-dtype pairs)
+// and stores the 16-byte chunks into the weight tile in the 128-byte-swizzled K-major layout the
+// tensor core reads; then it arrives on the stage's barrier.  The control thread loads the
+// activation tile with TMA (same swizzle, no multicast) and issues tcgen05.mma (M=128, N=128,
+// K=16, fp32 accumulate in TMEM) once both halves of a stage are in; tcgen05.commit frees the
+// stage.  The epilogue warps read TMEM with tcgen05.ld.  Every barrier wait is bounded: on a
+// timeout the CTA records an error flag, drains what it issued, frees TMEM and returns.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "vy_moe.cuh"
 
 namespace vy {
-size_t prefill_workspace_bytes(const vy_moe_call* c) {
-    (void)c;
-    return 0;
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kStages = 3;        // shared-memory stages (activation tile + weight tiles)
+constexpr int kPack = 4;          // packed-code staging depth, private to each dequant thread
+constexpr int kDqThreads = 128;   // one per weight-tile row
+constexpr int kThreads = kDqThreads + 32;
+constexpr uint32_t kSpinLimit = 1u << 22;   // x ~0.5 us backoff: seconds before giving up
+constexpr int kTileBytes = kBM * kBK * 2;   // 16 KB: one 128 x 64 bf16 tile
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+
+// ── mbarrier / TMA / tcgen05 wrappers ───────────────────────────────────────────────────────
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait; false once the CTA has aborted or after kSpinLimit polls (then it aborts it).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int32_t* err) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (i > 32) __nanosleep(128);
+    }
+    *abort_flag = 1;
+    atomicOr(err, 4);
+    return false;
+}
+
+// Bounded wait that ignores the abort flag: used to drain work already issued (TMA loads,
+// MMAs) before the CTA frees its shared memory and TMEM.
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int32_t* err) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if (i > 32) __nanosleep(128);
+    }
+    atomicOr(err, 8);
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{ .reg .pred p; setp.ne.b32 p, %4, 0; tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// K-major, 128-byte swizzle, 128 rows x 64 bf16 per tile, rows 128 bytes apart, 8-row groups
+// 1024 bytes apart (SBO); LBO unused for swizzled K-major (1); version 1; layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+    const uint64_t addr = smem_u32(tile);
+    return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, A/B bf16 (1) or fp16 (0), both K-major,
+// N = kBN, M = kBM.
+template <int ACT>
+__host__ __device__ constexpr uint32_t idesc_f16() {
+    return (1u << 4) | (uint32_t(ACT == VY_BF16 ? 1 : 0) << 7) | (uint32_t(ACT == VY_BF16 ? 1 : 0) << 10) |
+           (uint32_t(kBN >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+}
+
+// ── the gather ──────────────────────────────────────────────────────────────────────────────
+
+struct GatherParams {
+    const void* x;
+    int64_t x_stride;
+    int hidden, top_k;
+    const int32_t* order;
+    const int32_t* live_start;   // live_start[n_live] = rows kept
+    const int32_t* counters;
+    uint16_t* x_sorted;          // [n, hidden], 8-element groups permuted
+};
+
+__global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
+    grid_dependency_wait();
+    const int n_rows = p.live_start[p.counters[0]];
+    const int groups = p.hidden / 8;
+    const int64_t total = int64_t(n_rows) * groups;
+    for (int64_t q = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; q < total; q += int64_t(gridDim.x) * blockDim.x) {
+        const int pos = static_cast<int>(q / groups), c = static_cast<int>(q - int64_t(pos) * groups) * 8;
+        const int row = p.order[pos];
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(p.x) + int64_t(row / p.top_k) * p.x_stride + c;
+        uint16_t v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = src[j];
+        uint4 o;
+        o.x = v[0] | (uint32_t(v[4]) << 16);
+        o.y = v[1] | (uint32_t(v[5]) << 16);
+        o.z = v[2] | (uint32_t(v[6]) << 16);
+        o.w = v[3] | (uint32_t(v[7]) << 16);
+        *reinterpret_cast<uint4*>(p.x_sorted + int64_t(pos) * p.hidden + c) = o;
+    }
+}
+
+// ── the GEMM ────────────────────────────────────────────────────────────────────────────────
+
+struct GemmParams {
+    int kdim;              // K of this GEMM (hidden for gate/up, inter for down)
+    int ndim;              // output features (inter for gate/up, hidden for down)
+    int gs_shift;
+    int top_k;
+    int64_t w_off[2], s_off[2], z_off[2];   // roles: gate, up (NMAT 2) or down (NMAT 1)
+    const PassEntry* passes;
+    const int32_t* unit_start;
+    int32_t* counters;     // [0] n_live, [2] error flags
+    const int32_t* order;
+    uint16_t* h_sorted;    // gate/up output [n, inter] (sorted rows, permuted groups)
+    uint16_t* h_out;       // optional natural-order h by row id
+    float* contrib;        // down output [rows, hidden] by row id
+    const void* weights;
+    int w_dtype;
+    bool w_round;
+    int64_t w_tok_stride, w_slot_stride;
+    const int32_t* w_index;
+};
+
+template <int NMAT>
+struct __align__(1024) GemmSmem {
+    uint16_t a[kStages][kBM * kBK];                 // activation tiles (TMA, swizzled)
+    uint16_t b[kStages][NMAT][kBN * kBK];           // weight tiles (dequantised, swizzled)
+    uint4 pack[kPack][NMAT * 2][kDqThreads];        // packed codes, private per thread
+    uint64_t full_a[kStages], full_b[kStages], empty[kStages], done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+template <int ACT, int SC, bool ZERO, int NMAT>
+__global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, GemmParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    GemmSmem<NMAT>& S = *reinterpret_cast<GemmSmem<NMAT>*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    grid_dependency_wait();
+    const int n_live = p.counters[0];
+    const int n_tiles = n_live > 0 ? p.unit_start[n_live] : 0;
+    if (static_cast<int>(blockIdx.x) >= n_tiles) return;     // uniform: before any barrier
+    const PassEntry pe = p.passes[blockIdx.x];
+    const int n0 = blockIdx.y * kBN;
+    const int nk = p.kdim / kBK;
+    constexpr uint32_t kTmemCols = NMAT == 2 ? 256 : 128;
+
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&S.full_a[i], 1);
+            mbar_init(&S.full_b[i], kDqThreads);
+            mbar_init(&S.empty[i], 1);
+        }
+        mbar_init(&S.done, 1);
+        S.abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) tmem_alloc(&S.tmem_base, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = S.tmem_base;
+    volatile int* abort_flag = &S.abort_flag;
+    int32_t* err = p.counters + 2;
+    const bool ok_ptrs = pe.pk != 0 && pe.sc != 0 && (pe.pk & 15) == 0;
+    if (!ok_ptrs && tid == 0) atomicOr(err, 1);
+
+    if (tid < kDqThreads) {
+        // ── dequant producer: weight-tile row `tid` of every matrix ─────────────────────────
+        const int r = tid;
+        const int wpr = p.kdim / 8;
+        const int groups = p.kdim >> p.gs_shift;
+        const int32_t* src[NMAT];
+        int sbase[NMAT], zbase[NMAT];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) {
+            src[m] = reinterpret_cast<const int32_t*>(pe.pk) + p.w_off[m] + int64_t(n0 + r) * wpr;
+            sbase[m] = static_cast<int>(p.s_off[m]) + (n0 + r) * groups;
+            zbase[m] = static_cast<int>(p.z_off[m]) + ((n0 + r) >> 3) * groups;
+        }
+        const void* sc = reinterpret_cast<const void*>(pe.sc);
+        const int32_t* zp = reinterpret_cast<const int32_t*>(pe.zp);
+        auto issue = [&](int s) {
+            if (s < nk && ok_ptrs) {
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    cp_async16(&S.pack[s % kPack][2 * m][r], src[m] + s * 8);
+                    cp_async16(&S.pack[s % kPack][2 * m + 1][r], src[m] + s * 8 + 4);
+                }
+            }
+            cp_async_commit();
+        };
+#pragma unroll
+        for (int s = 0; s < kPack - 1; ++s) issue(s);
+        for (int s = 0; s < nk; ++s) {
+            issue(s + kPack - 1);
+            cp_async_wait<kPack - 1>();
+            const int slot = s % kStages;
+            if (s >= kStages && !mbar_wait(&S.empty[slot], ((s / kStages) - 1) & 1, abort_flag, err)) break;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const uint4 lo = S.pack[s % kPack][2 * m][r], hi = S.pack[s % kPack][2 * m + 1][r];
+                const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                unsigned char* row_base = reinterpret_cast<unsigned char*>(S.b[slot][m]) + r * 128;
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    const int grp = (s * kBK + w * 8) >> p.gs_shift;
+                    uint32_t sb;
+                    if constexpr (SC == ACT) sb = __ldg(reinterpret_cast<const unsigned short*>(sc) + sbase[m] + grp);
+                    else sb = act_bits<ACT>(load_scale<SC>(sc, sbase[m] + grp));
+                    const uint32_t spair = __byte_perm(sb, 0, 0x1010);
+                    uint32_t bpair;
+                    if constexpr (ZERO) {
+                        const uint32_t zw = static_cast<uint32_t>(__ldg(zp + zbase[m] + grp));
+                        bpair = int4_bias_pair<ACT>((zw >> (4 * ((n0 + r) & 7))) & 15u);
+                    } else {
+                        bpair = int4_bias_pair<ACT>(8u);
+                    }
+                    uint4 o;
+                    o.x = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 0), bpair), spair);
+                    o.y = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 1), bpair), spair);
+                    o.z = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 2), bpair), spair);
+                    o.w = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 3), bpair), spair);
+                    *reinterpret_cast<uint4*>(row_base + ((w ^ (r & 7)) << 4)) = o;
+                }
+            }
+            fence_async_smem();
+            mbar_arrive(&S.full_b[slot]);
+        }
+        cp_async_wait<0>();
+    } else if (warp == kDqThreads / 32 && lane == 0) {
+        // ── control: activation tiles by TMA, tcgen05.mma, commits ─────────────────────────
+        constexpr uint32_t idesc = idesc_f16<ACT>();
+        int loaded = 0, landed = 0;   // activation tiles issued / seen complete
+        for (; loaded < kStages - 1 && loaded < nk; ++loaded) {
+            mbar_expect_tx(&S.full_a[loaded], kTileBytes);
+            tma_load_2d(S.a[loaded], &tmap_a, loaded * kBK, pe.row0, &S.full_a[loaded]);
+        }
+        for (int s = 0; s < nk; ++s) {
+            const int t = s + kStages - 1;
+            if (t < nk) {
+                const int ts = t % kStages;
+                if (t >= kStages && !mbar_wait(&S.empty[ts], ((t / kStages) - 1) & 1, abort_flag, err)) break;
+                mbar_expect_tx(&S.full_a[ts], kTileBytes);
+                tma_load_2d(S.a[ts], &tmap_a, t * kBK, pe.row0, &S.full_a[ts]);
+                loaded = t + 1;
+            }
+            const int slot = s % kStages;
+            const uint32_t par = (s / kStages) & 1;
+            if (!mbar_wait(&S.full_a[slot], par, abort_flag, err)) break;
+            landed = s + 1;
+            if (!mbar_wait(&S.full_b[slot], par, abort_flag, err)) break;
+            tc_fence_after();
+            const uint64_t ad = sw128_desc(S.a[slot]);
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const uint64_t bd = sw128_desc(S.b[slot][m]);
+#pragma unroll
+                for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
+                    umma(tmem + m * kBN, ad + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
+            }
+            umma_commit(&S.empty[slot]);
+        }
+        umma_commit(&S.done);   // arrives once every MMA issued so far has completed
+        // aborted: the activation tiles still in flight must land before shared memory is released
+        for (int t = landed; t < loaded; ++t)
+            if (!mbar_drain(&S.full_a[t % kStages], (t / kStages) & 1, err)) break;
+    }
+
+    // ── epilogue: TMEM -> registers -> global ───────────────────────────────────────────────
+    if (tid < kDqThreads) {
+        // every MMA must be complete before TMEM is read or freed, on the abort path too
+        const bool finished = mbar_drain(&S.done, 0, err) && !*abort_flag && ok_ptrs;
+        __syncwarp();
+        tc_fence_after();
+        const int m_row = tid;                            // TMEM lane = tile row
+        const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
+        const bool live = m_row < pe.ncols;
+        const int pos = pe.row0 + m_row;
+        if (NMAT == 2) {
+#pragma unroll 1
+            for (int c = 0; c < kBN; c += 16) {
+                uint32_t gr[16], ur[16];
+                tmem_ld16(lane_addr + c, gr);
+                tmem_ld16(lane_addr + kBN + c, ur);
+                if (finished && live) {
+                    uint32_t hb[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float gv = round_act<ACT>(__uint_as_float(gr[j]));
+                        const float uv = round_act<ACT>(__uint_as_float(ur[j]));
+                        const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
+                        hb[j] = act_bits<ACT>(__fmul_rn(av, uv));
+                    }
+                    // columns n0+c .. +16 are two 8-element groups; store them permuted
+                    uint4 o0, o1;
+                    o0.x = hb[0] | (hb[4] << 16);
+                    o0.y = hb[1] | (hb[5] << 16);
+                    o0.z = hb[2] | (hb[6] << 16);
+                    o0.w = hb[3] | (hb[7] << 16);
+                    o1.x = hb[8] | (hb[12] << 16);
+                    o1.y = hb[9] | (hb[13] << 16);
+                    o1.z = hb[10] | (hb[14] << 16);
+                    o1.w = hb[11] | (hb[15] << 16);
+                    uint4* dst = reinterpret_cast<uint4*>(p.h_sorted + int64_t(pos) * p.ndim + n0 + c);
+                    dst[0] = o0;
+                    dst[1] = o1;
+                    if (p.h_out) {
+                        const int rowid = p.order[pos];
+                        for (int j = 0; j < 16; ++j)
+                            p.h_out[int64_t(rowid) * p.ndim + n0 + c + j] = static_cast<uint16_t>(hb[j]);
+                    }
+                }
+            }
+        } else {
+            const int rowid = live ? p.order[pos] : 0;
+            float wv = 0.f;
+            if (finished && live) {
+                const int64_t t = rowid / p.top_k;
+                const int k = rowid - int(t) * p.top_k;
+                const int widx = p.w_index ? p.w_index[rowid] : k;
+                wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
+            }
+#pragma unroll 1
+            for (int c = 0; c < kBN; c += 16) {
+                uint32_t yr[16];
+                tmem_ld16(lane_addr + c, yr);
+                if (finished && live) {
+                    float4 o[4];
+                    float* of = reinterpret_cast<float*>(o);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        float cv = __fmul_rn(round_act<ACT>(__uint_as_float(yr[j])), wv);
+                        if (p.w_round) cv = round_act<ACT>(cv);
+                        of[j] = cv;
+                    }
+                    float4* dst = reinterpret_cast<float4*>(p.contrib + int64_t(rowid) * p.ndim + n0 + c);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) dst[q] = o[q];
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// out[t] = token t's contributions in the plan's slot order (ascending expert id, then slot;
+// dropped rows are -1 and add nothing), fp32.
+__global__ void __launch_bounds__(256) slot_combine_kernel(const float* __restrict__ contrib,
+                                                           const int32_t* __restrict__ slot_order,
+                                                           int64_t n_tokens, int top_k, int hidden,
+                                                           float* out, int64_t out_stride) {
+    grid_dependency_wait();
+    for (int64_t t = blockIdx.y; t < n_tokens; t += gridDim.y)
+    for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < hidden; c += gridDim.x * blockDim.x * 4) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < top_k; ++k) {
+            const int row = slot_order[t * top_k + k];
+            if (row < 0) continue;
+            const float4 v = *reinterpret_cast<const float4*>(contrib + int64_t(row) * hidden + c);
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
+        }
+        float* o = out + t * out_stride + c;
+        o[0] = a.x;
+        o[1] = a.y;
+        o[2] = a.z;
+        o[3] = a.w;
+    }
+}
+
+// ── host ────────────────────────────────────────────────────────────────────────────────────
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn(int* status) {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    *status = fn ? VY_OK : fail(VY_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    return fn;
+}
+
+// A [rows, cols] 16-bit matrix as 128 x 64 tiles with the 128-byte swizzle.
+int make_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int act) {
+    int st;
+    EncodeTiledFn fn = encode_fn(&st);
+    if (!fn) return st;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+    const cuuint32_t box[2] = {kBK, kBM};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, act == VY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                    const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(VY_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return VY_OK;
+}
+
+struct PrefillLayout {
+    int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters;
+    PassEntry* passes;
+    uint16_t *x_sorted, *h_sorted;
+    float* contrib;
+    size_t bytes;
+    int64_t max_tiles;
+};
+
+PrefillLayout prefill_layout(const vy_moe_call* c, void* base) {
+    const int64_t n = c->n_tokens * c->top_k, E = c->n_experts;
+    const int64_t H = c->geom->hidden, I = c->geom->inter;
+    Carve cv{static_cast<char*>(base), 0};
+    PrefillLayout L{};
+    L.order = cv.take<int32_t>(n);
+    L.live_expert = cv.take<int32_t>(E);
+    L.live_start = cv.take<int32_t>(E + 1);
+    L.unit_start = cv.take<int32_t>(E + 1);
+    L.slot_order = cv.take<int32_t>(n);
+    L.counters = cv.take<int32_t>(4);
+    L.max_tiles = n / kBM + (n < E ? n : E) + 1;
+    L.passes = cv.take<PassEntry>(L.max_tiles);
+    L.x_sorted = cv.take<uint16_t>(n * H);
+    L.h_sorted = cv.take<uint16_t>(n * I);
+    L.contrib = c->contrib ? nullptr : cv.take<float>(n * H);
+    L.bytes = cv.used;
+    return L;
+}
+
+template <int ACT, int SC, bool ZERO, int NMAT>
+int launch_gemm(const CUtensorMap& map, const GemmParams& gp, int max_tiles, cudaStream_t s) {
+    auto kern = gemm_kernel<ACT, SC, ZERO, NMAT>;
+    const size_t smem = sizeof(GemmSmem<NMAT>) + 1024;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "prefill GEMM shared memory: %s", cudaGetErrorString(e));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(max_tiles), static_cast<unsigned>(gp.ndim / kBN));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, map, gp);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "prefill GEMM launch: %s", cudaGetErrorString(e));
+    return VY_OK;
+}
+
+template <int ACT, int SC, bool ZERO>
+int run_prefill_gemms(const CUtensorMap& ma, const GemmParams& g1, const CUtensorMap& mh, const GemmParams& g2,
+                      int max_tiles, cudaStream_t s) {
+    int st = launch_gemm<ACT, SC, ZERO, 2>(ma, g1, max_tiles, s);
+    if (st != VY_OK) return st;
+    return launch_gemm<ACT, SC, ZERO, 1>(mh, g2, max_tiles, s);
+}
+
+template <int ACT>
+int dispatch_prefill(int sc, bool zero, const CUtensorMap& ma, const GemmParams& g1, const CUtensorMap& mh,
+                     const GemmParams& g2, int max_tiles, cudaStream_t s) {
+#define VY_PF(SCV)                                                                                \
+    return zero ? run_prefill_gemms<ACT, SCV, true>(ma, g1, mh, g2, max_tiles, s)                 \
+                : run_prefill_gemms<ACT, SCV, false>(ma, g1, mh, g2, max_tiles, s);
+    switch (sc) {
+        case VY_BF16: VY_PF(VY_BF16)
+        case VY_F16: VY_PF(VY_F16)
+        default: VY_PF(VY_F32)
+    }
+#undef VY_PF
+}
+
+}  // namespace
+
+size_t prefill_workspace_bytes(const vy_moe_call* c) {
+    if (!c || !c->geom) return 0;
+    return prefill_layout(c, nullptr).bytes + 1024;
+}
+
 }  // namespace vy
 
 using namespace vy;
 
 extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
-    (void)c;
-    (void)stream;
-    return fail(VY_ERR_UNSUPPORTED, "vy_moe_prefill: not built yet");
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if ((st = validate_call(c)) != VY_OK) return st;
+    if (c->n_tokens == 0) return ok();
+    const vy_expert_geom& g = *c->geom;
+    if (g.group_size < 8 || g.hidden % kBN || g.inter % kBN)
+        return fail(VY_ERR_UNSUPPORTED, "prefill tiles need hidden / intermediate multiples of %d", kBN);
+    PrefillLayout L = prefill_layout(c, nullptr);
+    if (!c->workspace || c->workspace_bytes < L.bytes + 1024)
+        return fail(VY_ERR_WORKSPACE, "workspace %zu bytes, %zu needed", c->workspace_bytes, L.bytes + 1024);
+    char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 1023) & ~uintptr_t(1023));
+    L = prefill_layout(c, base);
+    cudaStream_t s = as_stream(stream);
+    const int64_t n = c->n_tokens * c->top_k;
+    int gs_shift = 0;
+    while ((1 << gs_shift) < g.group_size) ++gs_shift;
+
+    PlanArgs pa{};
+    pa.ids = c->expert_ids;
+    pa.ids64 = c->ids_dtype == VY_I64;
+    pa.n_tokens = c->n_tokens;
+    pa.top_k = c->top_k;
+    pa.n_experts = c->n_experts;
+    pa.order = L.order;
+    pa.live_expert = L.live_expert;
+    pa.live_start = L.live_start;
+    pa.unit_start = L.unit_start;
+    pa.slot_order = L.slot_order;
+    pa.counters = L.counters;
+    pa.tok_per_unit = kBM;
+    pa.expert_table = c->expert_table;
+    pa.passes = L.passes;
+    if ((st = launch_plan(pa, dev->sm_count, s)) != VY_OK) return st;
+
+    GatherParams gp{c->x, c->x_row_stride, g.hidden, c->top_k, L.order, L.live_start, L.counters, L.x_sorted};
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>(dev->sm_count * 4));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, gather_kernel, gp);
+        if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gather launch: %s", cudaGetErrorString(e));
+    }
+
+    CUtensorMap map_x, map_h;
+    if ((st = make_tile_map(&map_x, L.x_sorted, n, g.hidden, c->act_dtype)) != VY_OK) return st;
+    if ((st = make_tile_map(&map_h, L.h_sorted, n, g.inter, c->act_dtype)) != VY_OK) return st;
+
+    GemmParams g1{};
+    g1.kdim = g.hidden;
+    g1.ndim = g.inter;
+    g1.gs_shift = gs_shift;
+    g1.top_k = c->top_k;
+    g1.w_off[0] = g.word_off[0];
+    g1.w_off[1] = g.word_off[1];
+    g1.s_off[0] = g.scale_off[0];
+    g1.s_off[1] = g.scale_off[1];
+    g1.z_off[0] = g.zero_off[0];
+    g1.z_off[1] = g.zero_off[1];
+    g1.passes = L.passes;
+    g1.unit_start = L.unit_start;
+    g1.counters = L.counters;
+    g1.order = L.order;
+    g1.h_sorted = L.h_sorted;
+    g1.h_out = static_cast<uint16_t*>(c->h_out);
+
+    GemmParams g2 = g1;
+    g2.kdim = g.inter;
+    g2.ndim = g.hidden;
+    g2.w_off[0] = g.word_off[2];
+    g2.s_off[0] = g.scale_off[2];
+    g2.z_off[0] = g.zero_off[2];
+    g2.h_sorted = nullptr;
+    g2.h_out = nullptr;
+    g2.contrib = c->contrib ? c->contrib : L.contrib;
+    g2.weights = c->weights;
+    g2.w_dtype = c->w_dtype;
+    g2.w_round = c->w_dtype == c->act_dtype;
+    g2.w_tok_stride = c->w_tok_stride;
+    g2.w_slot_stride = c->w_slot_stride;
+    g2.w_index = c->w_index;
+
+    const int max_tiles = static_cast<int>(L.max_tiles);
+    const bool zero = g.has_zero != 0;
+    st = c->act_dtype == VY_BF16
+             ? dispatch_prefill<VY_BF16>(g.scale_dtype, zero, map_x, g1, map_h, g2, max_tiles, s)
+             : dispatch_prefill<VY_F16>(g.scale_dtype, zero, map_x, g1, map_h, g2, max_tiles, s);
+    if (st != VY_OK) return st;
+    if (c->contrib) return check_launch("vy_moe_prefill");
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(static_cast<unsigned>((g.hidden / 4 + 255) / 256),
+                           static_cast<unsigned>(c->n_tokens < 65535 ? c->n_tokens : 65535));
+        cfg.blockDim = dim3(256);
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, slot_combine_kernel, static_cast<const float*>(L.contrib),
+                                           static_cast<const int32_t*>(L.slot_order), c->n_tokens, c->top_k,
+                                           g.hidden, c->out, c->out_row_stride);
+        if (e != cudaSuccess) return fail(VY_ERR_CUDA, "combine launch: %s", cudaGetErrorString(e));
+    }
+    return check_launch("vy_moe_prefill");
 }

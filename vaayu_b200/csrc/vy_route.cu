@@ -81,7 +81,7 @@ __device__ __forceinline__ void file_pass_row(const PlanArgs& p, int e, int ls, 
     if (!p.passes) return;
     const int tpu = p.tok_per_unit, r = pos - ls, q = r / tpu, col = r - q * tpu;
     PassEntry& pe = p.passes[ustart + q];
-    pe.rows[col] = row;
+    if (col < kMaxPassCols) pe.rows[col] = row;   // row ids are kept for GEMV-sized passes only
     if (col == 0) {
         pe.pk = p.expert_table[3 * e];
         pe.sc = p.expert_table[3 * e + 1];
