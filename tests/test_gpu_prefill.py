@@ -215,3 +215,70 @@ def test_back_to_back_calls_do_not_share_a_table():
     torch.cuda.synchronize()
     for (x, eidx, w, blobs), out in zip(cases, outs):
         assert torch.equal(out, _launch(x, eidx, w, blobs))
+
+
+# ── the resident-table path (device routing) at prefill sizes, every dtype / zero-point form ──
+
+def _table_case(hid=1024, inter=512, gs=128, n_exp=8, top_k=4, tokens=300, seed=0, zeros=False,
+                act=BF, scale_dtype=None, w_dtype=torch.float32):
+    blobs = T.make_blobs(hid, inter, n_exp, gs=gs, seed=seed + 300, zeros=zeros, scale_dtype=scale_dtype)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(tokens, hid, generator=g).to(act).cuda()
+    logits = torch.randn(tokens, n_exp, generator=g) + torch.linspace(0, 1.5, n_exp)
+    w, idx = torch.topk(logits.softmax(-1), top_k, -1)
+    w = (w / w.sum(-1, keepdim=True)).to(w_dtype).cuda()
+    return blobs, x, idx.cuda(), w
+
+
+FORMS = [pytest.param(dict(), id="bf16-fp16scale-g128"),
+         pytest.param(dict(zeros=True), id="zero-points-g128"),
+         pytest.param(dict(zeros=True, gs=32), id="zero-points-g32"),
+         pytest.param(dict(act=torch.float16, gs=64, w_dtype=torch.float16), id="fp16-act-g64"),
+         pytest.param(dict(scale_dtype=torch.float32, gs=32), id="fp32-scale-g32"),
+         pytest.param(dict(scale_dtype=torch.bfloat16), id="bf16-scale-g128"),
+         pytest.param(dict(hid=1152, inter=384, gs=64), id="hidden-1152-tail-block")]
+
+
+@pytest.mark.parametrize("kw", FORMS)
+def test_resident_table_prefill_matches_the_oracle(kw):
+    """300 tokens x 1024 outputs.  The tensor cores accumulate each output over the whole K in
+    one fp32 chain (as the reference's own GPU kernels do), so among ~600k rounding points of h a
+    few hundred land on the other side of a bf16 boundary than the oracle's double-accumulated
+    dot; the max-abs bar at this size is therefore taken against the fp64 truth: no worse than
+    the oracle's own error (rel-L2 within 5%, max-abs within 10%)."""
+    blobs, x, idx, w = _table_case(**kw)
+    got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=pk._prefill_path()).cpu().numpy()
+    ref = T.oracle_layer(blobs, x, idx, w)
+    assert T.rel_l2(got, ref) <= 1e-3
+    assert T.max_abs_over_rms(got, ref) <= 4e-2
+    truth = T.fp64_layer(blobs, x, idx, w)
+    assert T.rel_l2(got, truth) <= 1.05 * T.rel_l2(ref, truth) + 1e-12
+    assert T.max_abs_over_rms(got, truth) <= 1.1 * T.max_abs_over_rms(ref, truth)
+
+
+@pytest.mark.parametrize("kw", FORMS[:3])
+def test_resident_table_prefill_h_stage_is_correctly_rounded(kw):
+    blobs, x, idx, w = _table_case(**kw)
+    inter = kw.get("inter", 512)
+    h = torch.empty(idx.numel(), inter, dtype=x.dtype, device="cuda")
+    c = torch.empty(idx.numel(), x.shape[1], device="cuda")
+    vb.moe_forward(x, idx, torch.ones_like(w), pk.ExpertTable(blobs), path=pk._prefill_path(), h_out=h,
+                   contrib=c)
+    _o, h_ref = T.oracle_layer(blobs, x, idx, torch.ones_like(w), want_h=True)
+    assert (T.to_np(h) == h_ref).mean() >= 0.99
+
+
+def test_one_expert_taking_every_row_runs_several_tiles():
+    """600 tokens x top-2 on experts 0 and 1 only: 600 rows each, five 128-row tiles per expert."""
+    blobs, x, idx, w = _table_case(tokens=600, top_k=2, seed=5)
+    idx = torch.tensor([0, 1], device="cuda").repeat(600, 1)
+    got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=pk._prefill_path()).cpu().numpy()
+    assert T.rel_l2(got, T.oracle_layer(blobs, x, idx, w)) <= 1e-3
+
+
+def test_prefill_and_the_gemv_path_agree():
+    blobs, x, idx, w = _table_case(tokens=200, seed=6)
+    table = pk.ExpertTable(blobs)
+    a = vb.moe_forward(x, idx, w, table, path=pk._prefill_path()).cpu().numpy()
+    b = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE).cpu().numpy()
+    assert T.rel_l2(a, b) <= 1e-3 and T.max_abs_over_rms(a, b) <= 2e-2

@@ -27,13 +27,15 @@
 namespace vy {
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 64;
-constexpr int kStages = 3;        // shared-memory stages (activation tile + weight tiles)
-constexpr int kPack = 4;          // packed-code staging depth, private to each dequant thread
-constexpr int kDqThreads = 128;   // one per weight-tile row
+constexpr int kBM = 128, kBK = 64;
+constexpr int kBlk = 128;             // rows of one weight block
+constexpr int kBN = 2 * kBlk;         // a CTA's N: two weight blocks (gate + up, or 256 down rows)
+constexpr int kStages = 3;            // shared-memory stages (activation tile + weight tile)
+constexpr int kPack = 4;              // packed-code staging depth, private to each dequant thread
+constexpr int kDqThreads = 2 * kBlk;  // one per weight-tile row
 constexpr int kThreads = kDqThreads + 32;
-constexpr uint32_t kSpinLimit = 1u << 22;   // x ~0.5 us backoff: seconds before giving up
-constexpr int kTileBytes = kBM * kBK * 2;   // 16 KB: one 128 x 64 bf16 tile
+constexpr uint64_t kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
+constexpr int kTileBytes = kBM * kBK * 2;     // 16 KB: one 128 x 64 activation tile
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -60,28 +62,44 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait; false once the CTA has aborted or after kSpinLimit polls (then it aborts it).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int32_t* err) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
-        if (mbar_try(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (i > 32) __nanosleep(128);
-    }
-    *abort_flag = 1;
-    atomicOr(err, 4);
-    return false;
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
-// Bounded wait that ignores the abort flag: used to drain work already issued (TMA loads,
-// MMAs) before the CTA frees its shared memory and TMEM.
-__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int32_t* err) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+// Bounded wait (try_wait suspends in hardware between polls); false once the CTA has aborted, or
+// after kWaitNs, when it aborts the CTA itself (error bit 4).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int32_t* err) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (;;) {
         if (mbar_try(bar, parity)) return true;
-        if (i > 32) __nanosleep(128);
+        if (*abort_flag) return false;
+        if (now_ns() - t0 > kWaitNs) {
+            *abort_flag = 1;
+            atomicOr(err, 4);
+            return false;
+        }
     }
-    atomicOr(err, 8);
-    return false;
+}
+
+// Bounded wait that ignores the abort flag: drains work already issued (TMA loads, MMAs) before
+// the CTA releases its shared memory and TMEM (error bit 8 if even that times out).
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int32_t* err) {
+    const uint64_t t0 = now_ns();
+    for (;;) {
+        if (mbar_try(bar, parity)) return true;
+        if (now_ns() - t0 > kWaitNs) {
+            atomicOr(err, 8);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -123,8 +141,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// K-major, 128-byte swizzle, 128 rows x 64 bf16 per tile, rows 128 bytes apart, 8-row groups
-// 1024 bytes apart (SBO); LBO unused for swizzled K-major (1); version 1; layout SWIZZLE_128B.
+// K-major, 128-byte swizzle, 64 bf16 per row, rows 128 bytes apart, 8-row groups 1024 bytes
+// apart (SBO); LBO unused for swizzled K-major (1); version 1; layout SWIZZLE_128B.
 __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
     const uint64_t addr = smem_u32(tile);
     return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | (uint64_t(1024 >> 4) << 32) | (1ull << 46) |
@@ -179,7 +197,7 @@ struct GemmParams {
     int ndim;              // output features (inter for gate/up, hidden for down)
     int gs_shift;
     int top_k;
-    int64_t w_off[2], s_off[2], z_off[2];   // roles: gate, up (NMAT 2) or down (NMAT 1)
+    int64_t w_off[2], s_off[2], z_off[2];   // roles: gate, up (KIND 0) or down (KIND 1, [0])
     const PassEntry* passes;
     const int32_t* unit_start;
     int32_t* counters;     // [0] n_live, [2] error flags
@@ -194,21 +212,41 @@ struct GemmParams {
     const int32_t* w_index;
 };
 
-template <int NMAT>
 struct __align__(1024) GemmSmem {
-    uint16_t a[kStages][kBM * kBK];                 // activation tiles (TMA, swizzled)
-    uint16_t b[kStages][NMAT][kBN * kBK];           // weight tiles (dequantised, swizzled)
-    uint4 pack[kPack][NMAT * 2][kDqThreads];        // packed codes, private per thread
+    uint16_t a[kStages][kBM * kBK];            // activation tiles (TMA, swizzled)
+    uint16_t b[kStages][kBN * kBK];            // weight tiles: rows 0-127 block 0, 128-255 block 1
+    uint4 pack[kPack][2][kDqThreads];          // packed codes, private per thread
+    uint2 sz[kPack][2][kDqThreads];            // the 8-byte words holding a stage's scale / zero word
     uint64_t full_a[kStages], full_b[kStages], empty[kStages], done;
     uint32_t tmem_base;
     int abort_flag;
 };
 
-template <int ACT, int SC, bool ZERO, int NMAT>
+// The activation-dtype bits of scale element `sub` of an 8-byte scale word.
+template <int ACT, int SC>
+__device__ __forceinline__ uint32_t scale_bits(uint2 v, int sub) {
+    if constexpr (SC == VY_F32) {
+        return act_bits<ACT>(__uint_as_float(sub ? v.y : v.x));
+    } else {
+        const uint32_t w = (sub & 2) ? v.y : v.x;
+        const uint32_t b16 = (sub & 1) ? (w >> 16) : (w & 0xFFFFu);
+        if constexpr (SC == ACT) {
+            return b16;
+        } else if constexpr (SC == VY_F16) {
+            return act_bits<ACT>(__half2float(__ushort_as_half(static_cast<unsigned short>(b16))));
+        } else {
+            return act_bits<ACT>(__bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(b16))));
+        }
+    }
+}
+
+// KIND 0: gate and up blocks of the same 128 intermediate rows; the epilogue writes
+//         h = act(act(silu(g)) * u).
+// KIND 1: two 128-row blocks of down; the epilogue writes contributions act(y) * w by row id.
+template <int ACT, int SC, bool ZERO, int KIND>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, GemmParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    GemmSmem<NMAT>& S = *reinterpret_cast<GemmSmem<NMAT>*>(
-        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    GemmSmem& S = *reinterpret_cast<GemmSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     grid_dependency_wait();
@@ -216,9 +254,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int n_tiles = n_live > 0 ? p.unit_start[n_live] : 0;
     if (static_cast<int>(blockIdx.x) >= n_tiles) return;     // uniform: before any barrier
     const PassEntry pe = p.passes[blockIdx.x];
-    const int n0 = blockIdx.y * kBN;
+    const int nbase = blockIdx.y * (KIND == 0 ? kBlk : kBN);
     const int nk = p.kdim / kBK;
-    constexpr uint32_t kTmemCols = NMAT == 2 ? 256 : 128;
+    constexpr uint32_t kTmemCols = kBN;
 
     if (tid == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -237,34 +275,41 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const uint32_t tmem = S.tmem_base;
     volatile int* abort_flag = &S.abort_flag;
     int32_t* err = p.counters + 2;
-    const bool ok_ptrs = pe.pk != 0 && pe.sc != 0 && (pe.pk & 15) == 0;
+    // stream bases: packed codes 16-byte aligned, scale / zero streams 8-byte aligned
+    const bool ok_ptrs = pe.pk != 0 && pe.sc != 0 && (pe.pk & 15) == 0 && (pe.sc & 7) == 0 &&
+                         (!ZERO || (pe.zp != 0 && (pe.zp & 7) == 0));
     if (!ok_ptrs && tid == 0) atomicOr(err, 1);
 
     if (tid < kDqThreads) {
-        // ── dequant producer: weight-tile row `tid` of every matrix ─────────────────────────
-        const int r = tid;
+        // ── dequant producer: weight-tile row `tid` ─────────────────────────────────────────
+        const int blk = tid >> 7, r = tid & (kBlk - 1);
+        const int m = KIND == 0 ? blk : 0;
+        const int row = KIND == 0 ? nbase + r : nbase + blk * kBlk + r;
+        const bool go = ok_ptrs && row < p.ndim;
         const int wpr = p.kdim / 8;
         const int groups = p.kdim >> p.gs_shift;
-        const int32_t* src[NMAT];
-        int sbase[NMAT], zbase[NMAT];
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) {
-            src[m] = reinterpret_cast<const int32_t*>(pe.pk) + p.w_off[m] + int64_t(n0 + r) * wpr;
-            sbase[m] = static_cast<int>(p.s_off[m]) + (n0 + r) * groups;
-            zbase[m] = static_cast<int>(p.z_off[m]) + ((n0 + r) >> 3) * groups;
-        }
-        const void* sc = reinterpret_cast<const void*>(pe.sc);
-        const int32_t* zp = reinterpret_cast<const int32_t*>(pe.zp);
+        const int32_t* src = reinterpret_cast<const int32_t*>(pe.pk) + p.w_off[m] + int64_t(row) * wpr;
+        const int64_t sidx0 = p.s_off[m] + int64_t(row) * groups;
+        const int64_t zidx0 = p.z_off[m] + int64_t(row >> 3) * groups;
+        const unsigned char* sc_bytes = reinterpret_cast<const unsigned char*>(pe.sc);
+        const unsigned char* zp_bytes = reinterpret_cast<const unsigned char*>(pe.zp);
+        constexpr int kScBytes = SC == VY_F32 ? 4 : 2;
+        // the scale / zero element of stage s sits in the 8-byte word that contains it; streams
+        // hold a multiple of 4 (16-bit) or 2 (32-bit) elements, so that word is inside the stream
         auto issue = [&](int s) {
-            if (s < nk && ok_ptrs) {
-#pragma unroll
-                for (int m = 0; m < NMAT; ++m) {
-                    cp_async16(&S.pack[s % kPack][2 * m][r], src[m] + s * 8);
-                    cp_async16(&S.pack[s % kPack][2 * m + 1][r], src[m] + s * 8 + 4);
-                }
+            if (s < nk && go) {
+                cp_async16(&S.pack[s % kPack][0][tid], src + s * 8);
+                cp_async16(&S.pack[s % kPack][1][tid], src + s * 8 + 4);
+                const int64_t grp = (int64_t(s) * kBK) >> p.gs_shift;
+                cp_async8(&S.sz[s % kPack][0][tid], sc_bytes + (((sidx0 + grp) * kScBytes) & ~int64_t(7)));
+                if constexpr (ZERO)
+                    cp_async8(&S.sz[s % kPack][1][tid], zp_bytes + (((zidx0 + grp) * 4) & ~int64_t(7)));
             }
             cp_async_commit();
         };
+        const bool two_groups = p.gs_shift == 5;   // group 32: a 64-wide stage spans two groups
+        constexpr int kSubMask = SC == VY_F32 ? 1 : 3;
+        unsigned char* row_base = reinterpret_cast<unsigned char*>(S.b[0]) + tid * 128;
 #pragma unroll
         for (int s = 0; s < kPack - 1; ++s) issue(s);
         for (int s = 0; s < nk; ++s) {
@@ -272,39 +317,39 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             cp_async_wait<kPack - 1>();
             const int slot = s % kStages;
             if (s >= kStages && !mbar_wait(&S.empty[slot], ((s / kStages) - 1) & 1, abort_flag, err)) break;
+            const int ps = s % kPack;
+            const uint4 lo = S.pack[ps][0][tid], hi = S.pack[ps][1][tid];
+            const int64_t grp = (int64_t(s) * kBK) >> p.gs_shift;
+            const uint2 sw = S.sz[ps][0][tid];
+            const int sub = static_cast<int>(sidx0 + grp) & kSubMask;
+            const uint32_t s0 = __byte_perm(scale_bits<ACT, SC>(sw, sub), 0, 0x1010);
+            const uint32_t s1 = two_groups ? __byte_perm(scale_bits<ACT, SC>(sw, sub + 1), 0, 0x1010) : s0;
+            uint32_t b0 = int4_bias_pair<ACT>(8u), b1 = b0;
+            if constexpr (ZERO) {
+                const uint2 zw = S.sz[ps][1][tid];
+                const int zs = static_cast<int>(zidx0 + grp) & 1;
+                const int nib = 4 * (row & 7);
+                b0 = int4_bias_pair<ACT>(((zs ? zw.y : zw.x) >> nib) & 15u);
+                b1 = two_groups ? int4_bias_pair<ACT>(((zs ? zw.x : zw.y) >> nib) & 15u) : b0;
+            }
+            const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            unsigned char* dst = row_base + slot * (kBN * kBK * 2);
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                const uint4 lo = S.pack[s % kPack][2 * m][r], hi = S.pack[s % kPack][2 * m + 1][r];
-                const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-                unsigned char* row_base = reinterpret_cast<unsigned char*>(S.b[slot][m]) + r * 128;
-#pragma unroll
-                for (int w = 0; w < 8; ++w) {
-                    const int grp = (s * kBK + w * 8) >> p.gs_shift;
-                    uint32_t sb;
-                    if constexpr (SC == ACT) sb = __ldg(reinterpret_cast<const unsigned short*>(sc) + sbase[m] + grp);
-                    else sb = act_bits<ACT>(load_scale<SC>(sc, sbase[m] + grp));
-                    const uint32_t spair = __byte_perm(sb, 0, 0x1010);
-                    uint32_t bpair;
-                    if constexpr (ZERO) {
-                        const uint32_t zw = static_cast<uint32_t>(__ldg(zp + zbase[m] + grp));
-                        bpair = int4_bias_pair<ACT>((zw >> (4 * ((n0 + r) & 7))) & 15u);
-                    } else {
-                        bpair = int4_bias_pair<ACT>(8u);
-                    }
-                    uint4 o;
-                    o.x = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 0), bpair), spair);
-                    o.y = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 1), bpair), spair);
-                    o.z = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 2), bpair), spair);
-                    o.w = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 3), bpair), spair);
-                    *reinterpret_cast<uint4*>(row_base + ((w ^ (r & 7)) << 4)) = o;
-                }
+            for (int w = 0; w < 8; ++w) {
+                const uint32_t sp = w < 4 ? s0 : s1, bp = w < 4 ? b0 : b1;
+                uint4 o;
+                o.x = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 0), bp), sp);
+                o.y = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 1), bp), sp);
+                o.z = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 2), bp), sp);
+                o.w = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 3), bp), sp);
+                *reinterpret_cast<uint4*>(dst + ((w ^ (r & 7)) << 4)) = o;
             }
             fence_async_smem();
             mbar_arrive(&S.full_b[slot]);
         }
         cp_async_wait<0>();
     } else if (warp == kDqThreads / 32 && lane == 0) {
-        // ── control: activation tiles by TMA, tcgen05.mma, commits ─────────────────────────
+        // ── control: activation tiles by TMA, tcgen05.mma (N = 256), commits ───────────────
         constexpr uint32_t idesc = idesc_f16<ACT>();
         int loaded = 0, landed = 0;   // activation tiles issued / seen complete
         for (; loaded < kStages - 1 && loaded < nk; ++loaded) {
@@ -326,14 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             landed = s + 1;
             if (!mbar_wait(&S.full_b[slot], par, abort_flag, err)) break;
             tc_fence_after();
-            const uint64_t ad = sw128_desc(S.a[slot]);
+            const uint64_t ad = sw128_desc(S.a[slot]), bd = sw128_desc(S.b[slot]);
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                const uint64_t bd = sw128_desc(S.b[slot][m]);
-#pragma unroll
-                for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
-                    umma(tmem + m * kBN, ad + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
-            }
+            for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
+                umma(tmem, ad + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
             umma_commit(&S.empty[slot]);
         }
         umma_commit(&S.done);   // arrives once every MMA issued so far has completed
@@ -342,22 +383,23 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             if (!mbar_drain(&S.full_a[t % kStages], (t / kStages) & 1, err)) break;
     }
 
-    // ── epilogue: TMEM -> registers -> global ───────────────────────────────────────────────
+    // ── epilogue: TMEM -> registers -> global (8 warps: lane quarter warp % 4) ──────────────
     if (tid < kDqThreads) {
         // every MMA must be complete before TMEM is read or freed, on the abort path too
         const bool finished = mbar_drain(&S.done, 0, err) && !*abort_flag && ok_ptrs;
         __syncwarp();
         tc_fence_after();
-        const int m_row = tid;                            // TMEM lane = tile row
-        const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
+        const int q = warp & 3, half = warp >> 2;
+        const int m_row = q * 32 + lane;                  // TMEM lane = tile row
+        const uint32_t lane_addr = tmem + (uint32_t(q * 32) << 16);
         const bool live = m_row < pe.ncols;
         const int pos = pe.row0 + m_row;
-        if (NMAT == 2) {
+        if constexpr (KIND == 0) {
 #pragma unroll 1
-            for (int c = 0; c < kBN; c += 16) {
+            for (int c = half * (kBlk / 2); c < (half + 1) * (kBlk / 2); c += 16) {
                 uint32_t gr[16], ur[16];
                 tmem_ld16(lane_addr + c, gr);
-                tmem_ld16(lane_addr + kBN + c, ur);
+                tmem_ld16(lane_addr + kBlk + c, ur);
                 if (finished && live) {
                     uint32_t hb[16];
 #pragma unroll
@@ -367,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                         const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
                         hb[j] = act_bits<ACT>(__fmul_rn(av, uv));
                     }
-                    // columns n0+c .. +16 are two 8-element groups; store them permuted
+                    // columns nbase+c .. +16 are two 8-element groups; store them permuted
                     uint4 o0, o1;
                     o0.x = hb[0] | (hb[4] << 16);
                     o0.y = hb[1] | (hb[5] << 16);
@@ -377,41 +419,44 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     o1.y = hb[9] | (hb[13] << 16);
                     o1.z = hb[10] | (hb[14] << 16);
                     o1.w = hb[11] | (hb[15] << 16);
-                    uint4* dst = reinterpret_cast<uint4*>(p.h_sorted + int64_t(pos) * p.ndim + n0 + c);
+                    uint4* dst = reinterpret_cast<uint4*>(p.h_sorted + int64_t(pos) * p.ndim + nbase + c);
                     dst[0] = o0;
                     dst[1] = o1;
                     if (p.h_out) {
                         const int rowid = p.order[pos];
                         for (int j = 0; j < 16; ++j)
-                            p.h_out[int64_t(rowid) * p.ndim + n0 + c + j] = static_cast<uint16_t>(hb[j]);
+                            p.h_out[int64_t(rowid) * p.ndim + nbase + c + j] = static_cast<uint16_t>(hb[j]);
                     }
                 }
             }
         } else {
-            const int rowid = live ? p.order[pos] : 0;
-            float wv = 0.f;
-            if (finished && live) {
-                const int64_t t = rowid / p.top_k;
-                const int k = rowid - int(t) * p.top_k;
-                const int widx = p.w_index ? p.w_index[rowid] : k;
-                wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
-            }
-#pragma unroll 1
-            for (int c = 0; c < kBN; c += 16) {
-                uint32_t yr[16];
-                tmem_ld16(lane_addr + c, yr);
+            const int col0 = nbase + half * kBlk;
+            if (col0 < p.ndim) {                          // warp-uniform
+                const int rowid = live ? p.order[pos] : 0;
+                float wv = 0.f;
                 if (finished && live) {
-                    float4 o[4];
-                    float* of = reinterpret_cast<float*>(o);
+                    const int64_t t = rowid / p.top_k;
+                    const int k = rowid - int(t) * p.top_k;
+                    const int widx = p.w_index ? p.w_index[rowid] : k;
+                    wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
+                }
+#pragma unroll 1
+                for (int c = 0; c < kBlk; c += 16) {
+                    uint32_t yr[16];
+                    tmem_ld16(lane_addr + half * kBlk + c, yr);
+                    if (finished && live) {
+                        float4 o[4];
+                        float* of = reinterpret_cast<float*>(o);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        float cv = __fmul_rn(round_act<ACT>(__uint_as_float(yr[j])), wv);
-                        if (p.w_round) cv = round_act<ACT>(cv);
-                        of[j] = cv;
+                        for (int j = 0; j < 16; ++j) {
+                            float cv = __fmul_rn(round_act<ACT>(__uint_as_float(yr[j])), wv);
+                            if (p.w_round) cv = round_act<ACT>(cv);
+                            of[j] = cv;
+                        }
+                        float4* dst = reinterpret_cast<float4*>(p.contrib + int64_t(rowid) * p.ndim + col0 + c);
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) dst[u] = o[u];
                     }
-                    float4* dst = reinterpret_cast<float4*>(p.contrib + int64_t(rowid) * p.ndim + n0 + c);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) dst[q] = o[q];
                 }
             }
         }
@@ -518,14 +563,15 @@ PrefillLayout prefill_layout(const vy_moe_call* c, void* base) {
     return L;
 }
 
-template <int ACT, int SC, bool ZERO, int NMAT>
+template <int ACT, int SC, bool ZERO, int KIND>
 int launch_gemm(const CUtensorMap& map, const GemmParams& gp, int max_tiles, cudaStream_t s) {
-    auto kern = gemm_kernel<ACT, SC, ZERO, NMAT>;
-    const size_t smem = sizeof(GemmSmem<NMAT>) + 1024;
+    auto kern = gemm_kernel<ACT, SC, ZERO, KIND>;
+    const size_t smem = sizeof(GemmSmem) + 1024;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "prefill GEMM shared memory: %s", cudaGetErrorString(e));
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(max_tiles), static_cast<unsigned>(gp.ndim / kBN));
+    const int nblk = KIND == 0 ? gp.ndim / kBlk : (gp.ndim + kBN - 1) / kBN;
+    cfg.gridDim = dim3(static_cast<unsigned>(max_tiles), static_cast<unsigned>(nblk));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -542,7 +588,7 @@ int launch_gemm(const CUtensorMap& map, const GemmParams& gp, int max_tiles, cud
 template <int ACT, int SC, bool ZERO>
 int run_prefill_gemms(const CUtensorMap& ma, const GemmParams& g1, const CUtensorMap& mh, const GemmParams& g2,
                       int max_tiles, cudaStream_t s) {
-    int st = launch_gemm<ACT, SC, ZERO, 2>(ma, g1, max_tiles, s);
+    int st = launch_gemm<ACT, SC, ZERO, 0>(ma, g1, max_tiles, s);
     if (st != VY_OK) return st;
     return launch_gemm<ACT, SC, ZERO, 1>(mh, g2, max_tiles, s);
 }
@@ -579,8 +625,12 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
     if ((st = validate_call(c)) != VY_OK) return st;
     if (c->n_tokens == 0) return ok();
     const vy_expert_geom& g = *c->geom;
-    if (g.group_size < 8 || g.hidden % kBN || g.inter % kBN)
-        return fail(VY_ERR_UNSUPPORTED, "prefill tiles need hidden / intermediate multiples of %d", kBN);
+    if (g.group_size < 32 || g.hidden % kBlk || g.inter % kBlk)
+        return fail(VY_ERR_UNSUPPORTED, "prefill tiles need hidden / intermediate multiples of %d", kBlk);
+    // a stage's scale / zero element is read as the aligned 8-byte word holding it
+    for (int r = 0; r < 3; ++r)
+        if (g.scale_off[r] % (g.scale_dtype == VY_F32 ? 2 : 4) || (g.has_zero && g.zero_off[r] % 2))
+            return fail(VY_ERR_UNSUPPORTED, "prefill: role %d's scale / zero offset is not a multiple of 8 bytes", r);
     PrefillLayout L = prefill_layout(c, nullptr);
     if (!c->workspace || c->workspace_bytes < L.bytes + 1024)
         return fail(VY_ERR_WORKSPACE, "workspace %zu bytes, %zu needed", c->workspace_bytes, L.bytes + 1024);
