@@ -1,23 +1,26 @@
 // vy_prefill.cu -- the prefill expert layer as tcgen05 grouped GEMMs (accumulators in TMEM).
 //
-//   plan (vy_route.cu)   rows grouped by expert; the pass table holds one entry per 128-row
-//                        M-tile of a live expert (stream pointers, first sorted row, row count)
+//   plan (vy_route.cu)   rows grouped by expert; the pass table holds one entry per 256-row unit
+//                        of a live expert (stream pointers, first sorted row, row count)
 //   gather_kernel        x rows in sorted order -> x_sorted, 8-element groups permuted the way the
 //                        dequantised pairs come out (code j pairs with code j + 4), so A and B
 //                        share one consistent K order
-//   gemm_kernel<2>       h = act(act(silu(act(x Wg^T))) * act(x Wu^T)) per M-tile x 128 columns
-//   gemm_kernel<1>       c = act(h Wd^T) * w (one fp32 rounding), scattered to the row ids
-//   combine (vy_route)   each token's contributions in ascending expert id, then slot
+//   gemm_kernel<0>       h = act(act(silu(act(x Wg^T))) * act(x Wu^T)), 256 rows x 128 columns
+//   gemm_kernel<1>       c = act(h Wd^T) * w (one fp32 rounding), 256 rows x 256 columns,
+//                        scattered to the row ids
+//   slot_combine_kernel  each token's contributions in ascending expert id, then slot
 //
-// A GEMM CTA: 4 dequant warps + 1 control warp.  Each dequant thread owns one row of the 128-row
-// weight tile: it copies that row's packed codes into a private cp.async ring, dequantises them
-// (the reference's exact rounding of every weight: sub.rn then mul.rn on activation-dtype pairs)
-// and stores the 16-byte chunks into the weight tile in the 128-byte-swizzled K-major layout the
-// tensor core reads; then it arrives on the stage's barrier.  The control thread loads the
-// activation tile with TMA (same swizzle, no multicast) and issues tcgen05.mma (M=128, N=128,
-// K=16, fp32 accumulate in TMEM) once both halves of a stage are in; tcgen05.commit frees the
-// stage.  The epilogue warps read TMEM with tcgen05.ld.  Every barrier wait is bounded: on a
-// timeout the CTA records an error flag, drains what it issued, frees TMEM and returns.
+// A GEMM CTA: 8 dequant warps + 1 control warp.  Each dequant thread owns one row of the 256-row
+// weight tile: it copies that row's packed codes, scale and zero word into a private cp.async
+// ring, dequantises them (the reference's exact rounding of every weight: sub.rn then mul.rn on
+// activation-dtype pairs) and stores the 16-byte chunks into the weight tile in the
+// 128-byte-swizzled K-major layout the tensor core reads; then it arrives on the stage's barrier.
+// The control thread loads the 256-row activation tile with one TMA box (same swizzle, no
+// multicast) and issues tcgen05.mma M=128 N=256 K=16 for each of the two 128-row halves into its
+// own 256 TMEM columns, so every dequantised weight tile feeds 256 rows; tcgen05.commit frees the
+// stages.  The dequant warps then read TMEM with tcgen05.ld for the epilogue.  Every barrier wait
+// is bounded: on a timeout the CTA records an error flag, drains what it issued, frees TMEM and
+// returns.
 #include <cuda.h>
 
 #include <mutex>
@@ -27,15 +30,18 @@
 namespace vy {
 namespace {
 
-constexpr int kBM = 128, kBK = 64;
+constexpr int kBM = 128, kBK = 64;    // one MMA: 128 rows, K = 64 per stage
+constexpr int kUnit = 2 * kBM;        // rows per CTA: two 128-row halves share the weight tile
 constexpr int kBlk = 128;             // rows of one weight block
 constexpr int kBN = 2 * kBlk;         // a CTA's N: two weight blocks (gate + up, or 256 down rows)
-constexpr int kStages = 3;            // shared-memory stages (activation tile + weight tile)
+constexpr int kAStages = 3;           // activation-tile ring (TMA)
+constexpr int kBStages = 2;           // weight-tile ring (dequant warps)
 constexpr int kPack = 4;              // packed-code staging depth, private to each dequant thread
 constexpr int kDqThreads = 2 * kBlk;  // one per weight-tile row
 constexpr int kThreads = kDqThreads + 32;
+constexpr uint32_t kTmemCols = 2 * kBN;       // one N = 256 accumulator per 128-row half
 constexpr uint64_t kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
-constexpr int kTileBytes = kBM * kBK * 2;     // 16 KB: one 128 x 64 activation tile
+constexpr int kTileBytes = kUnit * kBK * 2;   // 32 KB: one 256 x 64 activation tile
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -213,11 +219,11 @@ struct GemmParams {
 };
 
 struct __align__(1024) GemmSmem {
-    uint16_t a[kStages][kBM * kBK];            // activation tiles (TMA, swizzled)
-    uint16_t b[kStages][kBN * kBK];            // weight tiles: rows 0-127 block 0, 128-255 block 1
+    uint16_t a[kAStages][kUnit * kBK];         // activation tiles (TMA, swizzled): rows 0-255
+    uint16_t b[kBStages][kBN * kBK];           // weight tiles: rows 0-127 block 0, 128-255 block 1
     uint4 pack[kPack][2][kDqThreads];          // packed codes, private per thread
     uint2 sz[kPack][2][kDqThreads];            // the 8-byte words holding a stage's scale / zero word
-    uint64_t full_a[kStages], full_b[kStages], empty[kStages], done;
+    uint64_t full_a[kAStages], empty_a[kAStages], full_b[kBStages], empty_b[kBStages], done;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -256,13 +262,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const PassEntry pe = p.passes[blockIdx.x];
     const int nbase = blockIdx.y * (KIND == 0 ? kBlk : kBN);
     const int nk = p.kdim / kBK;
-    constexpr uint32_t kTmemCols = kBN;
+    const bool two = pe.ncols > kBM;                         // second 128-row half has rows
 
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) {
+        for (int i = 0; i < kAStages; ++i) {
             mbar_init(&S.full_a[i], 1);
+            mbar_init(&S.empty_a[i], 1);
+        }
+        for (int i = 0; i < kBStages; ++i) {
             mbar_init(&S.full_b[i], kDqThreads);
-            mbar_init(&S.empty[i], 1);
+            mbar_init(&S.empty_b[i], 1);
         }
         mbar_init(&S.done, 1);
         S.abort_flag = 0;
@@ -315,8 +324,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         for (int s = 0; s < nk; ++s) {
             issue(s + kPack - 1);
             cp_async_wait<kPack - 1>();
-            const int slot = s % kStages;
-            if (s >= kStages && !mbar_wait(&S.empty[slot], ((s / kStages) - 1) & 1, abort_flag, err)) break;
+            const int slot = s % kBStages;
+            if (s >= kBStages && !mbar_wait(&S.empty_b[slot], ((s / kBStages) - 1) & 1, abort_flag, err)) break;
             const int ps = s % kPack;
             const uint4 lo = S.pack[ps][0][tid], hi = S.pack[ps][1][tid];
             const int64_t grp = (int64_t(s) * kBK) >> p.gs_shift;
@@ -352,86 +361,95 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         // ── control: activation tiles by TMA, tcgen05.mma (N = 256), commits ───────────────
         constexpr uint32_t idesc = idesc_f16<ACT>();
         int loaded = 0, landed = 0;   // activation tiles issued / seen complete
-        for (; loaded < kStages - 1 && loaded < nk; ++loaded) {
+        for (; loaded < kAStages - 1 && loaded < nk; ++loaded) {
             mbar_expect_tx(&S.full_a[loaded], kTileBytes);
             tma_load_2d(S.a[loaded], &tmap_a, loaded * kBK, pe.row0, &S.full_a[loaded]);
         }
         for (int s = 0; s < nk; ++s) {
-            const int t = s + kStages - 1;
+            const int sa = s % kAStages, sb = s % kBStages;
+            if (!mbar_wait(&S.full_a[sa], (s / kAStages) & 1, abort_flag, err)) break;
+            landed = s + 1;
+            if (!mbar_wait(&S.full_b[sb], (s / kBStages) & 1, abort_flag, err)) break;
+            tc_fence_after();
+            const uint64_t ad = sw128_desc(S.a[sa]), bd = sw128_desc(S.b[sb]);
+            // second half: activation rows 128-255 start 128 rows x 128 bytes further on
+            constexpr uint64_t kHalf = (kBM * 128) >> 4;
+#pragma unroll
+            for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
+                umma(tmem, ad + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
+            if (two) {
+#pragma unroll
+                for (int j = 0; j < kBK / 16; ++j)
+                    umma(tmem + kBN, ad + kHalf + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
+            }
+            umma_commit(&S.empty_a[sa]);
+            umma_commit(&S.empty_b[sb]);
+            // the next activation tile goes into the slot MMA s-1 read: wait for it only now,
+            // with MMA s already queued behind it
+            const int t = s + kAStages - 1;
             if (t < nk) {
-                const int ts = t % kStages;
-                if (t >= kStages && !mbar_wait(&S.empty[ts], ((t / kStages) - 1) & 1, abort_flag, err)) break;
+                const int ts = t % kAStages;
+                if (t >= kAStages && !mbar_wait(&S.empty_a[ts], ((t / kAStages) - 1) & 1, abort_flag, err)) break;
                 mbar_expect_tx(&S.full_a[ts], kTileBytes);
                 tma_load_2d(S.a[ts], &tmap_a, t * kBK, pe.row0, &S.full_a[ts]);
                 loaded = t + 1;
             }
-            const int slot = s % kStages;
-            const uint32_t par = (s / kStages) & 1;
-            if (!mbar_wait(&S.full_a[slot], par, abort_flag, err)) break;
-            landed = s + 1;
-            if (!mbar_wait(&S.full_b[slot], par, abort_flag, err)) break;
-            tc_fence_after();
-            const uint64_t ad = sw128_desc(S.a[slot]), bd = sw128_desc(S.b[slot]);
-#pragma unroll
-            for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
-                umma(tmem, ad + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
-            umma_commit(&S.empty[slot]);
         }
         umma_commit(&S.done);   // arrives once every MMA issued so far has completed
         // aborted: the activation tiles still in flight must land before shared memory is released
         for (int t = landed; t < loaded; ++t)
-            if (!mbar_drain(&S.full_a[t % kStages], (t / kStages) & 1, err)) break;
+            if (!mbar_drain(&S.full_a[t % kAStages], (t / kAStages) & 1, err)) break;
     }
 
-    // ── epilogue: TMEM -> registers -> global (8 warps: lane quarter warp % 4) ──────────────
+    // ── epilogue: TMEM -> registers -> global.  Warp w reads TMEM lanes 32 (w % 4) .. +31
+    // (its lane quarter) of half w / 4: tile row 128 (w / 4) + 32 (w % 4) + lane ────────────
     if (tid < kDqThreads) {
         // every MMA must be complete before TMEM is read or freed, on the abort path too
         const bool finished = mbar_drain(&S.done, 0, err) && !*abort_flag && ok_ptrs;
         __syncwarp();
         tc_fence_after();
         const int q = warp & 3, half = warp >> 2;
-        const int m_row = q * 32 + lane;                  // TMEM lane = tile row
-        const uint32_t lane_addr = tmem + (uint32_t(q * 32) << 16);
+        const int m_row = half * kBM + q * 32 + lane;
+        const uint32_t lane_addr = tmem + (uint32_t(q * 32) << 16) + half * kBN;
         const bool live = m_row < pe.ncols;
         const int pos = pe.row0 + m_row;
-        if constexpr (KIND == 0) {
+        if (half == 0 || two) {                           // warp-uniform
+            if constexpr (KIND == 0) {
 #pragma unroll 1
-            for (int c = half * (kBlk / 2); c < (half + 1) * (kBlk / 2); c += 16) {
-                uint32_t gr[16], ur[16];
-                tmem_ld16(lane_addr + c, gr);
-                tmem_ld16(lane_addr + kBlk + c, ur);
-                if (finished && live) {
-                    uint32_t hb[16];
+                for (int c = 0; c < kBlk; c += 16) {
+                    uint32_t gr[16], ur[16];
+                    tmem_ld16(lane_addr + c, gr);
+                    tmem_ld16(lane_addr + kBlk + c, ur);
+                    if (finished && live) {
+                        uint32_t hb[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float gv = round_act<ACT>(__uint_as_float(gr[j]));
-                        const float uv = round_act<ACT>(__uint_as_float(ur[j]));
-                        const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
-                        hb[j] = act_bits<ACT>(__fmul_rn(av, uv));
-                    }
-                    // columns nbase+c .. +16 are two 8-element groups; store them permuted
-                    uint4 o0, o1;
-                    o0.x = hb[0] | (hb[4] << 16);
-                    o0.y = hb[1] | (hb[5] << 16);
-                    o0.z = hb[2] | (hb[6] << 16);
-                    o0.w = hb[3] | (hb[7] << 16);
-                    o1.x = hb[8] | (hb[12] << 16);
-                    o1.y = hb[9] | (hb[13] << 16);
-                    o1.z = hb[10] | (hb[14] << 16);
-                    o1.w = hb[11] | (hb[15] << 16);
-                    uint4* dst = reinterpret_cast<uint4*>(p.h_sorted + int64_t(pos) * p.ndim + nbase + c);
-                    dst[0] = o0;
-                    dst[1] = o1;
-                    if (p.h_out) {
-                        const int rowid = p.order[pos];
-                        for (int j = 0; j < 16; ++j)
-                            p.h_out[int64_t(rowid) * p.ndim + nbase + c + j] = static_cast<uint16_t>(hb[j]);
+                        for (int j = 0; j < 16; ++j) {
+                            const float gv = round_act<ACT>(__uint_as_float(gr[j]));
+                            const float uv = round_act<ACT>(__uint_as_float(ur[j]));
+                            const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
+                            hb[j] = act_bits<ACT>(__fmul_rn(av, uv));
+                        }
+                        // columns nbase+c .. +16 are two 8-element groups; store them permuted
+                        uint4 o0, o1;
+                        o0.x = hb[0] | (hb[4] << 16);
+                        o0.y = hb[1] | (hb[5] << 16);
+                        o0.z = hb[2] | (hb[6] << 16);
+                        o0.w = hb[3] | (hb[7] << 16);
+                        o1.x = hb[8] | (hb[12] << 16);
+                        o1.y = hb[9] | (hb[13] << 16);
+                        o1.z = hb[10] | (hb[14] << 16);
+                        o1.w = hb[11] | (hb[15] << 16);
+                        uint4* dst = reinterpret_cast<uint4*>(p.h_sorted + int64_t(pos) * p.ndim + nbase + c);
+                        dst[0] = o0;
+                        dst[1] = o1;
+                        if (p.h_out) {
+                            const int rowid = p.order[pos];
+                            for (int j = 0; j < 16; ++j)
+                                p.h_out[int64_t(rowid) * p.ndim + nbase + c + j] = static_cast<uint16_t>(hb[j]);
+                        }
                     }
                 }
-            }
-        } else {
-            const int col0 = nbase + half * kBlk;
-            if (col0 < p.ndim) {                          // warp-uniform
+            } else {
                 const int rowid = live ? p.order[pos] : 0;
                 float wv = 0.f;
                 if (finished && live) {
@@ -440,10 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     const int widx = p.w_index ? p.w_index[rowid] : k;
                     wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
                 }
+                const int ncol = min(kBN, p.ndim - nbase);   // 128 or 256: warp-uniform
 #pragma unroll 1
-                for (int c = 0; c < kBlk; c += 16) {
+                for (int c = 0; c < ncol; c += 16) {
                     uint32_t yr[16];
-                    tmem_ld16(lane_addr + half * kBlk + c, yr);
+                    tmem_ld16(lane_addr + c, yr);
                     if (finished && live) {
                         float4 o[4];
                         float* of = reinterpret_cast<float*>(o);
@@ -453,7 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                             if (p.w_round) cv = round_act<ACT>(cv);
                             of[j] = cv;
                         }
-                        float4* dst = reinterpret_cast<float4*>(p.contrib + int64_t(rowid) * p.ndim + col0 + c);
+                        float4* dst = reinterpret_cast<float4*>(p.contrib + int64_t(rowid) * p.ndim + nbase + c);
 #pragma unroll
                         for (int u = 0; u < 4; ++u) dst[u] = o[u];
                     }
@@ -517,14 +536,14 @@ EncodeTiledFn encode_fn(int* status) {
     return fn;
 }
 
-// A [rows, cols] 16-bit matrix as 128 x 64 tiles with the 128-byte swizzle.
+// A [rows, cols] 16-bit matrix as 256 x 64 tiles with the 128-byte swizzle.
 int make_tile_map(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int act) {
     int st;
     EncodeTiledFn fn = encode_fn(&st);
     if (!fn) return st;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
-    const cuuint32_t box[2] = {kBK, kBM};
+    const cuuint32_t box[2] = {kBK, kUnit};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = fn(map, act == VY_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -554,7 +573,7 @@ PrefillLayout prefill_layout(const vy_moe_call* c, void* base) {
     L.unit_start = cv.take<int32_t>(E + 1);
     L.slot_order = cv.take<int32_t>(n);
     L.counters = cv.take<int32_t>(4);
-    L.max_tiles = n / kBM + (n < E ? n : E) + 1;
+    L.max_tiles = n / kUnit + (n < E ? n : E) + 1;
     L.passes = cv.take<PassEntry>(L.max_tiles);
     L.x_sorted = cv.take<uint16_t>(n * H);
     L.h_sorted = cv.take<uint16_t>(n * I);
@@ -653,7 +672,7 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
     pa.unit_start = L.unit_start;
     pa.slot_order = L.slot_order;
     pa.counters = L.counters;
-    pa.tok_per_unit = kBM;
+    pa.tok_per_unit = kUnit;
     pa.expert_table = c->expert_table;
     pa.passes = L.passes;
     if ((st = launch_plan(pa, dev->sm_count, s)) != VY_OK) return st;
