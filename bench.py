@@ -41,8 +41,11 @@ import torch  # noqa: E402
 METRIC = "int4 MoE expert-layer tokens/s and % HBM/tensor roofline at 1/2/4/8 B200"
 WORKLOAD = dict(name="cfg1: Qwen3-30B-A3B-shaped int4 MoE layer, decode", hidden=2048, inter=768,
                 experts=128, top_k=8, tokens=32, group=128)
+PREFILL = dict(name="cfg2: Mixtral-8x7B-shaped int4 MoE layer, prefill", hidden=4096, inter=14336,
+               experts=8, top_k=2, tokens=2048, group=128, skew=0.9)
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
+FALLBACK_BF16 = 1590.0
 
 
 def hbm_peak():
@@ -50,6 +53,15 @@ def hbm_peak():
         return float(json.loads(PEAKS.read_text())["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM, "fallback"
+
+
+def bf16_peak():
+    """(burst TFLOP/s, sustained TFLOP/s or None, source)."""
+    try:
+        p = json.loads(PEAKS.read_text())
+        return float(p["bf16_tflops"]), float(p.get("bf16_tflops_sustained") or 0) or None, "measured"
+    except Exception:
+        return FALLBACK_BF16, None, "fallback"
 
 
 # ── distributed plumbing ─────────────────────────────────────────────────────────────────
@@ -173,6 +185,96 @@ def gate_up_bytes(table, idx):
     return per_expert * len(set(idx.reshape(-1).tolist()))
 
 
+def prefill_bench(args, device):
+    """Configuration 2 through the tcgen05 grouped-GEMM path: one layer call of 2048 tokens per
+    step (top-2 over 8 experts, logits skewed so expert loads differ ~4x), two layers rotated."""
+    import ctypes
+
+    import vaayu_b200 as vb
+    from vaayu_b200 import packed_expert_kernels as pk
+    from vaayu_b200 import synthetic
+    wl = PREFILL
+    T, K, H, I = wl["tokens"], wl["top_k"], wl["hidden"], wl["inter"]
+    L = 2
+    layers = [pk.ExpertTable(make_layer(2000 + l, wl, device)) for l in range(L)]
+    batches = []
+    for l in range(L):
+        g = torch.Generator(device=device).manual_seed(20_000 + l)
+        batches.append(tuple(v.to(device) for v in synthetic.make_tokens(T, H, wl["experts"], K, g,
+                                                                         skew=wl["skew"])))
+    loads = [torch.bincount(b[2].reshape(-1), minlength=wl["experts"]).tolist() for b in batches]
+    out = torch.empty(T, H, dtype=torch.float32, device=device)
+    ws = torch.empty(pk.moe_workspace_bytes(layers[0], T, K, path=vb.PATH_PREFILL), dtype=torch.uint8,
+                     device=device)
+
+    def step(i):
+        x, w, idx = batches[i % L]
+        vb.moe_forward(x, idx, w, layers[i % L], out=out, path=vb.PATH_PREFILL, workspace=ws)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    if args.profile:
+        ms = time_steps(step, args.steps, device)
+        print(json.dumps({"profile": "prefill", "ms_per_step": ms, "tokens": T, "layers": L}))
+        return None
+    steps = max(5, min(args.steps, 20))
+    with ClockSampler(device.index or 0) as clocks:
+        ms = time_steps(step, steps, device)
+    flops = 2.0 * T * K * 3 * H * I
+    # per-stage device times (serialised stages) for the per-kernel roofline
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    for e in evs:
+        e.record()
+    torch.cuda.synchronize(device)
+    handles = (ctypes.c_void_p * 5)(*[e.cuda_event for e in evs])
+    st = {"plan_gather": [], "gate_up_gemm": [], "down_gemm": [], "combine": []}
+    for i in range(steps):
+        x, w, idx = batches[i % L]
+        tb = layers[i % L]
+        c = pk._make_call(tb.geom_s, x, T, K, tb.n_experts, tb.table.data_ptr(), idx.data_ptr(), 6, w,
+                          w.stride(0), w.stride(1), None, out, None, None)
+        c.stage_events, c.n_stage_events = ctypes.cast(handles, ctypes.c_void_p), 5
+        pk._enqueue(c, vb.PATH_PREFILL, device, ws)
+        torch.cuda.synchronize(device)
+        st["plan_gather"].append(evs[0].elapsed_time(evs[1]))
+        st["gate_up_gemm"].append(evs[1].elapsed_time(evs[2]))
+        st["down_gemm"].append(evs[2].elapsed_time(evs[4]))
+        st["combine"].append(evs[4].elapsed_time(evs[3]))
+    st = {k: statistics.mean(v) for k, v in st.items()}
+    burst, sustained, src = bf16_peak()
+    gu_tf = (2.0 * T * K * 2 * H * I) / (st["gate_up_gemm"] / 1e3) / 1e12
+    dn_tf = (2.0 * T * K * H * I) / (st["down_gemm"] / 1e3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "prefill_gemm_traffic.json"
+    if tfile.exists():
+        try:
+            traffic = json.loads(tfile.read_text()).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+    layer_tf = flops / (ms / 1e3) / 1e12
+    cpu = cpu_prefill_baseline(layers[0], batches[0]) if not args.no_cpu else None
+    return {
+        "workload": wl["name"], "tokens": T, "top_k": K, "experts": wl["experts"], "hidden": H,
+        "expert_intermediate": I, "group_size": wl["group"], "layers_rotated": L,
+        "expert_rows_per_layer": loads,
+        "load_ratio_max_min": statistics.mean(max(x) / max(1, min(x)) for x in loads),
+        "l2": "inputs larger than L2: each step reads ~730 MB of expert weights",
+        "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "steps": steps,
+        "layer_tflops": layer_tf, "layer_frac_of_bf16_burst": layer_tf / burst,
+        "algorithmic_flops_per_step": flops,
+        "roofline": {"kernel": "gemm_kernel<gate/up> (tcgen05, int4 dequant in shared memory)",
+                     "bound": "tensor", "achieved": gu_tf, "peak": burst, "unit": "TFLOP/s",
+                     "frac": gu_tf / burst, "peak_source": src + " (burst)",
+                     "frac_of_sustained": gu_tf / sustained if sustained else None,
+                     "traffic": traffic, "launch_ms": st["gate_up_gemm"]},
+        "down_gemm": {"achieved_tflops": dn_tf, "frac": dn_tf / burst, "launch_ms": st["down_gemm"]},
+        "stage_ms": st,
+        "cpu_baseline": cpu,
+        "gpu_launches": 5 * steps,
+        "clocks": clocks.summary(),
+    }
+
+
 def time_steps(fn, steps, device):
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -193,6 +295,8 @@ def run_ours(args, rank, world, local):
     if world > 1:
         from vaayu_b200 import ep
         return ep.run_bench(args, rank, world, local, wl)
+    if args.profile == "prefill":
+        return prefill_bench(args, device)
 
     layers = [pk.ExpertTable(make_layer(1000 * l, wl, device)) for l in range(args.layers)]
     batches = {}
@@ -293,7 +397,10 @@ def run_ours(args, rank, world, local):
     h2d = dx.numel() * dx.element_size() + dw.numel() * dw.element_size() + di.numel() * di.element_size()
     d2h = out_h.numel() * out_h.element_size()
 
-    cpu = cpu_baseline(layers[0], batches[T][0], wl) if rank == 0 else None
+    cpu = cpu_baseline(layers[0], batches[T][0], wl) if rank == 0 and not args.no_cpu else None
+    del layers, batches
+    torch.cuda.empty_cache()
+    prefill = prefill_bench(args, device) if not args.no_prefill else None
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -317,6 +424,7 @@ def run_ours(args, rank, world, local):
         "cpu_baseline": cpu,
         "gpu_launches": 3 * args.steps,
         "clocks": clocks.summary(),
+        "prefill": prefill,
     }
     if rank == 0:
         print(json.dumps(line))
@@ -346,6 +454,20 @@ def cpu_baseline(table, batch, wl, budget_s=10.0):
     return {"value": reps * x.shape[0] / el, "unit": "tokens/s", "cores": threads, "kind": "port",
             "sample": f"{reps} full layer calls of the benchmark workload ({x.shape[0]} tokens each, "
                       f"{el:.1f} s), C oracle restating stock_experts_prefill(linear=_linear_fp32)"}
+
+
+def cpu_prefill_baseline(table, batch, tokens=48):
+    """The oracle port on a bounded sample of configuration 2: the first `tokens` tokens."""
+    from oracle import oracle as O
+    x, w, idx = batch
+    experts, xs, ids, ws = _oracle_inputs(table, (x[:tokens], w[:tokens], idx[:tokens]))
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    O.moe_layer(table.geom, experts, xs, O.BF16, ids, ws, O.F32, O.F16, threads=threads)
+    el = time.perf_counter() - t0
+    return {"value": tokens / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one layer call of the first {tokens} of the {x.shape[0]} tokens ({el:.1f} s), "
+                      f"C oracle restating stock_experts_prefill(linear=_linear_fp32)"}
 
 
 def run_reference(args, rank, world, local):
@@ -403,8 +525,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--layers", type=int, default=8)
-    ap.add_argument("--profile", action="store_true",
-                    help="only the timed loop of the main step (for ncu captures)")
+    ap.add_argument("--profile", nargs="?", const="decode", choices=("decode", "prefill"), default=None,
+                    help="only the timed loop of the decode (default) or prefill step, for ncu")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the configuration-2 prefill measurement")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_setup()

@@ -205,8 +205,10 @@ typedef struct vy_moe_call {
     size_t workspace_bytes;
     /* Optional per-stage timing (the reference's per-phase profile, vaayu/moe_patch.py:2431-2438):
      * when non-NULL, n_stage_events (>= 4) cudaEvent_t handles recorded on `stream` before the
-     * routing plan, after it, after the gate/up stage and after the down/combine stage.  Recording
-     * them serialises the stages (no programmatic overlap): a profiling mode, not the fast path. */
+     * routing plan, after it (and, for prefill, the row gather), after the gate/up stage and after
+     * the down/combine stage; vy_moe_prefill records a fifth, when given, between the down GEMM and
+     * the combine.  Recording them serialises the stages (no programmatic overlap): a profiling
+     * mode, not the fast path. */
     void* const* stage_events;
     int32_t n_stage_events;
     int32_t reserved1;

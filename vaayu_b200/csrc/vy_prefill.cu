@@ -10,17 +10,18 @@
 //                        scattered to the row ids
 //   slot_combine_kernel  each token's contributions in ascending expert id, then slot
 //
-// A GEMM CTA: 8 dequant warps + 1 control warp.  Each dequant thread owns one row of the 256-row
-// weight tile: it copies that row's packed codes, scale and zero word into a private cp.async
-// ring, dequantises them (the reference's exact rounding of every weight: sub.rn then mul.rn on
+// A GEMM CTA: 16 dequant warps + 1 control warp.  Each dequant thread owns one K half of one
+// row of the 256-row weight tile (32 codes per stage): it copies those packed codes into a private
+// cp.async ring (the row's scale and zero words stream through registers, a word ahead),
+// dequantises them (the reference's exact rounding of every weight: sub.rn then mul.rn on
 // activation-dtype pairs) and stores the 16-byte chunks into the weight tile in the
-// 128-byte-swizzled K-major layout the tensor core reads; then it arrives on the stage's barrier.
-// The control thread loads the 256-row activation tile with one TMA box (same swizzle, no
-// multicast) and issues tcgen05.mma M=128 N=256 K=16 for each of the two 128-row halves into its
-// own 256 TMEM columns, so every dequantised weight tile feeds 256 rows; tcgen05.commit frees the
-// stages.  The dequant warps then read TMEM with tcgen05.ld for the epilogue.  Every barrier wait
-// is bounded: on a timeout the CTA records an error flag, drains what it issued, frees TMEM and
-// returns.
+// 128-byte-swizzled K-major layout the tensor core reads; then each warp arrives once on the
+// stage's barrier.  The control thread loads the 256-row activation tile with one TMA box (same
+// swizzle, no multicast; three tiles in flight) and issues tcgen05.mma M=128 N=256 K=16 for each
+// of the two 128-row halves into its own 256 TMEM columns, so every dequantised weight tile feeds
+// 256 rows; tcgen05.commit frees the stages.  The dequant warps then read TMEM with tcgen05.ld for
+// the epilogue.  Every barrier wait is bounded: on a timeout the CTA records an error flag, drains
+// what it issued, frees TMEM and returns.
 #include <cuda.h>
 
 #include <mutex>
@@ -34,10 +35,10 @@ constexpr int kBM = 128, kBK = 64;    // one MMA: 128 rows, K = 64 per stage
 constexpr int kUnit = 2 * kBM;        // rows per CTA: two 128-row halves share the weight tile
 constexpr int kBlk = 128;             // rows of one weight block
 constexpr int kBN = 2 * kBlk;         // a CTA's N: two weight blocks (gate + up, or 256 down rows)
-constexpr int kAStages = 3;           // activation-tile ring (TMA)
+constexpr int kAStages = 4;           // activation-tile ring (TMA): three tiles in flight
 constexpr int kBStages = 2;           // weight-tile ring (dequant warps)
 constexpr int kPack = 4;              // packed-code staging depth, private to each dequant thread
-constexpr int kDqThreads = 2 * kBlk;  // one per weight-tile row
+constexpr int kDqThreads = 4 * kBlk;  // two per weight-tile row: K halves of each stage
 constexpr int kThreads = kDqThreads + 32;
 constexpr uint32_t kTmemCols = 2 * kBN;       // one N = 256 accumulator per 128-row half
 constexpr uint64_t kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
@@ -104,9 +105,40 @@ __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int32
     }
 }
 
-__device__ __forceinline__ void cp_async8(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ uint2 ld_nc_v2(const void* p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
 }
+
+// One row's scale (or zero-point) elements [first, last] read as the aligned 8-byte words that
+// hold them (2^LG elements per word): the word of the current stage sits in a register and the
+// next one is loaded when the current one is entered, a whole word period before it is needed.
+// Only words holding an element of the row are read.
+template <int LG>
+struct WordStream {
+    const uint2* words;
+    uint32_t last;      // the row's last element
+    uint32_t wi;        // index of the word in `cur`
+    uint2 cur, nxt;
+    __device__ __forceinline__ void start(const void* base, uint32_t first_elem, uint32_t last_elem, bool go) {
+        words = reinterpret_cast<const uint2*>(base);
+        last = last_elem;
+        wi = first_elem >> LG;
+        cur = go ? ld_nc_v2(words + wi) : make_uint2(0u, 0u);
+        nxt = (go && ((wi + 1) << LG) <= last) ? ld_nc_v2(words + wi + 1) : make_uint2(0u, 0u);
+    }
+    // the word holding element e (e never moves more than one word per call)
+    __device__ __forceinline__ uint2 at(uint32_t e, bool go) {
+        const uint32_t w = e >> LG;
+        if (w != wi) {
+            wi = w;
+            cur = nxt;
+            if (go && ((w + 1) << LG) <= last) nxt = ld_nc_v2(words + w + 1);
+        }
+        return cur;
+    }
+};
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
@@ -221,8 +253,7 @@ struct GemmParams {
 struct __align__(1024) GemmSmem {
     uint16_t a[kAStages][kUnit * kBK];         // activation tiles (TMA, swizzled): rows 0-255
     uint16_t b[kBStages][kBN * kBK];           // weight tiles: rows 0-127 block 0, 128-255 block 1
-    uint4 pack[kPack][2][kDqThreads];          // packed codes, private per thread
-    uint2 sz[kPack][2][kDqThreads];            // the 8-byte words holding a stage's scale / zero word
+    uint4 pack[kPack][kDqThreads];             // packed codes, private per thread
     uint64_t full_a[kAStages], empty_a[kAStages], full_b[kBStages], empty_b[kBStages], done;
     uint32_t tmem_base;
     int abort_flag;
@@ -270,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(&S.empty_a[i], 1);
         }
         for (int i = 0; i < kBStages; ++i) {
-            mbar_init(&S.full_b[i], kDqThreads);
+            mbar_init(&S.full_b[i], kDqThreads / 32);   // one arrive per dequant warp
             mbar_init(&S.empty_b[i], 1);
         }
         mbar_init(&S.done, 1);
@@ -290,71 +321,70 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (!ok_ptrs && tid == 0) atomicOr(err, 1);
 
     if (tid < kDqThreads) {
-        // ── dequant producer: weight-tile row `tid` ─────────────────────────────────────────
-        const int blk = tid >> 7, r = tid & (kBlk - 1);
+        // ── dequant producer: tile row r = tid % 256, K half hh = tid / 256 of every stage
+        // (words 4 hh .. 4 hh + 3 of the stage's 8: 32 codes, inside one scale group) ────────
+        const int r = tid & (kBN - 1), hh = tid >> 8;
+        const int blk = r >> 7;
         const int m = KIND == 0 ? blk : 0;
-        const int row = KIND == 0 ? nbase + r : nbase + blk * kBlk + r;
+        const int row = KIND == 0 ? nbase + (r & (kBlk - 1)) : nbase + r;
         const bool go = ok_ptrs && row < p.ndim;
-        const int wpr = p.kdim / 8;
-        const int groups = p.kdim >> p.gs_shift;
-        const int32_t* src = reinterpret_cast<const int32_t*>(pe.pk) + p.w_off[m] + int64_t(row) * wpr;
-        const int64_t sidx0 = p.s_off[m] + int64_t(row) * groups;
-        const int64_t zidx0 = p.z_off[m] + int64_t(row >> 3) * groups;
-        const unsigned char* sc_bytes = reinterpret_cast<const unsigned char*>(pe.sc);
-        const unsigned char* zp_bytes = reinterpret_cast<const unsigned char*>(pe.zp);
-        constexpr int kScBytes = SC == VY_F32 ? 4 : 2;
-        // the scale / zero element of stage s sits in the 8-byte word that contains it; streams
-        // hold a multiple of 4 (16-bit) or 2 (32-bit) elements, so that word is inside the stream
+        const uint32_t groups = static_cast<uint32_t>(p.kdim) >> p.gs_shift;
+        const int32_t* src = reinterpret_cast<const int32_t*>(pe.pk) + p.w_off[m] +
+                             int64_t(row) * (p.kdim / 8) + hh * 4;
+        const uint32_t sidx0 = static_cast<uint32_t>(p.s_off[m]) + static_cast<uint32_t>(row) * groups;
+        const uint32_t zidx0 = static_cast<uint32_t>(p.z_off[m]) + static_cast<uint32_t>(row >> 3) * groups;
+        constexpr int kScLog = SC == VY_F32 ? 1 : 2;      // scale elements per 8-byte word: 2 or 4
+        const int gs_shift = p.gs_shift;
+        const int nib = 4 * (row & 7);
+        WordStream<kScLog> scw;
+        WordStream<1> zpw;
+        scw.start(reinterpret_cast<const void*>(pe.sc), sidx0 + (static_cast<uint32_t>(hh * 32) >> gs_shift),
+                  sidx0 + groups - 1, go);
+        if constexpr (ZERO)
+            zpw.start(reinterpret_cast<const void*>(pe.zp), zidx0 + (static_cast<uint32_t>(hh * 32) >> gs_shift),
+                      zidx0 + groups - 1, go);
+        // chunk c = 4 hh + i of tile row r sits at r * 128 + ((c ^ (r & 7)) << 4)
+        uint32_t off[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) off[i] = r * 128 + (((4 * hh + i) ^ (r & 7)) << 4);
+        unsigned char* b_base = reinterpret_cast<unsigned char*>(S.b[0]);
         auto issue = [&](int s) {
-            if (s < nk && go) {
-                cp_async16(&S.pack[s % kPack][0][tid], src + s * 8);
-                cp_async16(&S.pack[s % kPack][1][tid], src + s * 8 + 4);
-                const int64_t grp = (int64_t(s) * kBK) >> p.gs_shift;
-                cp_async8(&S.sz[s % kPack][0][tid], sc_bytes + (((sidx0 + grp) * kScBytes) & ~int64_t(7)));
-                if constexpr (ZERO)
-                    cp_async8(&S.sz[s % kPack][1][tid], zp_bytes + (((zidx0 + grp) * 4) & ~int64_t(7)));
-            }
+            if (s < nk && go) cp_async16(&S.pack[s % kPack][tid], src + s * 8);
             cp_async_commit();
         };
-        const bool two_groups = p.gs_shift == 5;   // group 32: a 64-wide stage spans two groups
-        constexpr int kSubMask = SC == VY_F32 ? 1 : 3;
-        unsigned char* row_base = reinterpret_cast<unsigned char*>(S.b[0]) + tid * 128;
 #pragma unroll
         for (int s = 0; s < kPack - 1; ++s) issue(s);
         for (int s = 0; s < nk; ++s) {
             issue(s + kPack - 1);
+            const uint32_t grp = static_cast<uint32_t>(s * kBK + hh * 32) >> gs_shift;
+            const uint2 sw = scw.at(sidx0 + grp, go);
+            uint2 zw = make_uint2(0u, 0u);
+            if constexpr (ZERO) zw = zpw.at(zidx0 + grp, go);
             cp_async_wait<kPack - 1>();
-            const int slot = s % kBStages;
-            if (s >= kBStages && !mbar_wait(&S.empty_b[slot], ((s / kBStages) - 1) & 1, abort_flag, err)) break;
+            const int slot = s & (kBStages - 1);
+            // warp-uniform decision: a lane that left the loop alone would strand the warp's arrive
+            if (s >= kBStages &&
+                !__all_sync(0xffffffffu, mbar_wait(&S.empty_b[slot], ((s / kBStages) - 1) & 1, abort_flag, err)))
+                break;
             const int ps = s % kPack;
-            const uint4 lo = S.pack[ps][0][tid], hi = S.pack[ps][1][tid];
-            const int64_t grp = (int64_t(s) * kBK) >> p.gs_shift;
-            const uint2 sw = S.sz[ps][0][tid];
-            const int sub = static_cast<int>(sidx0 + grp) & kSubMask;
-            const uint32_t s0 = __byte_perm(scale_bits<ACT, SC>(sw, sub), 0, 0x1010);
-            const uint32_t s1 = two_groups ? __byte_perm(scale_bits<ACT, SC>(sw, sub + 1), 0, 0x1010) : s0;
-            uint32_t b0 = int4_bias_pair<ACT>(8u), b1 = b0;
-            if constexpr (ZERO) {
-                const uint2 zw = S.sz[ps][1][tid];
-                const int zs = static_cast<int>(zidx0 + grp) & 1;
-                const int nib = 4 * (row & 7);
-                b0 = int4_bias_pair<ACT>(((zs ? zw.y : zw.x) >> nib) & 15u);
-                b1 = two_groups ? int4_bias_pair<ACT>(((zs ? zw.x : zw.y) >> nib) & 15u) : b0;
-            }
-            const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-            unsigned char* dst = row_base + slot * (kBN * kBK * 2);
+            const uint4 wv = S.pack[ps][tid];
+            const uint32_t sp = __byte_perm(scale_bits<ACT, SC>(sw, (sidx0 + grp) & ((1u << kScLog) - 1)), 0, 0x1010);
+            uint32_t bp = int4_bias_pair<ACT>(8u);
+            if constexpr (ZERO) bp = int4_bias_pair<ACT>(((((zidx0 + grp) & 1) ? zw.y : zw.x) >> nib) & 15u);
+            const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+            unsigned char* dst = b_base + slot * (kBN * kBK * 2);
 #pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                const uint32_t sp = w < 4 ? s0 : s1, bp = w < 4 ? b0 : b1;
+            for (int w = 0; w < 4; ++w) {
                 uint4 o;
                 o.x = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 0), bp), sp);
                 o.y = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 1), bp), sp);
                 o.z = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 2), bp), sp);
                 o.w = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 3), bp), sp);
-                *reinterpret_cast<uint4*>(dst + ((w ^ (r & 7)) << 4)) = o;
+                *reinterpret_cast<uint4*>(dst + off[w]) = o;
             }
             fence_async_smem();
-            mbar_arrive(&S.full_b[slot]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.full_b[slot]);
         }
         cp_async_wait<0>();
     } else if (warp == kDqThreads / 32 && lane == 0) {
@@ -402,13 +432,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
 
     // ── epilogue: TMEM -> registers -> global.  Warp w reads TMEM lanes 32 (w % 4) .. +31
-    // (its lane quarter) of half w / 4: tile row 128 (w / 4) + 32 (w % 4) + lane ────────────
+    // (its lane quarter) of M half (w / 4) % 2, i.e. tile row 128 ((w / 4) % 2) + 32 (w % 4) +
+    // lane, columns of half w / 8 ──────────────────────────────────────────────────────────────
     if (tid < kDqThreads) {
         // every MMA must be complete before TMEM is read or freed, on the abort path too
         const bool finished = mbar_drain(&S.done, 0, err) && !*abort_flag && ok_ptrs;
         __syncwarp();
         tc_fence_after();
-        const int q = warp & 3, half = warp >> 2;
+        const int q = warp & 3, half = (warp >> 2) & 1, ch = warp >> 3;   // lane quarter, M half, column half
         const int m_row = half * kBM + q * 32 + lane;
         const uint32_t lane_addr = tmem + (uint32_t(q * 32) << 16) + half * kBN;
         const bool live = m_row < pe.ncols;
@@ -416,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         if (half == 0 || two) {                           // warp-uniform
             if constexpr (KIND == 0) {
 #pragma unroll 1
-                for (int c = 0; c < kBlk; c += 16) {
+                for (int c = ch * (kBlk / 2); c < (ch + 1) * (kBlk / 2); c += 16) {
                     uint32_t gr[16], ur[16];
                     tmem_ld16(lane_addr + c, gr);
                     tmem_ld16(lane_addr + kBlk + c, ur);
@@ -460,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                 }
                 const int ncol = min(kBN, p.ndim - nbase);   // 128 or 256: warp-uniform
 #pragma unroll 1
-                for (int c = 0; c < ncol; c += 16) {
+                for (int c = ch * kBlk; c < min(ncol, (ch + 1) * kBlk); c += 16) {
                     uint32_t yr[16];
                     tmem_ld16(lane_addr + c, yr);
                     if (finished && live) {
@@ -604,26 +635,27 @@ int launch_gemm(const CUtensorMap& map, const GemmParams& gp, int max_tiles, cud
     return VY_OK;
 }
 
-template <int ACT, int SC, bool ZERO>
-int run_prefill_gemms(const CUtensorMap& ma, const GemmParams& g1, const CUtensorMap& mh, const GemmParams& g2,
-                      int max_tiles, cudaStream_t s) {
-    int st = launch_gemm<ACT, SC, ZERO, 0>(ma, g1, max_tiles, s);
-    if (st != VY_OK) return st;
-    return launch_gemm<ACT, SC, ZERO, 1>(mh, g2, max_tiles, s);
-}
-
 template <int ACT>
-int dispatch_prefill(int sc, bool zero, const CUtensorMap& ma, const GemmParams& g1, const CUtensorMap& mh,
-                     const GemmParams& g2, int max_tiles, cudaStream_t s) {
-#define VY_PF(SCV)                                                                                \
-    return zero ? run_prefill_gemms<ACT, SCV, true>(ma, g1, mh, g2, max_tiles, s)                 \
-                : run_prefill_gemms<ACT, SCV, false>(ma, g1, mh, g2, max_tiles, s);
+int dispatch_gemm(int kind, int sc, bool zero, const CUtensorMap& map, const GemmParams& gp, int max_tiles,
+                  cudaStream_t s) {
+#define VY_PF(SCV)                                                                                   \
+    if (kind == 0)                                                                                   \
+        return zero ? launch_gemm<ACT, SCV, true, 0>(map, gp, max_tiles, s)                          \
+                    : launch_gemm<ACT, SCV, false, 0>(map, gp, max_tiles, s);                        \
+    return zero ? launch_gemm<ACT, SCV, true, 1>(map, gp, max_tiles, s)                              \
+                : launch_gemm<ACT, SCV, false, 1>(map, gp, max_tiles, s);
     switch (sc) {
         case VY_BF16: VY_PF(VY_BF16)
         case VY_F16: VY_PF(VY_F16)
         default: VY_PF(VY_F32)
     }
 #undef VY_PF
+}
+
+int launch_prefill_gemm(int act, int kind, int sc, bool zero, const CUtensorMap& map, const GemmParams& gp,
+                        int max_tiles, cudaStream_t s) {
+    return act == VY_BF16 ? dispatch_gemm<VY_BF16>(kind, sc, zero, map, gp, max_tiles, s)
+                          : dispatch_gemm<VY_F16>(kind, sc, zero, map, gp, max_tiles, s);
 }
 
 }  // namespace
@@ -675,6 +707,10 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
     pa.tok_per_unit = kUnit;
     pa.expert_table = c->expert_table;
     pa.passes = L.passes;
+    cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
+    const bool timed = ev != nullptr && c->n_stage_events >= 4;
+    if (timed && cudaEventRecord(ev[0], s) != cudaSuccess)
+        return fail(VY_ERR_INVALID, "stage_events[0] is not a usable cudaEvent_t");
     if ((st = launch_plan(pa, dev->sm_count, s)) != VY_OK) return st;
 
     GatherParams gp{c->x, c->x_row_stride, g.hidden, c->top_k, L.order, L.live_start, L.counters, L.x_sorted};
@@ -732,11 +768,17 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
 
     const int max_tiles = static_cast<int>(L.max_tiles);
     const bool zero = g.has_zero != 0;
-    st = c->act_dtype == VY_BF16
-             ? dispatch_prefill<VY_BF16>(g.scale_dtype, zero, map_x, g1, map_h, g2, max_tiles, s)
-             : dispatch_prefill<VY_F16>(g.scale_dtype, zero, map_x, g1, map_h, g2, max_tiles, s);
-    if (st != VY_OK) return st;
-    if (c->contrib) return check_launch("vy_moe_prefill");
+    if (timed) cudaEventRecord(ev[1], s);
+    if ((st = launch_prefill_gemm(c->act_dtype, 0, g.scale_dtype, zero, map_x, g1, max_tiles, s)) != VY_OK)
+        return st;
+    if (timed) cudaEventRecord(ev[2], s);
+    if ((st = launch_prefill_gemm(c->act_dtype, 1, g.scale_dtype, zero, map_h, g2, max_tiles, s)) != VY_OK)
+        return st;
+    if (timed && c->n_stage_events >= 5) cudaEventRecord(ev[4], s);
+    if (c->contrib) {
+        if (timed) cudaEventRecord(ev[3], s);
+        return check_launch("vy_moe_prefill");
+    }
     {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(static_cast<unsigned>((g.hidden / 4 + 255) / 256),
@@ -753,5 +795,6 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
                                            g.hidden, c->out, c->out_row_stride);
         if (e != cudaSuccess) return fail(VY_ERR_CUDA, "combine launch: %s", cudaGetErrorString(e));
     }
+    if (timed) cudaEventRecord(ev[3], s);
     return check_launch("vy_moe_prefill");
 }
