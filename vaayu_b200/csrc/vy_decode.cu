@@ -634,13 +634,14 @@ struct DecodeLayout {
 // can have is n_tokens; empty blocks are skipped at run time, so NB only costs registers.
 int nb_for(int64_t n_tokens) { return n_tokens <= 32 ? 1 : (n_tokens <= 64 ? 2 : 4); }
 
-// CTAs per down-projection row tile: enough for ~2 resident CTAs per SM, but no more chunks
-// than the call can have live experts per warp.
+// CTAs per down-projection row tile: as many as keep the whole grid resident at once (two CTAs
+// per SM; a grid a fraction of a wave larger runs a second, mostly empty wave), but no more
+// chunks than the call can have live experts per warp.
 int down_chunks(const vy_moe_call* c, int sm_count) {
     const int64_t n = c->n_tokens * c->top_k;
     const int n_tiles = c->geom->hidden / kTileRows;
     const int64_t max_live = n < c->n_experts ? n : c->n_experts;
-    int chunks = (2 * sm_count + n_tiles - 1) / n_tiles;
+    int chunks = (2 * sm_count) / n_tiles;
     const int cap = static_cast<int>((max_live + kWarps - 1) / kWarps);
     if (chunks > cap) chunks = cap;
     return chunks < 1 ? 1 : chunks;

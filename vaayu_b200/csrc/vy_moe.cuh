@@ -49,6 +49,10 @@ struct PlanArgs {
 size_t plan_smem_bytes(int n_experts);
 int plan_validate(int64_t n_tokens, int top_k, int n_experts);
 int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream);
+// out[t] = sum of contrib rows slot_order[t*top_k .. +top_k) (row ids, -1 = none), fp32, in
+// that order; launched with programmatic stream serialisation.
+int launch_slot_combine(const float* contrib, const int32_t* slot_order, int64_t n_tokens, int top_k, int hidden,
+                        float* out, int64_t out_stride, cudaStream_t s);
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
                    cudaStream_t stream);

@@ -520,33 +520,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
 }
 
-// out[t] = token t's contributions in the plan's slot order (ascending expert id, then slot;
-// dropped rows are -1 and add nothing), fp32.
-__global__ void __launch_bounds__(256) slot_combine_kernel(const float* __restrict__ contrib,
-                                                           const int32_t* __restrict__ slot_order,
-                                                           int64_t n_tokens, int top_k, int hidden,
-                                                           float* out, int64_t out_stride) {
-    grid_dependency_wait();
-    for (int64_t t = blockIdx.y; t < n_tokens; t += gridDim.y)
-    for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < hidden; c += gridDim.x * blockDim.x * 4) {
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = 0; k < top_k; ++k) {
-            const int row = slot_order[t * top_k + k];
-            if (row < 0) continue;
-            const float4 v = *reinterpret_cast<const float4*>(contrib + int64_t(row) * hidden + c);
-            a.x += v.x;
-            a.y += v.y;
-            a.z += v.z;
-            a.w += v.w;
-        }
-        float* o = out + t * out_stride + c;
-        o[0] = a.x;
-        o[1] = a.y;
-        o[2] = a.z;
-        o[3] = a.w;
-    }
-}
-
 // ── host ────────────────────────────────────────────────────────────────────────────────────
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -779,22 +752,9 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
         if (timed) cudaEventRecord(ev[3], s);
         return check_launch("vy_moe_prefill");
     }
-    {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(static_cast<unsigned>((g.hidden / 4 + 255) / 256),
-                           static_cast<unsigned>(c->n_tokens < 65535 ? c->n_tokens : 65535));
-        cfg.blockDim = dim3(256);
-        cfg.stream = s;
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, slot_combine_kernel, static_cast<const float*>(L.contrib),
-                                           static_cast<const int32_t*>(L.slot_order), c->n_tokens, c->top_k,
-                                           g.hidden, c->out, c->out_row_stride);
-        if (e != cudaSuccess) return fail(VY_ERR_CUDA, "combine launch: %s", cudaGetErrorString(e));
-    }
+    if ((st = launch_slot_combine(L.contrib, L.slot_order, c->n_tokens, c->top_k, g.hidden, c->out,
+                                  c->out_row_stride, s)) != VY_OK)
+        return st;
     if (timed) cudaEventRecord(ev[3], s);
     return check_launch("vy_moe_prefill");
 }

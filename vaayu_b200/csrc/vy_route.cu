@@ -482,6 +482,51 @@ int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream) {
     return check_launch("routing plan");
 }
 
+// out[t] = token t's contributions in the plan's slot order (ascending expert id, then slot;
+// dropped rows are -1 and add nothing), fp32.
+__global__ void __launch_bounds__(256) slot_combine_kernel(const float* __restrict__ contrib,
+                                                           const int32_t* __restrict__ slot_order,
+                                                           int64_t n_tokens, int top_k, int hidden,
+                                                           float* out, int64_t out_stride) {
+    grid_dependency_wait();
+    for (int64_t t = blockIdx.y; t < n_tokens; t += gridDim.y)
+    for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < hidden; c += gridDim.x * blockDim.x * 4) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = 0; k < top_k; ++k) {
+            const int row = slot_order[t * top_k + k];
+            if (row < 0) continue;
+            const float4 v = *reinterpret_cast<const float4*>(contrib + int64_t(row) * hidden + c);
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
+        }
+        float* o = out + t * out_stride + c;
+        o[0] = a.x;
+        o[1] = a.y;
+        o[2] = a.z;
+        o[3] = a.w;
+    }
+}
+
+int launch_slot_combine(const float* contrib, const int32_t* slot_order, int64_t n_tokens, int top_k, int hidden,
+                        float* out, int64_t out_stride, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((hidden / 4 + 255) / 256),
+                       static_cast<unsigned>(n_tokens < 65535 ? n_tokens : 65535));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, slot_combine_kernel, contrib, slot_order, n_tokens, top_k, hidden,
+                                       out, out_stride);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "combine launch: %s", cudaGetErrorString(e));
+    return VY_OK;
+}
+
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
                    cudaStream_t stream) {
