@@ -19,10 +19,11 @@ __device__ __forceinline__ int load_id(const void* ids, bool ids64, int64_t j) {
     return reinterpret_cast<const int32_t*>(ids)[j];
 }
 
-// Exclusive scan of one int per thread over the block; returns this thread's prefix and puts
-// the total in *total.  `scratch` holds kPlanWarps + 1 ints.
+// Exclusive scan of one int per thread over the block (any whole number of warps up to
+// kPlanWarps); returns this thread's prefix and puts the total in *total.  `scratch` holds
+// kPlanWarps + 1 ints.
 __device__ int block_exclusive_scan(int v, int* scratch, int* total) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     int x = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -32,14 +33,14 @@ __device__ int block_exclusive_scan(int v, int* scratch, int* total) {
     if (lane == 31) scratch[warp] = x;
     __syncthreads();
     if (warp == 0) {
-        int w = lane < kPlanWarps ? scratch[lane] : 0;
+        int w = lane < nw ? scratch[lane] : 0;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             int y = __shfl_up_sync(0xffffffffu, w, o);
             if (lane >= o) w += y;
         }
-        if (lane < kPlanWarps) scratch[lane] = w;   // inclusive prefix of warp sums
-        if (lane == kPlanWarps - 1) scratch[kPlanWarps] = w;
+        if (lane < nw) scratch[lane] = w;   // inclusive prefix of warp sums
+        if (lane == nw - 1) scratch[kPlanWarps] = w;
     }
     __syncthreads();
     int base = warp > 0 ? scratch[warp - 1] : 0;
@@ -76,16 +77,16 @@ __device__ __forceinline__ void write_slot_order(const PlanArgs& p, const int* i
 
 // Sorted position `pos` of a live expert's run (run start `ls`, length `count`, first pass
 // `ustart`, expert `e`) holds row `row`: file it in the pass table.
-__device__ __forceinline__ void file_pass_row(const PlanArgs& p, int e, int ls, int count, int ustart,
-                                              int pos, int row) {
+__device__ __forceinline__ void file_pass_row(const PlanArgs& p, const int64_t* table, int e, int ls, int count,
+                                              int ustart, int pos, int row) {
     if (!p.passes) return;
     const int tpu = p.tok_per_unit, r = pos - ls, q = r / tpu, col = r - q * tpu;
     PassEntry& pe = p.passes[ustart + q];
     if (col < kMaxPassCols) pe.rows[col] = row;   // row ids are kept for GEMV-sized passes only
     if (col == 0) {
-        pe.pk = p.expert_table[3 * e];
-        pe.sc = p.expert_table[3 * e + 1];
-        pe.zp = p.expert_table[3 * e + 2];
+        pe.pk = table[3 * e];
+        pe.sc = table[3 * e + 1];
+        pe.zp = table[3 * e + 2];
         pe.row0 = pos;
         pe.ncols = min(tpu, count - q * tpu);
     }
@@ -96,8 +97,11 @@ __device__ void plan_small(const PlanArgs& p) {
     __shared__ int keys[kSmallPlan];
     __shared__ int ls[kSmallPlan + 1];
     __shared__ int scratch[kPlanWarps + 1];
+    __shared__ int64_t table[3 * kMaxExperts];   // the expert pointer table, read while sorting
     const int n = static_cast<int>(p.n_tokens * p.top_k), tid = threadIdx.x, E = p.n_experts;
     const int lane = tid & 31;
+    if (p.passes)
+        for (int i = tid; i < 3 * E; i += blockDim.x) table[i] = p.expert_table[i];
     int e = -1;
     if (tid < n) {
         e = load_id(p.ids, p.ids64, tid);
@@ -107,8 +111,8 @@ __device__ void plan_small(const PlanArgs& p) {
     int key = (tid < n && e >= 0) ? ((e << 10) | tid) : kKeyNone;
     const int tpu = p.tok_per_unit;
     if (n <= 32) {
+        __syncthreads();                         // ids[] and table[] in place
         if (tid >= 32) return;
-        __syncwarp();
         for (int k = 2; k <= 32; k <<= 1)
             for (int j = k >> 1; j > 0; j >>= 1) key = warp_sort_step(key, lane, k, j);
         const bool valid = key != kKeyNone;
@@ -139,7 +143,7 @@ __device__ void plan_small(const PlanArgs& p) {
             const int run_start = valid ? (31 - __clz(upto)) : 0;
             const int rend = __shfl_sync(0xffffffffu, run_end, run_start);
             const int ust = __shfl_sync(0xffffffffu, incl - units, run_start);
-            if (valid) file_pass_row(p, ek, run_start, rend - run_start, ust, lane, key & 1023);
+            if (valid) file_pass_row(p, table, ek, run_start, rend - run_start, ust, lane, key & 1023);
         }
         const int n_live = __popc(fm), total_units = __shfl_sync(0xffffffffu, incl, 31);
         if (lane == 0) {
@@ -196,7 +200,7 @@ __device__ void plan_small(const PlanArgs& p) {
         keys[tid] = ustart;                       // keys[] is free now: per-live-expert first pass
         __syncthreads();
         const int run = li + (first ? 1 : 0) - 1; // this position's live index
-        if (valid) file_pass_row(p, ek, ls[run], ls[run + 1] - ls[run], keys[run], tid, key & 1023);
+        if (valid) file_pass_row(p, table, ek, ls[run], ls[run + 1] - ls[run], keys[run], tid, key & 1023);
     }
     if (tid == 0) {
         p.counters[0] = n_live;
@@ -329,7 +333,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
                 else hi = mid - 1;
             }
             const int ls0 = p.live_start[lo];
-            file_pass_row(p, p.live_expert[lo], ls0, p.live_start[lo + 1] - ls0, p.unit_start[lo],
+            file_pass_row(p, p.expert_table, p.live_expert[lo], ls0, p.live_start[lo + 1] - ls0, p.unit_start[lo],
                           static_cast<int>(pos), p.order[pos]);
         }
     }
@@ -472,13 +476,21 @@ int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream) {
                              static_cast<int>(plan_smem_bytes(kMaxExperts)));
         configured = true;
     }
+    // a decode-sized plan sorts with as many threads as the next power of two of its rows (the
+    // fewer warps, the cheaper every block barrier); the counting sort takes the full block
+    const int64_t n = p.n_tokens * p.top_k;
+    int threads = kPlanThreads;
+    if (n <= kSmallPlan) {
+        threads = 64;
+        while (threads < n) threads <<= 1;
+    }
     int perm_blocks = 0;
     if (p.x_perm) {
         int64_t groups = p.n_tokens * (p.hidden / 8);
-        int64_t b = (groups + kPlanThreads - 1) / kPlanThreads;
+        int64_t b = (groups + threads - 1) / threads;
         perm_blocks = static_cast<int>(b < 4 * sm_count ? b : 4 * sm_count);
     }
-    plan_kernel<<<1 + perm_blocks, kPlanThreads, smem, stream>>>(p);
+    plan_kernel<<<1 + perm_blocks, threads, smem, stream>>>(p);
     return check_launch("routing plan");
 }
 
