@@ -70,7 +70,7 @@ def _worker(rank, port, result_dir):
             uneven_refused = False
         except ValueError:
             uneven_refused = True
-        layer = ExpertParallelLayer(None, E, compute=compute, combine_fn=combine, hidden=H)
+        layer = ExpertParallelLayer(None, E, compute=compute, combine_fn=combine, hidden=H, mode="dispatch")
         x, ids, w = toks[rank]
         got = layer.forward(x, ids, w)
         ref = O.moe_layer(_geom(), experts, TH.to_np(x), O.BF16, ids.numpy(), w.numpy(), O.F32, O.F16)
@@ -81,9 +81,75 @@ def _worker(rank, port, result_dir):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_equals_one_process_bit_for_bit(tmp_path):
+def test_dispatch_mode_equals_one_process_bit_for_bit(tmp_path):
     mp.spawn(_worker, args=(_free_port(), str(tmp_path)), nprocs=2, join=True)
     for r in range(2):
         ok, err, uneven_refused = np.load(tmp_path / f"rank{r}.npy")
         assert ok, f"rank {r}: max |diff| {err}"
         assert uneven_refused, "7 experts over 2 ranks must be refused"
+
+
+# ── replicate mode: all-gathered tokens, per-rank partial sums, rank-ordered combine ──────────
+
+def _partials(local_experts, xa, local, wa):
+    """Per-token fp32 sum of the local slots' contributions, ascending local expert id then slot."""
+    from oracle import oracle as O
+    from tests import helpers as TH
+    local = np.asarray(local)
+    out = np.zeros((local.shape[0], H), np.float32)
+    rows = [(t, k) for t in range(local.shape[0]) for k in range(local.shape[1]) if local[t, k] >= 0]
+    if not rows:
+        return out
+    xr = TH.to_np(xa)[[t for t, _ in rows]]
+    ids = np.array([[local[t, k]] for t, k in rows], np.int64)
+    ws = np.array([float(wa[t, k]) for t, k in rows], np.float32)
+    _o, y = O.moe_layer(_geom(), local_experts, xr, O.BF16, ids, ws, O.F32, O.F16, want_y=True)
+    by_tok = {}
+    for i, (t, k) in enumerate(rows):
+        by_tok.setdefault(t, []).append((int(local[t, k]), k, i))
+    for t, lst in by_tok.items():
+        for _e, _k, i in sorted(lst):
+            out[t] = (out[t] + y[i]).astype(np.float32)
+    return out
+
+
+def _replicate_worker(rank, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        from oracle import oracle as O
+        from tests import helpers as TH
+        from vaayu_b200.ep import ExpertParallelLayer
+        experts, toks = _setup()
+        per = E // 2
+        local_experts = experts[rank * per:(rank + 1) * per]
+        layer = ExpertParallelLayer(None, E, hidden=H, mode="replicate",
+                                    layer_fn=lambda xa, lo, wa: torch.from_numpy(_partials(local_experts, xa, lo, wa)))
+        x, ids, w = toks[rank]
+        got = layer.forward(x, ids, w).numpy()
+        again = layer.forward(x, ids, w).numpy()
+        # the expectation in one process: each rank's partial over this rank's tokens, summed in
+        # rank order
+        exp = np.zeros((T, H), np.float32)
+        for q in range(2):
+            lo = ids.numpy() - q * per
+            lo = np.where((lo >= 0) & (lo < per), lo, -1)
+            part = _partials(experts[q * per:(q + 1) * per], x, lo, w.numpy())
+            exp = part.copy() if q == 0 else (exp + part).astype(np.float32)
+        full = O.moe_layer(_geom(), experts, TH.to_np(x), O.BF16, ids.numpy(), w.numpy(), O.F32, O.F16)
+        np.save(os.path.join(result_dir, f"rep{rank}.npy"),
+                np.array([np.array_equal(got, exp), np.array_equal(got, again),
+                          float(np.abs(got - full).max() / (np.sqrt(np.mean(full ** 2)) + 1e-30))]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_replicate_mode_is_the_rank_ordered_sum_of_per_rank_partials(tmp_path):
+    """Exact: (rank 0's slots summed in ascending id) + (rank 1's ...), deterministic across
+    calls, and within fp32 rounding of the single-process layer."""
+    mp.spawn(_replicate_worker, args=(_free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        exact, repeat, rel = np.load(tmp_path / f"rep{r}.npy")
+        assert exact, f"rank {r}: not the rank-ordered partial sum"
+        assert repeat, f"rank {r}: two calls differ"
+        assert rel < 1e-5, f"rank {r}: {rel} of RMS from the single-process layer"

@@ -3,7 +3,24 @@ tokens dispatched to the ranks that hold their routed experts and combined back 
 home rank.
 
 Layout: rank r holds the contiguous expert range [r * E/P, (r+1) * E/P) as a resident
-`ExpertTable`; tokens start sharded (each rank owns its own batch).  One layer call:
+`ExpertTable`; tokens start sharded (each rank owns its own batch).  Two exchange modes:
+
+"replicate" (decode-sized batches; no host synchronisation, two collectives):
+
+  1. every rank's tokens -- activations, expert ids, routing weights, packed into one byte row
+     per token -- are all-gathered (NCCL over NVLink);
+  2. each rank runs the local kernels over all P*T tokens with only its own experts' slots kept
+     (the others become -1, which the routing plan drops): per token the fp32 sum of its local
+     contributions in ascending expert id (`moe_forward`'s own combine);
+  3. the per-token partial sums go back to the tokens' home ranks with one equal-split
+     all-to-all;
+  4. the home rank adds the P partials in rank order -- ascending expert ranges.
+
+  The result is deterministic and independent of arrival order; it groups the fp32 sum by rank
+  ((sum of rank 0's slots) + (sum of rank 1's slots) + ...), so it agrees with the single-GPU
+  layer to fp32 rounding, not bit for bit.
+
+"dispatch" (large batches, where replicating every token to every rank would move too much):
 
   1. every (token, slot) row is addressed to the rank owning its expert; the per-destination row
      counts cross with one all-to-all (and come to the host: they size the variable exchange);
@@ -17,7 +34,7 @@ Layout: rank r holds the contiguous expert range [r * E/P, (r+1) * E/P) as a res
      (`combine`) -- `accumulate_expert_outputs`' order (vaayu/moe_patch.py:914-940).
 
 A row's contribution does not depend on the rows it is computed with, and step 5 is the same fp32
-sum in the same order as on one GPU, so the expert-parallel result equals the single-GPU result
+sum in the same order as on one GPU, so the dispatch-mode result equals the single-GPU result
 bit for bit.  The reference is single-GPU; this module has no counterpart there.
 """
 from __future__ import annotations
@@ -33,13 +50,25 @@ class ExpertParallelLayer:
 
     local_blobs   the blobs of this rank's experts, in global id order
     n_experts     the layer's total expert count (divisible by the world size)
+    mode          "replicate", "dispatch" or "auto" (replicate when every rank's batch is at most
+                  `replicate_max_tokens` tokens)
     compute       optional (x_rows, local_ids [R,1], w_rows [R,1]) -> contributions [R, H] fp32;
-                  default: the CUDA kernels over this rank's `ExpertTable`
+                  dispatch mode; default: the CUDA kernels over this rank's `ExpertTable`
     combine_fn    optional (contrib [T*K, H], global ids [T, K]) -> out [T, H]; default `combine`
+    layer_fn      optional (x [N, H], local ids [N, K] with -1 for other ranks' slots, w [N, K])
+                  -> per-token partial sums [N, H] fp32; replicate mode; default: the CUDA kernels
     """
 
     def __init__(self, local_blobs, n_experts: int, group=None, compute: Optional[Callable] = None,
-                 combine_fn: Optional[Callable] = None, hidden: Optional[int] = None):
+                 combine_fn: Optional[Callable] = None, hidden: Optional[int] = None,
+                 mode: str = "auto", replicate_max_tokens: int = 256,
+                 layer_fn: Optional[Callable] = None):
+        if mode not in ("auto", "replicate", "dispatch"):
+            raise ValueError(f"mode {mode!r}")
+        self.mode = mode
+        self.replicate_max_tokens = replicate_max_tokens
+        self._layer_fn = layer_fn
+        self._bufs = {}
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -51,7 +80,7 @@ class ExpertParallelLayer:
         self._compute = compute
         self._combine = combine_fn
         self.table = None
-        if compute is None:
+        if compute is None and layer_fn is None:
             from .packed_expert_kernels import ExpertTable
             self.table = ExpertTable(local_blobs)
             self.hidden = self.table.hidden
@@ -110,8 +139,72 @@ class ExpertParallelLayer:
         rows[order] = back                                       # (token, slot) order again
         return rows
 
+    # ── replicate mode ───────────────────────────────────────────────────────────────────
+    def _buffers(self, T, K, x, weights):
+        key = (T, K, x.dtype, weights.dtype, x.device)
+        b = self._bufs.get(key)
+        if b is None:
+            H = x.shape[1]
+            xb, wb = 2 * H, weights.element_size() * K
+            row = xb + 4 * K + wb
+            row += (-row) % 16                       # 16-byte rows: the activation views stay aligned
+            P = self.world
+            ws = None
+            if self.table is not None:
+                from .packed_expert_kernels import PATH_DECODE, moe_workspace_bytes
+                ws = torch.empty(moe_workspace_bytes(self.table, P * T, K, path=PATH_DECODE),
+                                 dtype=torch.uint8, device=x.device)
+            b = dict(row=row, xb=xb, wb=wb, ws=ws,
+                     send=torch.empty(T, row, dtype=torch.uint8, device=x.device),
+                     recv=torch.empty(P * T, row, dtype=torch.uint8, device=x.device),
+                     partial=torch.empty(P * T, H, dtype=torch.float32, device=x.device),
+                     back=torch.empty(P, T, H, dtype=torch.float32, device=x.device))
+            self._bufs[key] = b
+        return b
+
+    def replicate_forward(self, x, ids, weights, out=None):
+        """out [T, hidden] fp32: replicate mode (see the module docstring)."""
+        T, K = ids.shape
+        H = x.shape[1]
+        P = self.world
+        b = self._buffers(T, K, x, weights)
+        send, recv, partial, back = b["send"], b["recv"], b["partial"], b["back"]
+        xb, wb = b["xb"], b["wb"]
+        send[:, :xb].view(x.dtype).copy_(x)
+        send[:, xb:xb + 4 * K].view(torch.int32).copy_(ids)
+        send[:, xb + 4 * K:xb + 4 * K + wb].view(weights.dtype).copy_(weights.reshape(T, K))
+        if P == 1:
+            recv.copy_(send)
+        else:
+            dist.all_gather_into_tensor(recv, send, group=self.group)
+        xa = recv[:, :xb].view(x.dtype)
+        ga = recv[:, xb:xb + 4 * K].view(torch.int32)
+        wa = recv[:, xb + 4 * K:xb + 4 * K + wb].view(weights.dtype)
+        local = ga - self.lo
+        local = torch.where((local >= 0) & (local < self.per_rank), local, torch.full_like(local, -1))
+        if self._layer_fn is not None:
+            partial.copy_(self._layer_fn(xa, local, wa))
+        else:
+            from .packed_expert_kernels import PATH_DECODE, moe_forward
+            moe_forward(xa, local, wa, self.table, out=partial, path=PATH_DECODE, workspace=b["ws"])
+        if P == 1:
+            back[0].copy_(partial)
+        else:
+            dist.all_to_all_single(back.view(P * T, H), partial, group=self.group)
+        if out is None:
+            out = torch.empty(T, H, dtype=torch.float32, device=x.device)
+        out.copy_(back[0])
+        for r in range(1, P):          # rank order: ascending expert ranges, one fp32 add each
+            out.add_(back[r])
+        return out
+
     def forward(self, x, ids, weights, out=None):
         """out [T, hidden] fp32 for this rank's tokens: ids are GLOBAL expert ids [T, K]."""
+        mode = self.mode
+        if mode == "auto":
+            mode = "replicate" if ids.shape[0] <= self.replicate_max_tokens else "dispatch"
+        if mode == "replicate":
+            return self.replicate_forward(x, ids, weights, out)
         recv_x, recv_ids, recv_w, plan = self.dispatch(x, ids, weights)
         contrib = self.compute(recv_x, recv_ids, recv_w)
         rows = self.gather_back(contrib, plan)
@@ -142,9 +235,36 @@ def run_bench(args, rank, world, local, wl):
     out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
     L = args.layers
 
+    # each layer's step (pack, all-gather, kernels, all-to-all, combine) as one CUDA graph over
+    # static input buffers; eager calls when capture is not possible here
+    xs = [b[0].clone() for b in batches]
+    ws_ = [b[1].clone() for b in batches]
+    ids_ = [b[2].clone() for b in batches]
+    graphs = []
+    for l in range(L):
+        for _ in range(2):
+            layers[l].forward(xs[l], ids_[l], ws_[l], out)
+    torch.cuda.synchronize(device)
+    bench.barrier(world)
+    try:
+        for l in range(L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                layers[l].forward(xs[l], ids_[l], ws_[l], out)
+            graphs.append(g)
+        torch.cuda.synchronize(device)
+    except Exception as e:  # noqa: BLE001 - report and run eagerly
+        graphs = []
+        if rank == 0:
+            print(f"# EP graph capture unavailable, eager steps: {e}", flush=True)
+    bench.barrier(world)
+
     def step(i):
-        x, w, idx = batches[i % L]
-        layers[i % L].forward(x, idx, w, out)
+        l = i % L
+        if graphs:
+            graphs[l].replay()
+        else:
+            layers[l].forward(xs[l], ids_[l], ws_[l], out)
 
     for i in range(args.warmup):
         step(i)
@@ -155,15 +275,18 @@ def run_bench(args, rank, world, local, wl):
     ms = bench.max_over_ranks(ms, world)
 
     pin = [(x.cpu().pin_memory(), w.cpu().pin_memory(), i.cpu().pin_memory()) for x, w, i in batches]
-    dx, dw, di = (torch.empty_like(t) for t in batches[0])
     out_h = torch.empty(T, wl["hidden"], dtype=torch.float32).pin_memory()
 
     def e2e_step(i):
-        xh, wh, ih = pin[i % L]
-        dx.copy_(xh, non_blocking=True)
-        dw.copy_(wh, non_blocking=True)
-        di.copy_(ih, non_blocking=True)
-        layers[i % L].forward(dx, di, dw, out)
+        l = i % L
+        xh, wh, ih = pin[l]
+        xs[l].copy_(xh, non_blocking=True)
+        ws_[l].copy_(wh, non_blocking=True)
+        ids_[l].copy_(ih, non_blocking=True)
+        if graphs:
+            graphs[l].replay()
+        else:
+            layers[l].forward(xs[l], ids_[l], ws_[l], out)
         out_h.copy_(out, non_blocking=True)
 
     for i in range(args.warmup):
@@ -171,7 +294,10 @@ def run_bench(args, rank, world, local, wl):
     bench.barrier(world)
     e2e_ms = bench.max_over_ranks(bench.time_steps(e2e_step, args.steps, device), world)
     bench.barrier(world)
-    h2d = sum(t.numel() * t.element_size() for t in (dx, dw, di))
+    h2d = sum(t.numel() * t.element_size() for t in (xs[0], ws_[0], ids_[0]))
+    used_graphs = bool(graphs)
+    del graphs               # graphs holding NCCL calls go before the process group does
+    torch.cuda.synchronize(device)
     uniq = statistics.mean(len(set(b[2].reshape(-1).tolist())) for b in batches)
     peak, peak_kind = bench.hbm_peak()
     if rank == 0:
@@ -185,8 +311,10 @@ def run_bench(args, rank, world, local, wl):
                        "expert_intermediate": wl["inter"], "experts": E, "top_k": K,
                        "tokens_per_gpu": T, "group_size": wl["group"], "layers_rotated": L,
                        "l2": "inputs larger than L2 (each layer's expert weights exceed 126 MB per step)",
-                       "parallelism": f"ep{world}: {per} experts per GPU, NCCL all-to-all dispatch "
-                                      f"and combine", "routed_experts_per_rank_batch": uniq},
+                       "parallelism": f"ep{world}: {per} experts per GPU; replicate mode: one NCCL "
+                                      f"all-gather of the tokens, one all-to-all of per-token partial "
+                                      f"sums, rank-ordered combine",
+                       "routed_experts_per_rank_batch": uniq, "cuda_graphs": used_graphs},
             "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * 4,
                     "ms_per_step": e2e_ms},
