@@ -275,6 +275,53 @@ def prefill_bench(args, device):
     }
 
 
+def block_scaled_bench(args, device):
+    """Configuration 4: FP8-e4m3 [4096, 14336] with an fp32 scale per 128 x 128 block and NVFP4
+    (e2m1, an e4m3 scale per 16) of the same shape, each dequantised to bf16 and fused into a
+    decode GEMV at batch 1 and 16.  Two weight copies rotate so every call reads from HBM."""
+    from vaayu_b200 import block_scaled as bs
+    N, K = 4096, 14336
+    g = torch.Generator(device=device).manual_seed(4)
+    fp8, fp4 = [], []
+    for _ in range(2):
+        w = torch.randn(N, K, generator=g, device=device)
+        amax = w.abs().reshape(N // 128, 128, K // 128, 128).amax(dim=(1, 3)).clamp_min(1e-6)
+        scale = (amax / 448.0).float()
+        q = (w / scale.repeat_interleave(128, 0).repeat_interleave(128, 1)).to(torch.float8_e4m3fn)
+        fp8.append((q, scale))
+        codes = torch.randint(0, 256, (N, K // 2), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+        sc = (torch.rand(N, K // 16, generator=g, device=device) * 2 + 0.25).to(torch.float8_e4m3fn)
+        fp4.append((codes, sc))
+        del w, q
+    peak, src = hbm_peak()
+    steps = max(5, min(args.steps, 20))
+    res = {}
+
+    def timed(fn, nbytes):
+        for i in range(3):
+            fn(i)
+        ms = time_steps(fn, steps, device)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        return {"ms": ms, "GBps": gbs, "frac": gbs / peak}
+
+    out_bytes = N * K * 2
+    res["fp8_dequant"] = timed(lambda i: bs.dequantize_block_scaled(*fp8[i % 2]),
+                               N * K + fp8[0][1].numel() * 4 + out_bytes)
+    res["fp4_dequant"] = timed(lambda i: bs.dequantize_fp4_block_scaled(*fp4[i % 2]),
+                               N * K // 2 + N * K // 16 + out_bytes)
+    for t in (1, 16):
+        x = torch.randn(t, K, generator=g, device=device).to(torch.bfloat16)
+        o = torch.empty(t, N, dtype=torch.bfloat16, device=device)
+        res[f"fp8_gemv_T{t}"] = timed(lambda i: bs.fp8_gemv(x, *fp8[i % 2], out=o),
+                                      N * K + fp8[0][1].numel() * 4 + t * (K + N) * 2)
+        res[f"fp4_gemv_T{t}"] = timed(lambda i: bs.fp4_gemv(x, *fp4[i % 2], out=o),
+                                      N * K // 2 + N * K // 16 + t * (K + N) * 2)
+    return {"workload": "cfg4: block-scaled FP8 / NVFP4 [4096, 14336] dequant and decode GEMV",
+            "bound": "hbm", "peak_GBps": peak, "peak_source": src,
+            "bytes": "weights + scales read, bf16 output written (dequant) / x read, out written (GEMV)",
+            "steps": steps, "results": res, "gpu_launches": 6 * steps}
+
+
 def time_steps(fn, steps, device):
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -401,6 +448,7 @@ def run_ours(args, rank, world, local):
     del layers, batches
     torch.cuda.empty_cache()
     prefill = prefill_bench(args, device) if not args.no_prefill else None
+    blocks = block_scaled_bench(args, device) if not args.no_prefill else None
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -425,6 +473,7 @@ def run_ours(args, rank, world, local):
         "gpu_launches": 3 * args.steps,
         "clocks": clocks.summary(),
         "prefill": prefill,
+        "block_scaled": blocks,
     }
     if rank == 0:
         print(json.dumps(line))

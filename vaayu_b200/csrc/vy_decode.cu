@@ -38,6 +38,9 @@ constexpr int kStageK = 128;             // K elements of one row per pipeline s
 constexpr int kGuDepth = VY_GU_DEPTH;    // gate/up ring: stages in flight per warp (2 KB each)
 constexpr int kDnDepth = VY_DN_DEPTH;    // down ring: stages in flight per warp (1 KB each)
 constexpr int kTileRows = 16;
+// Resident down-projection CTAs per SM by column blocks: the register bound each variant meets
+// without spilling (its 64 KB shared-memory ring fits three); the down grid is one such wave.
+constexpr int kDnBlocksPerSm[5] = {0, 3, 2, 0, 1};
 
 struct GateUpParams {
     int hidden, inter, gs_shift, top_k;
@@ -362,7 +365,7 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
 }
 
 template <int ACT, int SC, bool ZERO, int NB>
-__global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) down_kernel(DownParams p) {
+__global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(DownParams p) {
     extern __shared__ uint4 ring[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
@@ -634,14 +637,14 @@ struct DecodeLayout {
 // can have is n_tokens; empty blocks are skipped at run time, so NB only costs registers.
 int nb_for(int64_t n_tokens) { return n_tokens <= 32 ? 1 : (n_tokens <= 64 ? 2 : 4); }
 
-// CTAs per down-projection row tile: as many as keep the whole grid resident at once (two CTAs
-// per SM; a grid a fraction of a wave larger runs a second, mostly empty wave), but no more
-// chunks than the call can have live experts per warp.
+// CTAs per down-projection row tile: as many as keep the whole grid resident at once (a grid a
+// fraction of a wave larger runs a second, mostly empty wave), but no more chunks than the call
+// can have live experts per warp.
 int down_chunks(const vy_moe_call* c, int sm_count) {
     const int64_t n = c->n_tokens * c->top_k;
     const int n_tiles = c->geom->hidden / kTileRows;
     const int64_t max_live = n < c->n_experts ? n : c->n_experts;
-    int chunks = (2 * sm_count) / n_tiles;
+    int chunks = (kDnBlocksPerSm[nb_for(c->n_tokens)] * sm_count) / n_tiles;
     const int cap = static_cast<int>((max_live + kWarps - 1) / kWarps);
     if (chunks > cap) chunks = cap;
     return chunks < 1 ? 1 : chunks;
