@@ -227,6 +227,109 @@ __global__ void __launch_bounds__(kThreads) fp4_dequant_kernel(
     }
 }
 
+// ── fast paths: whole 16-element chunks, each inside one row and one scale block ─────────────
+//
+// When the columns and the scale block width are multiples of 16, a chunk of 16 consecutive
+// elements has one scale: the row / block arithmetic is done once per chunk (32-bit), the codes
+// convert in pairs, and every thread keeps two chunks' loads in flight.  Same arithmetic as the
+// element-wise kernels above: fp32 product of the exact decoded value and the scale (RN), then
+// one rounding to the output dtype.
+
+template <int OUT>
+__device__ __forceinline__ void store16(void* out, uint32_t chunk, const float (&v)[16]) {
+    if constexpr (OUT == VY_F32) {
+        float4* d = reinterpret_cast<float4*>(out) + int64_t(chunk) * 4;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+        uint32_t p32[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if constexpr (OUT == VY_BF16) {
+                __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                p32[j] = *reinterpret_cast<uint32_t*>(&h);
+            } else {
+                __half2 h = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+                p32[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+        }
+        uint4* d = reinterpret_cast<uint4*>(out) + int64_t(chunk) * 2;
+        d[0] = make_uint4(p32[0], p32[1], p32[2], p32[3]);
+        d[1] = make_uint4(p32[4], p32[5], p32[6], p32[7]);
+    }
+}
+
+// 16 e4m3 codes (one uint4) times one scale.
+__device__ __forceinline__ void e4m3x16_times(const uint4 raw, float s, float (&v)[16]) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const __nv_fp8x2_storage_t pr = static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * h)) & 0xFFFFu);
+            const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+            v[4 * i + 2 * h] = __fmul_rn(f.x, s);
+            v[4 * i + 2 * h + 1] = __fmul_rn(f.y, s);
+        }
+    }
+}
+
+template <int SC, int OUT>
+__global__ void __launch_bounds__(kThreads) fp8_dequant_fast_kernel(const uint4* __restrict__ w, uint32_t chunks,
+                                                                    uint32_t cpr, const void* scale, uint32_t scols,
+                                                                    uint32_t bo, uint32_t bi16, void* out) {
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < chunks; q += 2 * stride) {
+        const uint32_t q2 = q + stride;
+        const bool two = q2 < chunks;
+        const uint4 a = __ldg(w + q);
+        const uint4 b = two ? __ldg(w + q2) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t ra = q / cpr, rb = q2 / cpr;
+        const float sa = load_block_scale<SC>(scale, int64_t(ra / bo) * scols + (q - ra * cpr) / bi16);
+        const float sb = two ? load_block_scale<SC>(scale, int64_t(rb / bo) * scols + (q2 - rb * cpr) / bi16) : 0.f;
+        float v[16];
+        e4m3x16_times(a, sa, v);
+        store16<OUT>(out, q, v);
+        if (two) {
+            e4m3x16_times(b, sb, v);
+            store16<OUT>(out, q2, v);
+        }
+    }
+}
+
+// 16 e2m1 codes (low nibble first) times one scale.
+__device__ __forceinline__ void e2m1x16_times(const uint2 raw, float s, float (&v)[16]) {
+    const uint32_t w[2] = {raw.x, raw.y};
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[8 * i + j] = __fmul_rn(e2m1_to_float((w[i] >> (4 * j)) & 15u), s);
+}
+
+template <int OUT>
+__global__ void __launch_bounds__(kThreads) fp4_dequant_fast_kernel(const uint2* __restrict__ w, uint32_t chunks,
+                                                                    uint32_t cpr, const uint8_t* __restrict__ scale,
+                                                                    uint32_t groups, uint32_t gs16, void* out) {
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < chunks; q += 2 * stride) {
+        const uint32_t q2 = q + stride;
+        const bool two = q2 < chunks;
+        const uint2 a = __ldg(w + q);
+        const uint2 b = two ? __ldg(w + q2) : make_uint2(0u, 0u);
+        const uint32_t ra = q / cpr, rb = q2 / cpr;
+        const float sa = e4m3_to_float(__ldg(scale + int64_t(ra) * groups + (q - ra * cpr) / gs16));
+        const float sb = two ? e4m3_to_float(__ldg(scale + int64_t(rb) * groups + (q2 - rb * cpr) / gs16)) : 0.f;
+        float v[16];
+        e2m1x16_times(a, sa, v);
+        store16<OUT>(out, q, v);
+        if (two) {
+            e2m1x16_times(b, sb, v);
+            store16<OUT>(out, q2, v);
+        }
+    }
+}
+
 bool act_dtype_ok(int d) { return d == VY_BF16 || d == VY_F16 || d == VY_F32; }
 
 // Dispatch (ACT x SC x BITS) for the two int-b kernels.
@@ -377,6 +480,30 @@ extern "C" int vy_fp8_dequant(const uint8_t* w, int64_t rows, int64_t cols, cons
     const int grid = grid_for((rows * cols + 15) / 16, dev->sm_count);
     cudaStream_t s = as_stream(stream);
     const int64_t bo = rows / srows, bi = cols / scols;
+    if (vec && cols % 16 == 0 && bi % 16 == 0 && rows * cols / 16 < (int64_t(1) << 31)) {
+        const uint32_t chunks = static_cast<uint32_t>(rows * cols / 16), cpr = static_cast<uint32_t>(cols / 16);
+        const int fgrid = grid_for((chunks + 1) / 2, dev->sm_count);
+        const uint4* w4 = reinterpret_cast<const uint4*>(w);
+        const uint32_t sc32 = static_cast<uint32_t>(scols), bo32 = static_cast<uint32_t>(bo),
+                       b16 = static_cast<uint32_t>(bi / 16);
+#define VY_FP8F(S, O) fp8_dequant_fast_kernel<S, O><<<fgrid, kThreads, 0, s>>>(w4, chunks, cpr, scale, sc32, bo32, b16, out)
+#define VY_FP8F_OUT(S)                                                  \
+    switch (out_dtype) {                                                \
+        case VY_BF16: VY_FP8F(S, VY_BF16); break;                       \
+        case VY_F16: VY_FP8F(S, VY_F16); break;                         \
+        default: VY_FP8F(S, VY_F32); break;                             \
+    }
+        switch (scale_dtype) {
+            case VY_F32: VY_FP8F_OUT(VY_F32) break;
+            case VY_BF16: VY_FP8F_OUT(VY_BF16) break;
+            case VY_F16: VY_FP8F_OUT(VY_F16) break;
+            case VY_E8M0: VY_FP8F_OUT(VY_E8M0) break;
+            default: return fail(VY_ERR_UNSUPPORTED, "block-scale dtype %d", scale_dtype);
+        }
+#undef VY_FP8F_OUT
+#undef VY_FP8F
+        return check_launch("vy_fp8_dequant");
+    }
 #define VY_FP8(S, O) fp8_dequant_kernel<S, O><<<grid, kThreads, 0, s>>>(w, rows, cols, scale, scols, bo, bi, out, vec)
 #define VY_FP8_OUT(S)                                                   \
     switch (out_dtype) {                                                \
@@ -410,6 +537,18 @@ extern "C" int vy_fp4_dequant(const uint8_t* w, int64_t rows, int64_t cols, cons
     const bool vec = (reinterpret_cast<uintptr_t>(w) & 7u) == 0 && aligned16(out);
     const int grid = grid_for((rows * cols + 15) / 16, dev->sm_count);
     cudaStream_t s = as_stream(stream);
+    if (vec && cols % 16 == 0 && group_size % 16 == 0 && rows * cols / 16 < (int64_t(1) << 31)) {
+        const uint32_t chunks = static_cast<uint32_t>(rows * cols / 16), cpr = static_cast<uint32_t>(cols / 16);
+        const uint32_t groups = static_cast<uint32_t>(cols / group_size), g16 = static_cast<uint32_t>(group_size / 16);
+        const int fgrid = grid_for((chunks + 1) / 2, dev->sm_count);
+        const uint2* w2 = reinterpret_cast<const uint2*>(w);
+        switch (out_dtype) {
+            case VY_BF16: fp4_dequant_fast_kernel<VY_BF16><<<fgrid, kThreads, 0, s>>>(w2, chunks, cpr, scale, groups, g16, out); break;
+            case VY_F16: fp4_dequant_fast_kernel<VY_F16><<<fgrid, kThreads, 0, s>>>(w2, chunks, cpr, scale, groups, g16, out); break;
+            default: fp4_dequant_fast_kernel<VY_F32><<<fgrid, kThreads, 0, s>>>(w2, chunks, cpr, scale, groups, g16, out); break;
+        }
+        return check_launch("vy_fp4_dequant");
+    }
     switch (out_dtype) {
         case VY_BF16: fp4_dequant_kernel<VY_BF16><<<grid, kThreads, 0, s>>>(w, rows, cols, scale, group_size, out, vec); break;
         case VY_F16: fp4_dequant_kernel<VY_F16><<<grid, kThreads, 0, s>>>(w, rows, cols, scale, group_size, out, vec); break;

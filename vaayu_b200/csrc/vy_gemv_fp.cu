@@ -22,6 +22,12 @@ __device__ __forceinline__ float e4m3f(uint32_t b) {
     return __half2float(__half(h));
 }
 
+// Two e4m3 codes (the low 16 bits of `b`) as floats, exactly.
+__device__ __forceinline__ float2 e4m3x2f(uint32_t b) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(b & 0xFFFFu), __NV_E4M3);
+    return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
 __device__ __forceinline__ float e2m1f(uint32_t nib) {
     uint32_t e = (nib >> 1) & 3u, m = nib & 1u;
     uint32_t bits = e ? (((e + 126u) << 23) | (m << 22)) : (m ? 0x3F000000u : 0u);
@@ -54,6 +60,7 @@ struct GemvParams {
     int scale_dtype;
     int64_t srows, scols, bo, bi;   // fp8 block scales
     int gs;                         // fp4 group
+    int div_shift;                  // log2 of the fp8 block width / fp4 group when a power of two, else -1
     const __nv_bfloat16* x;
     int64_t x_stride;
     int n_tokens;
@@ -79,6 +86,14 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
     const int64_t row_bytes = KIND == 0 ? p.k : p.k / 2;
     const uint8_t* wA = p.w + (okA ? rA : 0) * row_bytes;
     const uint8_t* wB = p.w + (okB ? rB : 0) * row_bytes;
+    // per-row scale bases, and K -> block / group index with a shift when possible (32-bit: k < 2^31)
+    const int64_t baseA = KIND == 0 ? (okA ? (rA / p.bo) * p.scols : 0) : (okA ? rA * (p.k / p.gs) : 0);
+    const int64_t baseB = KIND == 0 ? (okB ? (rB / p.bo) * p.scols : 0) : (okB ? rB * (p.k / p.gs) : 0);
+    const uint32_t div = static_cast<uint32_t>(KIND == 0 ? p.bi : p.gs);
+    const int dsh = p.div_shift;
+    auto kdiv = [&](uint32_t kk) { return dsh >= 0 ? (kk >> dsh) : (kk / div); };
+    const bool halves = KIND == 1 && (p.gs % 16) == 0;   // a thread's 32 fp4 codes: two whole groups
+    const uint8_t* sc8 = reinterpret_cast<const uint8_t*>(p.scale);
 
     float acc[NB][4];
 #pragma unroll
@@ -103,11 +118,19 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
         for (int u = 0; u < kUnroll; ++u) {
             const int64_t s = s0 + u;
             if (s >= s_hi) break;
-            const int64_t k0 = s * kStepK + tig * kPerThread;
-            float sa, sb;
+            const uint32_t k0 = static_cast<uint32_t>(s * kStepK + tig * kPerThread);
+            float sa = 0.f, sb = 0.f, ha[2] = {0.f, 0.f}, hb[2] = {0.f, 0.f};
             if constexpr (KIND == 0) {
-                sa = okA ? block_scale(p.scale, p.scale_dtype, (rA / p.bo) * p.scols + k0 / p.bi) : 0.f;
-                sb = okB ? block_scale(p.scale, p.scale_dtype, (rB / p.bo) * p.scols + k0 / p.bi) : 0.f;
+                const uint32_t kb = kdiv(k0);
+                sa = okA ? block_scale(p.scale, p.scale_dtype, baseA + kb) : 0.f;
+                sb = okB ? block_scale(p.scale, p.scale_dtype, baseB + kb) : 0.f;
+            } else if (halves) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const uint32_t gi = kdiv(k0 + 16 * hh);
+                    ha[hh] = okA ? e4m3f(__ldg(sc8 + baseA + gi)) : 0.f;
+                    hb[hh] = okB ? e4m3f(__ldg(sc8 + baseB + gi)) : 0.f;
+                }
             }
             const uint32_t wa[4] = {va[u].x, va[u].y, va[u].z, va[u].w};
             const uint32_t wb[4] = {vb[u].x, vb[u].y, vb[u].z, vb[u].w};
@@ -118,14 +141,22 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
                 uint32_t a0, a1, a2, a3;
                 if constexpr (KIND == 0) {
                     const uint32_t xa = wa[q], xb = wb[q];   // 4 codes: elements 4q..4q+3
-                    a0 = bf16_pair(__fmul_rn(e4m3f(xa), sa), __fmul_rn(e4m3f(xa >> 8), sa));
-                    a2 = bf16_pair(__fmul_rn(e4m3f(xa >> 16), sa), __fmul_rn(e4m3f(xa >> 24), sa));
-                    a1 = bf16_pair(__fmul_rn(e4m3f(xb), sb), __fmul_rn(e4m3f(xb >> 8), sb));
-                    a3 = bf16_pair(__fmul_rn(e4m3f(xb >> 16), sb), __fmul_rn(e4m3f(xb >> 24), sb));
+                    const float2 fa0 = e4m3x2f(xa), fa1 = e4m3x2f(xa >> 16);
+                    const float2 fb0 = e4m3x2f(xb), fb1 = e4m3x2f(xb >> 16);
+                    a0 = bf16_pair(__fmul_rn(fa0.x, sa), __fmul_rn(fa0.y, sa));
+                    a2 = bf16_pair(__fmul_rn(fa1.x, sa), __fmul_rn(fa1.y, sa));
+                    a1 = bf16_pair(__fmul_rn(fb0.x, sb), __fmul_rn(fb0.y, sb));
+                    a3 = bf16_pair(__fmul_rn(fb1.x, sb), __fmul_rn(fb1.y, sb));
                 } else {
-                    const int64_t gi = (k0 + 4 * q) / p.gs;
-                    const float fa = okA ? e4m3f(__ldg(reinterpret_cast<const uint8_t*>(p.scale) + rA * (p.k / p.gs) + gi)) : 0.f;
-                    const float fb = okB ? e4m3f(__ldg(reinterpret_cast<const uint8_t*>(p.scale) + rB * (p.k / p.gs) + gi)) : 0.f;
+                    float fa, fb;
+                    if (halves) {
+                        fa = ha[q >> 2];
+                        fb = hb[q >> 2];
+                    } else {
+                        const uint32_t gi = kdiv(k0 + 4 * q);
+                        fa = okA ? e4m3f(__ldg(sc8 + baseA + gi)) : 0.f;
+                        fb = okB ? e4m3f(__ldg(sc8 + baseB + gi)) : 0.f;
+                    }
                     const uint32_t xa = (wa[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;   // 4 nibbles
                     const uint32_t xb = (wb[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
                     a0 = bf16_pair(__fmul_rn(e2m1f(xa), fa), __fmul_rn(e2m1f(xa >> 4), fa));
@@ -172,9 +203,17 @@ int launch_gemv(int kind, const GemvParams& p, cudaStream_t s) {
     return check_launch(kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv");
 }
 
+int pow2_shift(int64_t v) {
+    if (v <= 0 || (v & (v - 1))) return -1;
+    int s = 0;
+    while ((int64_t(1) << s) < v) ++s;
+    return s;
+}
+
 int common_checks(const uint8_t* w, int64_t n, int64_t k, const void* x, int64_t x_stride,
                   int64_t n_tokens, void* out, int64_t out_stride, int64_t step) {
     if (n < 0 || k < 0 || n_tokens < 0) return fail(VY_ERR_INVALID, "negative size");
+    if (k >= (int64_t(1) << 31)) return fail(VY_ERR_UNSUPPORTED, "k %lld >= 2^31", (long long)k);
     if (n_tokens > 16) return fail(VY_ERR_UNSUPPORTED, "batch %lld > 16", (long long)n_tokens);
     if (k % step) return fail(VY_ERR_UNSUPPORTED, "k %lld is not a multiple of %lld", (long long)k, (long long)step);
     if (n == 0 || n_tokens == 0) return VY_OK;
@@ -207,7 +246,7 @@ extern "C" int vy_fp8_gemv(const uint8_t* w, int64_t n, int64_t k, const void* s
     if (scale_dtype != VY_F32 && scale_dtype != VY_BF16 && scale_dtype != VY_F16 && scale_dtype != VY_E8M0)
         return fail(VY_ERR_UNSUPPORTED, "block-scale dtype %d", scale_dtype);
     if (!scale) return fail(VY_ERR_INVALID, "null scale");
-    GemvParams p{w, n, k, scale, scale_dtype, srows, scols, n / srows, k / scols, 0,
+    GemvParams p{w, n, k, scale, scale_dtype, srows, scols, n / srows, k / scols, 0, pow2_shift(k / scols),
                  reinterpret_cast<const __nv_bfloat16*>(x), x_stride, static_cast<int>(n_tokens),
                  reinterpret_cast<__nv_bfloat16*>(out), out_stride};
     return launch_gemv(0, p, as_stream(stream));
@@ -224,7 +263,7 @@ extern "C" int vy_fp4_gemv(const uint8_t* w, int64_t n, int64_t k, const uint8_t
     if (group_size <= 0 || group_size % 4 || k % group_size)
         return fail(VY_ERR_UNSUPPORTED, "fp4 group %d", group_size);
     if (!scale) return fail(VY_ERR_INVALID, "null scale");
-    GemvParams p{w, n, k, scale, VY_E4M3, 0, 0, 0, 0, group_size,
+    GemvParams p{w, n, k, scale, VY_E4M3, 0, 0, 0, 0, group_size, pow2_shift(group_size),
                  reinterpret_cast<const __nv_bfloat16*>(x), x_stride, static_cast<int>(n_tokens),
                  reinterpret_cast<__nv_bfloat16*>(out), out_stride};
     return launch_gemv(1, p, as_stream(stream));
