@@ -28,6 +28,25 @@ __device__ __forceinline__ float2 e4m3x2f(uint32_t b) {
     return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
+// Four e2m1 codes (bits 0-15, low nibble first) as two bf16 pairs, exactly: the magnitudes
+// index an 8-entry byte table for each half of the bf16 pattern (prmt), the signs are the codes'
+// own sign bits replicated into bit 15 / 31 (prmt's sign-replicate selectors).
+__device__ __forceinline__ void e2m1x4_bf16(uint32_t c, uint32_t& e01, uint32_t& e23) {
+    // bf16 of 0, 0.5, 1, 1.5, 2, 3, 4, 6: low bytes 00 00 80 C0 00 40 80 C0, high 00 3F 3F 3F 40 40 40 40
+    const uint32_t mag = c & 0x7777u;
+    const uint32_t lo = __byte_perm(0xC0800000u, 0xC0804000u, mag);
+    const uint32_t hi = __byte_perm(0x3F3F3F00u, 0x40404040u, mag);
+    const uint32_t a = c << 4;   // byte 0 / 1 msb = sign of code 0 / 2; c's byte 0 / 1 msb = code 1 / 3
+    e01 = __byte_perm(lo, hi, 0x5140) | (__byte_perm(a, c, 0xC080) & 0x80008000u);
+    e23 = __byte_perm(lo, hi, 0x7362) | (__byte_perm(a, c, 0xD090) & 0x80008000u);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
 __device__ __forceinline__ float e2m1f(uint32_t nib) {
     uint32_t e = (nib >> 1) & 3u, m = nib & 1u;
     uint32_t bits = e ? (((e + 126u) << 23) | (m << 22)) : (m ? 0x3F000000u : 0u);
@@ -119,7 +138,8 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
             const int64_t s = s0 + u;
             if (s >= s_hi) break;
             const uint32_t k0 = static_cast<uint32_t>(s * kStepK + tig * kPerThread);
-            float sa = 0.f, sb = 0.f, ha[2] = {0.f, 0.f}, hb[2] = {0.f, 0.f};
+            float sa = 0.f, sb = 0.f;
+            uint32_t ha[2] = {0u, 0u}, hb[2] = {0u, 0u};   // fp4 group scales as bf16 pairs (exact)
             if constexpr (KIND == 0) {
                 const uint32_t kb = kdiv(k0);
                 sa = okA ? block_scale(p.scale, p.scale_dtype, baseA + kb) : 0.f;
@@ -128,8 +148,8 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
 #pragma unroll
                 for (int hh = 0; hh < 2; ++hh) {
                     const uint32_t gi = kdiv(k0 + 16 * hh);
-                    ha[hh] = okA ? e4m3f(__ldg(sc8 + baseA + gi)) : 0.f;
-                    hb[hh] = okB ? e4m3f(__ldg(sc8 + baseB + gi)) : 0.f;
+                    ha[hh] = okA ? bf16_pair(e4m3f(__ldg(sc8 + baseA + gi)), e4m3f(__ldg(sc8 + baseA + gi))) : 0u;
+                    hb[hh] = okB ? bf16_pair(e4m3f(__ldg(sc8 + baseB + gi)), e4m3f(__ldg(sc8 + baseB + gi))) : 0u;
                 }
             }
             const uint32_t wa[4] = {va[u].x, va[u].y, va[u].z, va[u].w};
@@ -148,21 +168,27 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
                     a1 = bf16_pair(__fmul_rn(fb0.x, sb), __fmul_rn(fb0.y, sb));
                     a3 = bf16_pair(__fmul_rn(fb1.x, sb), __fmul_rn(fb1.y, sb));
                 } else {
-                    float fa, fb;
-                    if (halves) {
-                        fa = ha[q >> 2];
-                        fb = hb[q >> 2];
-                    } else {
-                        const uint32_t gi = kdiv(k0 + 4 * q);
-                        fa = okA ? e4m3f(__ldg(sc8 + baseA + gi)) : 0.f;
-                        fb = okB ? e4m3f(__ldg(sc8 + baseB + gi)) : 0.f;
-                    }
                     const uint32_t xa = (wa[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;   // 4 nibbles
                     const uint32_t xb = (wb[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
-                    a0 = bf16_pair(__fmul_rn(e2m1f(xa), fa), __fmul_rn(e2m1f(xa >> 4), fa));
-                    a2 = bf16_pair(__fmul_rn(e2m1f(xa >> 8), fa), __fmul_rn(e2m1f(xa >> 12), fa));
-                    a1 = bf16_pair(__fmul_rn(e2m1f(xb), fb), __fmul_rn(e2m1f(xb >> 4), fb));
-                    a3 = bf16_pair(__fmul_rn(e2m1f(xb >> 8), fb), __fmul_rn(e2m1f(xb >> 12), fb));
+                    if (halves) {
+                        // e2m1 x e4m3 has at most 6 significant bits: the bf16 product is exact,
+                        // i.e. the same value the fp32 product rounded to bf16 gives
+                        uint32_t ea01, ea23, eb01, eb23;
+                        e2m1x4_bf16(xa, ea01, ea23);
+                        e2m1x4_bf16(xb, eb01, eb23);
+                        a0 = bf16x2_mul(ea01, ha[q >> 2]);
+                        a2 = bf16x2_mul(ea23, ha[q >> 2]);
+                        a1 = bf16x2_mul(eb01, hb[q >> 2]);
+                        a3 = bf16x2_mul(eb23, hb[q >> 2]);
+                    } else {
+                        const uint32_t gi = kdiv(k0 + 4 * q);
+                        const float fa = okA ? e4m3f(__ldg(sc8 + baseA + gi)) : 0.f;
+                        const float fb = okB ? e4m3f(__ldg(sc8 + baseB + gi)) : 0.f;
+                        a0 = bf16_pair(__fmul_rn(e2m1f(xa), fa), __fmul_rn(e2m1f(xa >> 4), fa));
+                        a2 = bf16_pair(__fmul_rn(e2m1f(xa >> 8), fa), __fmul_rn(e2m1f(xa >> 12), fa));
+                        a1 = bf16_pair(__fmul_rn(e2m1f(xb), fb), __fmul_rn(e2m1f(xb >> 4), fb));
+                        a3 = bf16_pair(__fmul_rn(e2m1f(xb >> 8), fb), __fmul_rn(e2m1f(xb >> 12), fb));
+                    }
                 }
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
