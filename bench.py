@@ -579,6 +579,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the configuration-2 prefill measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--ep-col-blocks", type=int, default=None, choices=(1, 2, 4),
+                    help="tokens per expert pass (x8) in the expert-parallel step; default by load")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, world, local = dist_setup()

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define VY_ABI_VERSION 1
+#define VY_ABI_VERSION 2
 
 enum vy_status {
     VY_OK = 0,
@@ -179,6 +179,16 @@ typedef struct vy_expert_geom {
  * c go there ([n_tokens*top_k, hidden] fp32) and `out` is not written (the expert-parallel
  * combine sums them on the token's home rank).  `h_out` (optional, [n_tokens*top_k, inter],
  * act dtype) receives each row's h: a stage probe for tests.
+ *
+ * Fields appended in ABI version 2 (zero keeps version-1 behaviour):
+ *   col_blocks      tokens one decode pass of an expert carries, in blocks of 8: 1, 2 or 4 (0:
+ *                   chosen from n_tokens).  An expert with more routed rows takes more passes
+ *                   (its weights are read once per pass); a caller that knows the rows per expert
+ *                   are few (e.g. a rank's share of an all-gathered batch) picks a small value.
+ *   expert_base     expert_ids[j] - expert_base indexes expert_table; ids outside
+ *                   [expert_base, expert_base + n_experts) drop their slot (a rank's own range of a
+ *                   global id space).
+ *   ids_row_stride  elements between consecutive tokens' rows of expert_ids (0: top_k).
  */
 typedef struct vy_moe_call {
     const vy_expert_geom* geom;
@@ -212,7 +222,19 @@ typedef struct vy_moe_call {
     void* const* stage_events;
     int32_t n_stage_events;
     int32_t reserved1;
+    /* ABI version 2 */
+    int32_t col_blocks;
+    int32_t expert_base;
+    int64_t ids_row_stride;
 } vy_moe_call;
+
+/*
+ * out[i] = ((parts[0][i] + parts[1][i]) + ...) + parts[n_parts-1][i], fp32, in part order: the
+ * expert-parallel combine of per-rank partial sums (ranks hold ascending expert ranges).  parts
+ * is [n_parts][n] contiguous; n a multiple of 4, both pointers 16-byte aligned.  No counterpart
+ * in the reference (it is single-GPU).
+ */
+int vy_sum_ordered(const float* parts, int32_t n_parts, int64_t n, float* out, void* stream);
 
 /* Bytes of workspace vy_moe_decode (path 0) / vy_moe_prefill (path 1) need for `call`. */
 size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path);

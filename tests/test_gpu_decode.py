@@ -248,3 +248,39 @@ def test_an_expert_id_outside_the_table_is_dropped():
     ref = vb.moe_forward(x, idx, w2, table, path=vb.PATH_DECODE)
     assert torch.equal(got[0], ref[0]) and torch.equal(got[2:], ref[2:])
     assert torch.allclose(got[1], ref[1], rtol=0, atol=1e-6)
+
+
+def test_global_ids_with_an_expert_base_read_through_a_strided_view():
+    """A rank's table holds experts [16, 32) of a global id space: ids outside it drop their
+    slot; the ids may sit in a wider buffer (row stride > top_k)."""
+    blobs, x, idx, w = _batched(1024, 512, 128, 32, 4, 24, seed=11)
+    local = pk.ExpertTable(blobs[16:32])
+    wide = torch.full((24, 9), -7, dtype=torch.int32, device="cuda")
+    wide[:, 2:6] = idx.to(torch.int32)
+    got = vb.moe_forward(x, wide[:, 2:6], w, local, path=vb.PATH_DECODE, expert_base=16)
+    masked = torch.where((idx >= 16) & (idx < 32), idx - 16, torch.full_like(idx, -1))
+    ref = vb.moe_forward(x, masked, w, local, path=vb.PATH_DECODE)
+    assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("col_blocks", [1, 2, 4])
+def test_the_column_block_count_does_not_change_a_bit(col_blocks):
+    """More passes per expert (col_blocks=1: 8 tokens per pass) or fewer: same per-row math."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 8, 4, 40, seed=12)
+    table = pk.ExpertTable(blobs)
+    ref = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE)
+    got = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, col_blocks=col_blocks)
+    assert torch.equal(got, ref)
+
+
+def test_ordered_partial_sum():
+    from vaayu_b200 import _lib
+    g = torch.Generator().manual_seed(3)
+    parts = (torch.randn(5, 32, 2048, generator=g) * torch.logspace(-3, 3, 5).reshape(5, 1, 1)).cuda()
+    out = torch.empty(32, 2048, device="cuda")
+    _lib.check(_lib.lib().vy_sum_ordered(parts.data_ptr(), 5, out.numel(), out.data_ptr(),
+                                         _lib.stream_of(out.device)), "vy_sum_ordered")
+    ref = parts[0].clone()
+    for q in range(1, 5):
+        ref += parts[q]
+    assert torch.equal(out, ref)

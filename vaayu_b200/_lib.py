@@ -38,7 +38,8 @@ class MoeCall(ctypes.Structure):
                 ("w_dtype", I32T), ("reserved0", I32T), ("w_tok_stride", I64T),
                 ("w_slot_stride", I64T), ("w_index", P), ("out", P), ("out_row_stride", I64T),
                 ("contrib", P), ("h_out", P), ("workspace", P), ("workspace_bytes", SZ),
-                ("stage_events", P), ("n_stage_events", I32T), ("reserved1", I32T)]
+                ("stage_events", P), ("n_stage_events", I32T), ("reserved1", I32T),
+                ("col_blocks", I32T), ("expert_base", I32T), ("ids_row_stride", I64T)]
 
 
 # name -> (restype, argtypes); every symbol include/vaayu_b200.h declares
@@ -59,6 +60,7 @@ SIGNATURES = {
     "vy_moe_decode_static": (ctypes.c_int, [ctypes.POINTER(MoeCall), P]),
     "vy_moe_prefill": (ctypes.c_int, [ctypes.POINTER(MoeCall), P]),
     "vy_moe_combine": (ctypes.c_int, [P, P, I32T, I64T, I32T, I64T, P, I64T, P]),
+    "vy_sum_ordered": (ctypes.c_int, [P, I32T, I64T, P, P]),
 }
 
 _LIB = None

@@ -636,6 +636,7 @@ struct DecodeLayout {
 // Column blocks (8 tokens each) one pass of a unit holds: the largest token count an expert
 // can have is n_tokens; empty blocks are skipped at run time, so NB only costs registers.
 int nb_for(int64_t n_tokens) { return n_tokens <= 32 ? 1 : (n_tokens <= 64 ? 2 : 4); }
+int call_nb(const vy_moe_call* c) { return c->col_blocks ? c->col_blocks : nb_for(c->n_tokens); }
 
 // CTAs per down-projection row tile: as many as keep the whole grid resident at once (a grid a
 // fraction of a wave larger runs a second, mostly empty wave), but no more chunks than the call
@@ -644,7 +645,7 @@ int down_chunks(const vy_moe_call* c, int sm_count) {
     const int64_t n = c->n_tokens * c->top_k;
     const int n_tiles = c->geom->hidden / kTileRows;
     const int64_t max_live = n < c->n_experts ? n : c->n_experts;
-    int chunks = (kDnBlocksPerSm[nb_for(c->n_tokens)] * sm_count) / n_tiles;
+    int chunks = (kDnBlocksPerSm[call_nb(c)] * sm_count) / n_tiles;
     const int cap = static_cast<int>((max_live + kWarps - 1) / kWarps);
     if (chunks > cap) chunks = cap;
     return chunks < 1 ? 1 : chunks;
@@ -664,7 +665,7 @@ DecodeLayout decode_layout(const vy_moe_call* c, void* base, int sm_count) {
     L.counters = cv.take<int32_t>(4);
     L.tile_done = cv.take<int32_t>(H / kTileRows);
     {
-        const int64_t tpu = nb_for(c->n_tokens) * 8, max_live = n < E ? n : E;
+        const int64_t tpu = call_nb(c) * 8, max_live = n < E ? n : E;
         L.passes = cv.take<PassEntry>(n / tpu + max_live + 1);
     }
     L.x_perm = cv.take<uint16_t>(c->n_tokens * H);
@@ -706,6 +707,10 @@ int validate_call(const vy_moe_call* c) {
         return fail(VY_ERR_UNSUPPORTED, "routing-weight dtype %d", c->w_dtype);
     if (c->ids_dtype != VY_I32 && c->ids_dtype != VY_I64)
         return fail(VY_ERR_UNSUPPORTED, "expert-id dtype %d", c->ids_dtype);
+    if (c->col_blocks != 0 && c->col_blocks != 1 && c->col_blocks != 2 && c->col_blocks != 4)
+        return fail(VY_ERR_UNSUPPORTED, "col_blocks %d (0, 1, 2 or 4)", c->col_blocks);
+    if (c->ids_row_stride != 0 && c->ids_row_stride < c->top_k)
+        return fail(VY_ERR_INVALID, "ids_row_stride %lld < top_k %d", (long long)c->ids_row_stride, c->top_k);
     int st = plan_validate(c->n_tokens, c->top_k, c->n_experts);
     if (st != VY_OK) return st;
     const int64_t n = c->n_tokens * c->top_k;
@@ -747,11 +752,13 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     L = decode_layout(c, base, dev->sm_count);
     const vy_expert_geom& g = *c->geom;
     cudaStream_t s = as_stream(stream);
-    const int nb = nb_for(c->n_tokens);
+    const int nb = call_nb(c);
 
     PlanArgs pa{};
     pa.ids = c->expert_ids;
     pa.ids64 = c->ids_dtype == VY_I64;
+    pa.ids_stride = c->ids_row_stride ? c->ids_row_stride : c->top_k;
+    pa.id_base = c->expert_base;
     pa.n_tokens = c->n_tokens;
     pa.top_k = c->top_k;
     pa.n_experts = c->n_experts;

@@ -22,6 +22,8 @@ struct __align__(16) PassEntry {
 struct PlanArgs {
     const void* ids;
     bool ids64;
+    int64_t ids_stride;    // elements between tokens' id rows (top_k when contiguous)
+    int id_base;           // ids are offset by this (a rank's range of a global id space)
     int64_t n_tokens;
     int top_k;
     int n_experts;

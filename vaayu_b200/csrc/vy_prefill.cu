@@ -668,6 +668,8 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
     PlanArgs pa{};
     pa.ids = c->expert_ids;
     pa.ids64 = c->ids_dtype == VY_I64;
+    pa.ids_stride = c->ids_row_stride ? c->ids_row_stride : c->top_k;
+    pa.id_base = c->expert_base;
     pa.n_tokens = c->n_tokens;
     pa.top_k = c->top_k;
     pa.n_experts = c->n_experts;

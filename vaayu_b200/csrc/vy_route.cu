@@ -19,6 +19,17 @@ __device__ __forceinline__ int load_id(const void* ids, bool ids64, int64_t j) {
     return reinterpret_cast<const int32_t*>(ids)[j];
 }
 
+// Expert index of row j = t * top_k + k (id - id_base; the caller range-checks it).
+__device__ __forceinline__ int plan_id(const PlanArgs& p, int64_t j) {
+    int64_t idx = j;
+    if (p.ids_stride != p.top_k) {
+        const int64_t t = j / p.top_k;
+        idx = t * p.ids_stride + (j - t * p.top_k);
+    }
+    const int e = load_id(p.ids, p.ids64, idx);
+    return e < 0 ? -1 : e - p.id_base;
+}
+
 // Exclusive scan of one int per thread over the block (any whole number of warps up to
 // kPlanWarps); returns this thread's prefix and puts the total in *total.  `scratch` holds
 // kPlanWarps + 1 ints.
@@ -104,7 +115,7 @@ __device__ void plan_small(const PlanArgs& p) {
         for (int i = tid; i < 3 * E; i += blockDim.x) table[i] = p.expert_table[i];
     int e = -1;
     if (tid < n) {
-        e = load_id(p.ids, p.ids64, tid);
+        e = plan_id(p, tid);
         if (e < 0 || e >= E) e = -1;
         ids[tid] = e;
     }
@@ -259,7 +270,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
         const int64_t row = base + lane;
         int e = -1;
         if (row < hi) {
-            e = load_id(p.ids, p.ids64, row);
+            e = plan_id(p, row);
             if (e < 0 || e >= E) {
                 atomicAdd(&dropped, 1);
                 e = -1;
@@ -308,7 +319,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
         const int64_t row = base + lane;
         int ex = -1;
         if (row < hi) {
-            ex = load_id(p.ids, p.ids64, row);
+            ex = plan_id(p, row);
             if (ex < 0 || ex >= E) ex = -1;
         }
         const unsigned mask = __match_any_sync(0xffffffffu, ex);
@@ -342,7 +353,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
     for (int64_t t = threadIdx.x; t < p.n_tokens; t += blockDim.x) {
         int key[kMaxTopK], idx[kMaxTopK];
         for (int k = 0; k < K; ++k) {
-            int ex = load_id(p.ids, p.ids64, t * K + k);
+            int ex = plan_id(p, t * K + k);
             key[k] = (ex < 0 || ex >= E) ? INT32_MAX : ex;
             idx[k] = k;
         }
@@ -551,9 +562,42 @@ int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_
     return check_launch("combine");
 }
 
+// out[i] = parts[0][i] + parts[1][i] + ... in part order, one fp32 add each (float4 lanes).
+__global__ void __launch_bounds__(256) sum_ordered_kernel(const float4* __restrict__ parts, int n_parts, int64_t n4,
+                                                          float4* out) {
+    for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n4; i += int64_t(gridDim.x) * blockDim.x) {
+        float4 a = parts[i];
+        for (int q = 1; q < n_parts; ++q) {
+            const float4 v = parts[int64_t(q) * n4 + i];
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
+        }
+        out[i] = a;
+    }
+}
+
 }  // namespace vy
 
 using namespace vy;
+
+extern "C" int vy_sum_ordered(const float* parts, int32_t n_parts, int64_t n, float* out, void* stream) {
+    int st;
+    const DeviceInfo* dev = device_info(&st);
+    if (!dev) return st;
+    if (n_parts < 1 || n < 0) return fail(VY_ERR_INVALID, "%d parts of %lld", n_parts, (long long)n);
+    if (n == 0) return ok();
+    if (!parts || !out) return fail(VY_ERR_INVALID, "null pointer");
+    if (n % 4 || !aligned16(parts) || !aligned16(out))
+        return fail(VY_ERR_ALIGNMENT, "parts / out must be 16-byte aligned with n a multiple of 4");
+    const int64_t n4 = n / 4;
+    int64_t blocks = (n4 + 255) / 256;
+    if (blocks > 8 * dev->sm_count) blocks = 8 * dev->sm_count;
+    sum_ordered_kernel<<<static_cast<unsigned>(blocks), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const float4*>(parts), n_parts, n4, reinterpret_cast<float4*>(out));
+    return check_launch("vy_sum_ordered");
+}
 
 extern "C" int vy_moe_route_permute(const void* ids, int32_t ids_dtype, int64_t n_tokens,
                                     int32_t top_k, int32_t n_experts, int32_t* order,
@@ -570,6 +614,8 @@ extern "C" int vy_moe_route_permute(const void* ids, int32_t ids_dtype, int64_t 
     PlanArgs p{};
     p.ids = ids;
     p.ids64 = ids_dtype == VY_I64;
+    p.ids_stride = top_k;
+    p.id_base = 0;
     p.n_tokens = n_tokens;
     p.top_k = top_k;
     p.n_experts = n_experts;

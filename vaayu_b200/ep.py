@@ -62,11 +62,12 @@ class ExpertParallelLayer:
     def __init__(self, local_blobs, n_experts: int, group=None, compute: Optional[Callable] = None,
                  combine_fn: Optional[Callable] = None, hidden: Optional[int] = None,
                  mode: str = "auto", replicate_max_tokens: int = 256,
-                 layer_fn: Optional[Callable] = None):
+                 layer_fn: Optional[Callable] = None, col_blocks: Optional[int] = None):
         if mode not in ("auto", "replicate", "dispatch"):
             raise ValueError(f"mode {mode!r}")
         self.mode = mode
         self.replicate_max_tokens = replicate_max_tokens
+        self.col_blocks = col_blocks
         self._layer_fn = layer_fn
         self._bufs = {}
         self.group = group
@@ -150,11 +151,16 @@ class ExpertParallelLayer:
             row += (-row) % 16                       # 16-byte rows: the activation views stay aligned
             P = self.world
             ws = None
+            # rows per local expert: the rank's share of the gathered slots over its experts
+            nb = self.col_blocks
+            if nb is None:
+                expect = T * K * P / max(1, self.n_experts)
+                nb = 1 if 1.5 * expect <= 8 else (2 if 1.5 * expect <= 16 else 4)
             if self.table is not None:
                 from .packed_expert_kernels import PATH_DECODE, moe_workspace_bytes
-                ws = torch.empty(moe_workspace_bytes(self.table, P * T, K, path=PATH_DECODE),
+                ws = torch.empty(moe_workspace_bytes(self.table, P * T, K, path=PATH_DECODE, col_blocks=nb),
                                  dtype=torch.uint8, device=x.device)
-            b = dict(row=row, xb=xb, wb=wb, ws=ws,
+            b = dict(row=row, xb=xb, wb=wb, ws=ws, nb=nb,
                      send=torch.empty(T, row, dtype=torch.uint8, device=x.device),
                      recv=torch.empty(P * T, row, dtype=torch.uint8, device=x.device),
                      partial=torch.empty(P * T, H, dtype=torch.float32, device=x.device),
@@ -180,22 +186,31 @@ class ExpertParallelLayer:
         xa = recv[:, :xb].view(x.dtype)
         ga = recv[:, xb:xb + 4 * K].view(torch.int32)
         wa = recv[:, xb + 4 * K:xb + 4 * K + wb].view(weights.dtype)
-        local = ga - self.lo
-        local = torch.where((local >= 0) & (local < self.per_rank), local, torch.full_like(local, -1))
         if self._layer_fn is not None:
+            local = ga - self.lo
+            local = torch.where((local >= 0) & (local < self.per_rank), local, torch.full_like(local, -1))
             partial.copy_(self._layer_fn(xa, local, wa))
         else:
+            # global ids straight from the gathered rows: the kernels keep [lo, lo + per_rank)
             from .packed_expert_kernels import PATH_DECODE, moe_forward
-            moe_forward(xa, local, wa, self.table, out=partial, path=PATH_DECODE, workspace=b["ws"])
+            moe_forward(xa, ga, wa, self.table, out=partial, path=PATH_DECODE, workspace=b["ws"],
+                        expert_base=self.lo, col_blocks=b["nb"])
         if P == 1:
             back[0].copy_(partial)
         else:
             dist.all_to_all_single(back.view(P * T, H), partial, group=self.group)
         if out is None:
             out = torch.empty(T, H, dtype=torch.float32, device=x.device)
-        out.copy_(back[0])
-        for r in range(1, P):          # rank order: ascending expert ranges, one fp32 add each
-            out.add_(back[r])
+        if back.is_cuda and out.is_contiguous():
+            from . import _lib
+            with torch.cuda.device(back.device):
+                # rank order: ascending expert ranges, one fp32 add each
+                _lib.check(_lib.lib().vy_sum_ordered(back.data_ptr(), P, T * H, out.data_ptr(),
+                                                     _lib.stream_of(back.device)), "vy_sum_ordered")
+        else:
+            out.copy_(back[0])
+            for r in range(1, P):          # rank order: ascending expert ranges, one fp32 add each
+                out.add_(back[r])
         return out
 
     def forward(self, x, ids, weights, out=None):
@@ -228,7 +243,8 @@ def run_bench(args, rank, world, local, wl):
     device = torch.device("cuda", local)
     E, T, K = wl["experts"], wl["tokens"], wl["top_k"]
     per = E // world
-    layers = [ExpertParallelLayer(bench.make_layer(1000 * l, wl, device, (rank * per, (rank + 1) * per)), E)
+    layers = [ExpertParallelLayer(bench.make_layer(1000 * l, wl, device, (rank * per, (rank + 1) * per)), E,
+                                  col_blocks=getattr(args, "ep_col_blocks", None))
               for l in range(args.layers)]
     batches = [tuple(v.to(device) for v in bench.make_tokens(l * 97 + rank, wl, T, device))
                for l in range(args.layers)]
@@ -314,7 +330,8 @@ def run_bench(args, rank, world, local, wl):
                        "parallelism": f"ep{world}: {per} experts per GPU; replicate mode: one NCCL "
                                       f"all-gather of the tokens, one all-to-all of per-token partial "
                                       f"sums, rank-ordered combine",
-                       "routed_experts_per_rank_batch": uniq, "cuda_graphs": used_graphs},
+                       "routed_experts_per_rank_batch": uniq, "cuda_graphs": used_graphs,
+                       "col_blocks": layers[0]._bufs and next(iter(layers[0]._bufs.values()))["nb"]},
             "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * 4,
                     "ms_per_step": e2e_ms},

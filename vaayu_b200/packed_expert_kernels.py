@@ -569,21 +569,24 @@ class ExpertTable:
 
 
 def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *, path=None,
-                contrib=None, h_out=None, w_index=None, workspace=None):
+                contrib=None, h_out=None, w_index=None, workspace=None, expert_base=0, col_blocks=0):
     """The layer over a resident `ExpertTable` with the routing already on the device.
 
     x [T, hidden] act dtype; expert_ids [T, K] int32/int64 (indices into `table`; an id outside
     it is dropped); routing_weights [T, K] (strided views fine); out [T, hidden] fp32, or
     `contrib` [T*K, hidden] fp32 for the per-row weighted contributions (expert-parallel combine
     on the home rank).  path: PATH_DECODE (token-batched GEMV) or PATH_PREFILL (tcgen05); default
-    by call size.  Nothing here synchronises with the host."""
+    by call size.  expert_base: expert_ids are global ids and the table holds [expert_base,
+    expert_base + n) (others drop their slot); expert_ids may be a row-strided view.  col_blocks:
+    tokens per decode pass of an expert in blocks of 8 (1, 2, 4; 0 = from the call size).
+    Nothing here synchronises with the host."""
     dev = _lib.require_cuda(x, expert_ids, routing_weights, out, contrib, what="moe_forward")
     _check_x(x, "moe_forward")
     why = _unsupported(table.geom, x.dtype, table.scale_dtype, routing_weights.dtype)
     if why is not None:
         raise NotImplementedError(f"moe_forward: {why}")
     n_tok, top_k = expert_ids.shape
-    ids = expert_ids if expert_ids.is_contiguous() else expert_ids.contiguous()
+    ids = expert_ids if expert_ids.stride(1) == 1 else expert_ids.contiguous()
     ids_code = _lib.DTYPE_CODE[ids.dtype]
     if out is None and contrib is None:
         out = torch.empty(n_tok, table.hidden, dtype=torch.float32, device=dev)
@@ -593,17 +596,20 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
         c = _make_call(table.geom_s, x, n_tok, top_k, table.n_experts, table.table.data_ptr(),
                        ids.data_ptr(), ids_code, routing_weights, routing_weights.stride(0),
                        routing_weights.stride(1), _lib.ptr(w_index), out, contrib, h_out)
+        c.expert_base, c.col_blocks = int(expert_base), int(col_blocks)
+        c.ids_row_stride = ids.stride(0)
         _enqueue(c, path, dev, workspace)
     return out
 
 
 def moe_workspace_bytes(table: ExpertTable, n_tokens: int, top_k: int, path: int = PATH_DECODE,
-                        contrib: bool = False) -> int:
+                        contrib: bool = False, col_blocks: int = 0) -> int:
     """Scratch bytes one `moe_forward` call of this size needs (to preallocate for graphs)."""
     c = _lib.MoeCall()
     c.geom = ctypes.pointer(table.geom_s)
     c.n_tokens, c.top_k, c.n_experts = n_tokens, top_k, table.n_experts
     c.contrib = 1 if contrib else None
+    c.col_blocks = int(col_blocks)
     return int(_lib.lib().vy_moe_workspace_size(ctypes.byref(c), path))
 
 
