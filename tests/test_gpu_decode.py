@@ -284,3 +284,15 @@ def test_ordered_partial_sum():
     for q in range(1, 5):
         ref += parts[q]
     assert torch.equal(out, ref)
+
+
+@pytest.mark.parametrize("hid,inter,tokens", [pytest.param(7168, 2048, 8, id="deepseek-v3-dims"),
+                                              pytest.param(3072, 1536, 80, id="four-column-blocks")])
+def test_down_grids_larger_than_one_resident_wave(hid, inter, tokens):
+    """DeepSeek-V3-shaped rows (448 down tiles) and a 4-column-block call (one CTA per SM): the
+    down kernel loops its resident grid over more (tile, chunk) items than it has CTAs."""
+    blobs, x, idx, w = _batched(hid, inter, 128, 16, 4, tokens, seed=13)
+    got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=vb.PATH_DECODE).cpu().numpy()
+    ref = T.oracle_layer(blobs, x, idx, w)
+    assert T.rel_l2(got, ref) <= 1e-3
+    assert T.max_abs_over_rms(got, ref) <= 2e-2

@@ -364,19 +364,16 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
     cp_async_wait<0>();
 }
 
+// One (row tile, chunk) of the down projection; the kernel below loops a resident grid over them.
 template <int ACT, int SC, bool ZERO, int NB>
-__global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(DownParams p) {
+__device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chunk) {
     extern __shared__ uint4 ring[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
     uint4* my_ring = ring + warp * (kDnDepth * 2 * 32);
     __shared__ UnitQueue<NB, kDnDepth> queue;
     float* ybuf = reinterpret_cast<float*>(ring + kWarps * kDnDepth * 2 * 32);
-    const int n_tiles = p.hidden / kTileRows;
-    const int tile = blockIdx.x % n_tiles, chunk = blockIdx.x / n_tiles;
     const int wstride = kWarps * p.n_chunks;   // passes: pg = chunk*kWarps + warp + q*wstride
-
-    grid_dependency_wait();
 
     const int n_live = p.counters[0];
     const int n_pass = n_live > 0 ? p.unit_start[n_live] : 0;
@@ -550,6 +547,19 @@ __global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(D
     }
 }
 
+// The down projection: a grid of at most one resident wave, each CTA taking (row tile, chunk)
+// work items in turn (a grid a fraction of a wave larger would run a second, mostly empty wave).
+template <int ACT, int SC, bool ZERO, int NB>
+__global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(DownParams p) {
+    grid_dependency_wait();
+    const int n_tiles = p.hidden / kTileRows;
+    const int items = n_tiles * p.n_chunks;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        down_tile<ACT, SC, ZERO, NB>(p, it % n_tiles, it / n_tiles);
+        __syncthreads();   // the ring, queue and contribution buffer are reused by the next item
+    }
+}
+
 // ── host side ─────────────────────────────────────────────────────────────────────────────
 
 size_t gu_smem() { return size_t(kWarps) * kGuDepth * 4 * 32 * sizeof(uint4); }
@@ -593,7 +603,8 @@ int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, size_
     cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_grid, gu_smem(), s, gu);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
     if (timed) cudaEventRecord(ev[2], s);
-    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, (dn.hidden / kTileRows) * dn.n_chunks, dn_smem, s, dn);
+    const int dn_items = (dn.hidden / kTileRows) * dn.n_chunks, dn_slots = kDnBlocksPerSm[NB] * sm_count;
+    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn_items < dn_slots ? dn_items : dn_slots, dn_smem, s, dn);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "down launch: %s", cudaGetErrorString(e));
     return check_launch("vy_moe_decode");
 }
