@@ -236,6 +236,28 @@ typedef struct vy_moe_call {
  */
 int vy_sum_ordered(const float* parts, int32_t n_parts, int64_t n, float* out, void* stream);
 
+/*
+ * Error flags of the last vy_moe_decode (path 0) / vy_moe_prefill (path 1) call made with this
+ * call structure and workspace, copied (enqueued on `stream`) to `out` (device or host int32):
+ *   VY_FLAG_BAD_EXPERT  a routed expert's streams were unusable (null or misaligned pointer);
+ *                       its slots contributed nothing
+ *   VY_FLAG_TIMEOUT     a device-side barrier wait ran out (bounded, never a hang); the work item
+ *                       it belonged to was abandoned and its output is not valid
+ *   VY_FLAG_DRAIN       draining in-flight copies after such a timeout ran out as well
+ * 0 = clean.  The routing plan of every call clears them.  No counterpart in the reference.
+ */
+#define VY_FLAG_BAD_EXPERT 1
+#define VY_FLAG_TIMEOUT 4
+#define VY_FLAG_DRAIN 8
+int vy_moe_error_flags(const vy_moe_call* call, int32_t path, int32_t* out, void* stream);
+
+/*
+ * Self-test of the failure path: one CTA runs the kernels' bounded barrier wait on a barrier that
+ * expects two arrivals and gets `arrivals` (0-2).  With fewer than two the wait gives up after
+ * `limit_ns` (<= 2 s) and ORs VY_FLAG_TIMEOUT into *flags (device int32); the context stays usable.
+ */
+int vy_selftest_bounded_wait(int32_t arrivals, int64_t limit_ns, int32_t* flags, void* stream);
+
 /* Bytes of workspace vy_moe_decode (path 0) / vy_moe_prefill (path 1) need for `call`. */
 size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path);
 

@@ -153,3 +153,40 @@ def test_replicate_mode_is_the_rank_ordered_sum_of_per_rank_partials(tmp_path):
         assert exact, f"rank {r}: not the rank-ordered partial sum"
         assert repeat, f"rank {r}: two calls differ"
         assert rel < 1e-5, f"rank {r}: {rel} of RMS from the single-process layer"
+
+
+# ── failure detection: a rank that never joins the exchange ──────────────────────────────────
+
+def _dropped_worker(rank, port, result_dir):
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=3))
+    try:
+        from vaayu_b200.ep import ExpertParallelLayer
+        _experts, toks = _setup()
+        if rank == 1:
+            time.sleep(6)          # never reaches the collective before rank 0's timeout
+            return
+        layer = ExpertParallelLayer(None, E, hidden=H, mode="replicate",
+                                    layer_fn=lambda xa, lo, wa: torch.zeros(xa.shape[0], H))
+        x, ids, w = toks[0]
+        t0 = time.time()
+        try:
+            layer.forward(x, ids, w)
+            outcome = 0.0
+        except Exception:      # noqa: BLE001 -- the timeout surfaces as an exception, not a hang
+            outcome = 1.0
+        np.save(os.path.join(result_dir, "dropped.npy"), np.array([outcome, time.time() - t0]))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:      # noqa: BLE001
+            pass
+
+
+def test_a_rank_that_never_joins_makes_the_others_raise_not_hang(tmp_path):
+    mp.spawn(_dropped_worker, args=(_free_port(), str(tmp_path)), nprocs=2, join=True)
+    raised, seconds = np.load(tmp_path / "dropped.npy")
+    assert raised == 1.0, "the exchange with a missing rank must raise"
+    assert seconds < 30

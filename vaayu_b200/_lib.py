@@ -61,6 +61,8 @@ SIGNATURES = {
     "vy_moe_prefill": (ctypes.c_int, [ctypes.POINTER(MoeCall), P]),
     "vy_moe_combine": (ctypes.c_int, [P, P, I32T, I64T, I32T, I64T, P, I64T, P]),
     "vy_sum_ordered": (ctypes.c_int, [P, I32T, I64T, P, P]),
+    "vy_moe_error_flags": (ctypes.c_int, [ctypes.POINTER(MoeCall), I32T, P, P]),
+    "vy_selftest_bounded_wait": (ctypes.c_int, [I32T, I64T, P, P]),
 }
 
 _LIB = None

@@ -743,6 +743,22 @@ int validate_call(const vy_moe_call* c) {
 
 using namespace vy;
 
+extern "C" int vy_moe_error_flags(const vy_moe_call* c, int32_t path, int32_t* out, void* stream) {
+    int st;
+    if (!device_info(&st)) return st;
+    if (!c || !c->geom || !c->workspace || !out) return fail(VY_ERR_INVALID, "null call, workspace or output");
+    const int32_t* flags;
+    if (path == 1) {
+        flags = prefill_flags(c);
+    } else {
+        char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 255) & ~uintptr_t(255));
+        flags = decode_layout(c, base, 1).counters + 2;
+    }
+    const cudaError_t e = cudaMemcpyAsync(out, flags, sizeof(int32_t), cudaMemcpyDefault, as_stream(stream));
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "error-flag copy: %s", cudaGetErrorString(e));
+    return VY_OK;
+}
+
 extern "C" size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path) {
     if (!call || !call->geom) return 0;
     if (path == 1) return prefill_workspace_bytes(call);

@@ -62,6 +62,7 @@ int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_
 // Shared validation of a vy_moe_call (decode and prefill entry points).
 int validate_call(const vy_moe_call* c);
 size_t prefill_workspace_bytes(const vy_moe_call* c);
+int32_t* prefill_flags(const vy_moe_call* c);   // the call's error flags in its (prefill) workspace
 
 // Workspace carve-up shared by the decode and prefill entry points.
 struct Carve {

@@ -76,20 +76,25 @@ __device__ __forceinline__ uint64_t now_ns() {
 }
 
 // Bounded wait (try_wait suspends in hardware between polls); false once the CTA has aborted, or
-// after kWaitNs, when it aborts the CTA itself (error bit 4).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int32_t* err) {
+// after `limit_ns`, when it aborts the CTA itself (error bit 4).
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              int32_t* err, uint64_t limit_ns) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = now_ns();
     for (;;) {
         if (mbar_try(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (now_ns() - t0 > kWaitNs) {
+        if (now_ns() - t0 > limit_ns) {
             *abort_flag = 1;
             atomicOr(err, 4);
             return false;
         }
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int32_t* err) {
+    return mbar_wait_for(bar, parity, abort_flag, err, kWaitNs);
 }
 
 // Bounded wait that ignores the abort flag: drains work already issued (TMA loads, MMAs) before
@@ -520,6 +525,21 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     }
 }
 
+// The bounded barrier wait the GEMM kernels use, against a barrier that expects two arrivals and
+// gets `arrivals`: with fewer, the wait runs out after `limit_ns`, sets error bit 4 and the kernel
+// returns -- the failure path, exercised without a fault or a hang.
+__global__ void selftest_wait_kernel(int arrivals, uint64_t limit_ns, int32_t* flags) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 2);
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 0; i < arrivals && i < 2; ++i) mbar_arrive(&bar);
+        mbar_wait_for(&bar, 0, &abort_flag, flags, limit_ns);
+    }
+}
+
 // ── host ────────────────────────────────────────────────────────────────────────────────────
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -633,6 +653,11 @@ int launch_prefill_gemm(int act, int kind, int sc, bool zero, const CUtensorMap&
 
 }  // namespace
 
+int32_t* prefill_flags(const vy_moe_call* c) {
+    char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 1023) & ~uintptr_t(1023));
+    return prefill_layout(c, base).counters + 2;
+}
+
 size_t prefill_workspace_bytes(const vy_moe_call* c) {
     if (!c || !c->geom) return 0;
     return prefill_layout(c, nullptr).bytes + 1024;
@@ -641,6 +666,15 @@ size_t prefill_workspace_bytes(const vy_moe_call* c) {
 }  // namespace vy
 
 using namespace vy;
+
+extern "C" int vy_selftest_bounded_wait(int32_t arrivals, int64_t limit_ns, int32_t* flags, void* stream) {
+    int st;
+    if (!device_info(&st)) return st;
+    if (!flags || limit_ns <= 0 || limit_ns > 2000000000ll)
+        return fail(VY_ERR_INVALID, "flags %p, limit %lld ns (0, 2 s]", static_cast<void*>(flags), (long long)limit_ns);
+    selftest_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(arrivals, static_cast<uint64_t>(limit_ns), flags);
+    return check_launch("vy_selftest_bounded_wait");
+}
 
 extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
     int st;

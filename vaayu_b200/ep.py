@@ -234,8 +234,10 @@ class ExpertParallelLayer:
 
 
 def run_bench(args, rank, world, local, wl):
-    """bench.py's N-GPU arm: configuration 1 at `wl['tokens']` tokens per rank (weak scaling), the
-    128 experts sharded E/N per rank, steps rotating over `args.layers` layers."""
+    """bench.py's N-GPU arm: `wl` (configuration 1 or 3) at `wl['tokens']` tokens per rank (weak
+    scaling), the routed experts sharded E/N per rank, steps rotating over `args.layers` layers.
+    A workload with `shared` experts replicates them on every rank, applies them to the rank's own
+    tokens and adds their output in bf16 (the model epilogue: out.to(bf16) + shared.to(bf16))."""
     import json
     import statistics
 
@@ -250,6 +252,21 @@ def run_bench(args, rank, world, local, wl):
                for l in range(args.layers)]
     out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
     L = args.layers
+    shared = None
+    if wl.get("shared"):
+        from .packed_expert_kernels import PATH_DECODE, ExpertTable, moe_forward
+        sw = dict(wl, experts=1)
+        shared = [ExpertTable(bench.make_layer(5000 + l, sw, device)) for l in range(L)]   # same on all ranks
+        sh_ids = torch.zeros(T, 1, dtype=torch.int32, device=device)
+        sh_w = torch.ones(T, 1, dtype=torch.float32, device=device)
+        sh_out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
+        result = torch.empty(T, wl["hidden"], dtype=torch.bfloat16, device=device)
+
+    def layer_step(l, x, idx, w):
+        layers[l].forward(x, idx, w, out)
+        if shared is not None:
+            moe_forward(x, sh_ids, sh_w, shared[l], out=sh_out, path=PATH_DECODE)
+            torch.add(out.to(torch.bfloat16), sh_out.to(torch.bfloat16), out=result)
 
     # each layer's step (pack, all-gather, kernels, all-to-all, combine) as one CUDA graph over
     # static input buffers; eager calls when capture is not possible here
@@ -259,14 +276,14 @@ def run_bench(args, rank, world, local, wl):
     graphs = []
     for l in range(L):
         for _ in range(2):
-            layers[l].forward(xs[l], ids_[l], ws_[l], out)
+            layer_step(l, xs[l], ids_[l], ws_[l])
     torch.cuda.synchronize(device)
     bench.barrier(world)
     try:
         for l in range(L):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
-                layers[l].forward(xs[l], ids_[l], ws_[l], out)
+                layer_step(l, xs[l], ids_[l], ws_[l])
             graphs.append(g)
         torch.cuda.synchronize(device)
     except Exception as e:  # noqa: BLE001 - report and run eagerly
@@ -280,7 +297,7 @@ def run_bench(args, rank, world, local, wl):
         if graphs:
             graphs[l].replay()
         else:
-            layers[l].forward(xs[l], ids_[l], ws_[l], out)
+            layer_step(l, xs[l], ids_[l], ws_[l])
 
     for i in range(args.warmup):
         step(i)
@@ -291,7 +308,7 @@ def run_bench(args, rank, world, local, wl):
     ms = bench.max_over_ranks(ms, world)
 
     pin = [(x.cpu().pin_memory(), w.cpu().pin_memory(), i.cpu().pin_memory()) for x, w, i in batches]
-    out_h = torch.empty(T, wl["hidden"], dtype=torch.float32).pin_memory()
+    out_h = torch.empty(T, wl["hidden"], dtype=torch.float32 if shared is None else torch.bfloat16).pin_memory()
 
     def e2e_step(i):
         l = i % L
@@ -302,8 +319,8 @@ def run_bench(args, rank, world, local, wl):
         if graphs:
             graphs[l].replay()
         else:
-            layers[l].forward(xs[l], ids_[l], ws_[l], out)
-        out_h.copy_(out, non_blocking=True)
+            layer_step(l, xs[l], ids_[l], ws_[l])
+        out_h.copy_(out if shared is None else result, non_blocking=True)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -331,9 +348,10 @@ def run_bench(args, rank, world, local, wl):
                                       f"all-gather of the tokens, one all-to-all of per-token partial "
                                       f"sums, rank-ordered combine",
                        "routed_experts_per_rank_batch": uniq, "cuda_graphs": used_graphs,
+                       "shared_experts": wl.get("shared", 0),
                        "col_blocks": layers[0]._bufs and next(iter(layers[0]._bufs.values()))["nb"]},
             "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * 4,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * out_h.element_size(),
                     "ms_per_step": e2e_ms},
             "roofline": {"kernel": "layer (expert parallel)", "bound": "hbm", "achieved": None,
                          "peak": peak, "unit": "GB/s", "frac": None, "peak_source": peak_kind,

@@ -568,8 +568,30 @@ class ExpertTable:
         return sum(t.numel() * t.element_size() for i in idx for t in self.blobs[i]["flat"].values())
 
 
+FLAG_BAD_EXPERT, FLAG_TIMEOUT, FLAG_DRAIN = 1, 4, 8
+_FLAG_TEXT = {FLAG_BAD_EXPERT: "a routed expert's streams were unusable (null or misaligned pointer); "
+                               "its slots contributed nothing",
+              FLAG_TIMEOUT: "a device-side barrier wait ran out; part of the output is not valid",
+              FLAG_DRAIN: "draining in-flight copies after a timeout ran out as well"}
+
+
+def describe_flags(flags: int) -> str:
+    return "; ".join(t for b, t in _FLAG_TEXT.items() if flags & b) or "clean"
+
+
+def _check_flags(c, path, dev) -> None:
+    """Synchronising read of a call's device error flags; raises RuntimeError when any is set."""
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    _lib.check(_lib.lib().vy_moe_error_flags(ctypes.byref(c), path, flags.data_ptr(), _lib.stream_of(dev)),
+               "vy_moe_error_flags")
+    v = int(flags.item())
+    if v:
+        raise RuntimeError(f"moe_forward: device error flags {v:#x}: {describe_flags(v)}")
+
+
 def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *, path=None,
-                contrib=None, h_out=None, w_index=None, workspace=None, expert_base=0, col_blocks=0):
+                contrib=None, h_out=None, w_index=None, workspace=None, expert_base=0, col_blocks=0,
+                check=False):
     """The layer over a resident `ExpertTable` with the routing already on the device.
 
     x [T, hidden] act dtype; expert_ids [T, K] int32/int64 (indices into `table`; an id outside
@@ -579,7 +601,8 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     by call size.  expert_base: expert_ids are global ids and the table holds [expert_base,
     expert_base + n) (others drop their slot); expert_ids may be a row-strided view.  col_blocks:
     tokens per decode pass of an expert in blocks of 8 (1, 2, 4; 0 = from the call size).
-    Nothing here synchronises with the host."""
+    Nothing here synchronises with the host -- except `check=True`, which reads the call's device
+    error flags afterwards and raises RuntimeError when any is set."""
     dev = _lib.require_cuda(x, expert_ids, routing_weights, out, contrib, what="moe_forward")
     _check_x(x, "moe_forward")
     why = _unsupported(table.geom, x.dtype, table.scale_dtype, routing_weights.dtype)
@@ -599,6 +622,8 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
         c.expert_base, c.col_blocks = int(expert_base), int(col_blocks)
         c.ids_row_stride = ids.stride(0)
         _enqueue(c, path, dev, workspace)
+        if check:
+            _check_flags(c, path, dev)
     return out
 
 
