@@ -41,6 +41,9 @@ import torch  # noqa: E402
 METRIC = "int4 MoE expert-layer tokens/s and % HBM/tensor roofline at 1/2/4/8 B200"
 WORKLOAD = dict(name="cfg1: Qwen3-30B-A3B-shaped int4 MoE layer, decode", hidden=2048, inter=768,
                 experts=128, top_k=8, tokens=32, group=128)
+CFG3 = dict(name="cfg3: DeepSeek-V3-shaped int4 MoE layer (256 routed experts, top-8, 1 shared), "
+                 "expert-parallel decode", hidden=7168, inter=2048, experts=256, top_k=8, tokens=64,
+            group=128, shared=1)
 PREFILL = dict(name="cfg2: Mixtral-8x7B-shaped int4 MoE layer, prefill", hidden=4096, inter=14336,
                experts=8, top_k=2, tokens=2048, group=128, skew=0.9)
 PEAKS = ROOT / "MEASURED_PEAKS.json"
@@ -339,9 +342,9 @@ def run_ours(args, rank, world, local):
     device = torch.device("cuda", local)
     wl = dict(WORKLOAD)
     T, K = wl["tokens"], wl["top_k"]
-    if world > 1:
+    if world > 1 or args.workload == "cfg3":
         from vaayu_b200 import ep
-        return ep.run_bench(args, rank, world, local, wl)
+        return ep.run_bench(args, rank, world, local, CFG3 if args.workload == "cfg3" else wl)
     if args.profile == "prefill":
         return prefill_bench(args, device)
 
@@ -579,6 +582,9 @@ def main():
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the configuration-2 prefill measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--workload", default="cfg1", choices=("cfg1", "cfg3"),
+                    help="cfg1 (default): the headline decode workload (expert-parallel for N > 1); "
+                         "cfg3: DeepSeek-V3 shape, expert-parallel at any N")
     ap.add_argument("--ep-col-blocks", type=int, default=None, choices=(1, 2, 4),
                     help="tokens per expert pass (x8) in the expert-parallel step; default by load")
     args = ap.parse_args()
