@@ -296,3 +296,28 @@ def test_down_grids_larger_than_one_resident_wave(hid, inter, tokens):
     ref = T.oracle_layer(blobs, x, idx, w)
     assert T.rel_l2(got, ref) <= 1e-3
     assert T.max_abs_over_rms(got, ref) <= 2e-2
+
+
+def test_a_layer_read_from_a_checkpoint_computes_the_same_output(tmp_path):
+    from vaayu_b200 import checkpoint as ck
+    from vaayu_b200 import synthetic
+    g = torch.Generator().manual_seed(31)
+    tensors, blobs = {}, []
+    for e in range(8):
+        by_role = synthetic.make_expert(1024, 512, g, group=128)
+        for role, seg in (("gate", "gate_proj"), ("down", "down_proj"), ("up", "up_proj")):
+            for comp, t in by_role[role].items():
+                tensors[f"model.layers.0.mlp.experts.{e}.{seg}.{comp}"] = t
+        blobs.append(vb.build_expert_blob({r: {k: (v if k == "weight_shape" else v.cuda()) for k, v in c.items()}
+                                           for r, c in by_role.items()}))
+    ck.write_safetensors(str(tmp_path / "m.safetensors"), tensors)
+    cp = ck.Checkpoint(str(tmp_path / "m.safetensors"))
+    try:
+        table = cp.layer_table("model.layers.0.mlp")
+        x = torch.randn(6, 1024, generator=g).to(torch.bfloat16).cuda()
+        w, idx = torch.topk(torch.randn(6, 8, generator=g).softmax(-1), 2, -1)
+        w, idx = w.cuda(), idx.cuda()
+        assert torch.equal(vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE),
+                           vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=vb.PATH_DECODE))
+    finally:
+        cp.close()

@@ -7,6 +7,7 @@ torch or Triton fallback: calls on CPU tensors or geometry the kernels do not ta
 """
 from .block_scaled import (dequantize_block_scaled, dequantize_fp4_block_scaled, fp4_gemv,
                            fp8_gemv)
+from .checkpoint import Checkpoint, group_packed_tensors_by_weight, packed_roles_complete
 from .moe_patch import (accumulate_expert_outputs, build_expert_blob, compute_expert_dispatch,
                         dequantize_expert_blob, dequantize_expert_weights,
                         dequantize_packed_weight, expert_weights_from_entry, route_experts,
@@ -17,11 +18,12 @@ from .packed_expert_kernels import (PATH_DECODE, PATH_PREFILL, ExpertTable, comb
                                     packed_experts_decode_graphed, packed_experts_prefill)
 
 __all__ = [
-    "PATH_DECODE", "PATH_PREFILL", "ExpertTable", "accumulate_expert_outputs",
+    "PATH_DECODE", "PATH_PREFILL", "Checkpoint", "ExpertTable", "accumulate_expert_outputs",
     "build_expert_blob", "combine", "compute_expert_dispatch", "dequantize_block_scaled",
     "dequantize_expert_blob", "dequantize_expert_weights", "dequantize_fp4_block_scaled",
     "dequantize_packed_weight", "expert_weights_from_entry", "fp4_gemv", "fp8_gemv",
-    "install_packed_expert_kernels", "moe_forward", "moe_workspace_bytes",
+    "group_packed_tensors_by_weight", "install_packed_expert_kernels", "moe_forward",
+    "moe_workspace_bytes", "packed_roles_complete",
     "packed_experts_decode", "packed_experts_decode_graphed", "packed_experts_prefill",
     "route_experts", "route_permute", "topk_softmax", "unpack_int32_to_int8",
 ]
