@@ -321,3 +321,27 @@ def test_a_layer_read_from_a_checkpoint_computes_the_same_output(tmp_path):
                            vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=vb.PATH_DECODE))
     finally:
         cp.close()
+
+
+@pytest.mark.parametrize("gated", [False, True], ids=["deepseek-ungated", "qwen-sigmoid-gated"])
+def test_the_shared_expert_joins_like_the_model_epilogue(gated):
+    """result = routed_sum.to(bf16) + shared.to(bf16); gated: sigmoid(gate) * shared in bf16."""
+    routed, x, idx, w = _batched(1024, 512, 128, 8, 2, 10, seed=17)
+    shared = T.make_blobs(1024, 512, 1, gs=128, seed=99)
+    gate = torch.sigmoid(torch.randn(10, 1, generator=torch.Generator().manual_seed(5))).to(torch.bfloat16).cuda() \
+        if gated else None
+    got = vb.moe_forward_with_shared(x, idx, w, pk.ExpertTable(routed), pk.ExpertTable(shared), gate=gate)
+    r = torch.from_numpy(T.oracle_layer(routed, x, idx, w))
+    sh_w = gate.float().cpu() if gated else torch.ones(10, 1)
+    s = torch.from_numpy(T.oracle_layer(shared, x, torch.zeros(10, 1, dtype=torch.long),
+                                        sh_w.to(torch.bfloat16) if gated else sh_w))
+    ref = (r.to(torch.bfloat16) + s.to(torch.bfloat16)).float().numpy()
+    g = got.float().cpu().numpy()
+    assert got.dtype == torch.bfloat16
+    assert T.rel_l2(g, ref) <= 2e-3
+    # each bf16 term (routed sum, shared output) may sit one bf16 step from the oracle's, and the
+    # sum rounds once more: at most 2^-7 of |routed| + |shared| + |result| (cancellation included)
+    rb, sb = r.to(torch.bfloat16).float().numpy(), s.to(torch.bfloat16).float().numpy()
+    rms = float(np.sqrt(np.mean(ref ** 2)))
+    bound = 2.0 ** -7 * (np.abs(rb) + np.abs(sb) + np.abs(ref)) + 1e-3 * rms
+    assert np.all(np.abs(g - ref) <= bound)

@@ -13,7 +13,8 @@ from .moe_patch import (accumulate_expert_outputs, build_expert_blob, compute_ex
                         dequantize_packed_weight, expert_weights_from_entry, route_experts,
                         route_permute, topk_softmax, unpack_int32_to_int8)
 from .packed_expert_kernels import (PATH_DECODE, PATH_PREFILL, ExpertTable, combine,
-                                    install_packed_expert_kernels, moe_forward,
+                                    install_packed_expert_kernels, moe_forward, moe_forward_with_shared,
+                                    shared_expert_forward,
                                     moe_workspace_bytes, packed_experts_decode,
                                     packed_experts_decode_graphed, packed_experts_prefill)
 
@@ -23,7 +24,7 @@ __all__ = [
     "dequantize_expert_blob", "dequantize_expert_weights", "dequantize_fp4_block_scaled",
     "dequantize_packed_weight", "expert_weights_from_entry", "fp4_gemv", "fp8_gemv",
     "group_packed_tensors_by_weight", "install_packed_expert_kernels", "moe_forward",
-    "moe_workspace_bytes", "packed_roles_complete",
+    "moe_forward_with_shared", "moe_workspace_bytes", "packed_roles_complete", "shared_expert_forward",
     "packed_experts_decode", "packed_experts_decode_graphed", "packed_experts_prefill",
     "route_experts", "route_permute", "topk_softmax", "unpack_int32_to_int8",
 ]

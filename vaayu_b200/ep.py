@@ -254,18 +254,17 @@ def run_bench(args, rank, world, local, wl):
     L = args.layers
     shared = None
     if wl.get("shared"):
-        from .packed_expert_kernels import PATH_DECODE, ExpertTable, moe_forward
+        from .packed_expert_kernels import PATH_DECODE, ExpertTable, moe_workspace_bytes, shared_expert_forward
         sw = dict(wl, experts=1)
         shared = [ExpertTable(bench.make_layer(5000 + l, sw, device)) for l in range(L)]   # same on all ranks
-        sh_ids = torch.zeros(T, 1, dtype=torch.int32, device=device)
-        sh_w = torch.ones(T, 1, dtype=torch.float32, device=device)
         sh_out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
+        sh_ws = torch.empty(moe_workspace_bytes(shared[0], T, 1, path=PATH_DECODE), dtype=torch.uint8, device=device)
         result = torch.empty(T, wl["hidden"], dtype=torch.bfloat16, device=device)
 
     def layer_step(l, x, idx, w):
         layers[l].forward(x, idx, w, out)
         if shared is not None:
-            moe_forward(x, sh_ids, sh_w, shared[l], out=sh_out, path=PATH_DECODE)
+            shared_expert_forward(x, shared[l], out=sh_out, workspace=sh_ws)
             torch.add(out.to(torch.bfloat16), sh_out.to(torch.bfloat16), out=result)
 
     # each layer's step (pack, all-gather, kernels, all-to-all, combine) as one CUDA graph over

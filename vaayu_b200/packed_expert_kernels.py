@@ -627,6 +627,28 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     return out
 
 
+def shared_expert_forward(x, shared: ExpertTable, gate=None, out=None, *, workspace=None):
+    """The always-on shared expert of a MoE block on the kernels (`_shared_expert_output`,
+    vaayu/moe_patch.py:554-580): `shared` is a one-expert table.  Ungated (DeepSeek): the expert's
+    output act(h . Wd) in fp32.  Gated (Qwen2 / Qwen3-Next): `gate` [T] or [T, 1] holds
+    sigmoid(gate logits) in the activation dtype, and the product rounds to it as the model's
+    `sigmoid(gate(x)) * shared(x)` does.  Returns out [T, hidden] fp32."""
+    dev = x.device
+    T = x.shape[0]
+    ids = torch.zeros(T, 1, dtype=torch.int32, device=dev)
+    w = torch.ones(T, 1, dtype=torch.float32, device=dev) if gate is None else gate.reshape(T, 1)
+    return moe_forward(x, ids, w, shared, out=out, path=PATH_DECODE, workspace=workspace)
+
+
+def moe_forward_with_shared(x, expert_ids, routing_weights, table: ExpertTable, shared: ExpertTable,
+                            gate=None, out=None, **kw):
+    """The routed layer plus the shared expert, combined as the reference's epilogue does
+    (`_tail`, vaayu/packed_expert_kernels.py:502-508): out.to(act) + shared.to(act).  Returns the
+    act-dtype result; `out` (optional) receives the routed fp32 sum."""
+    out = moe_forward(x, expert_ids, routing_weights, table, out=out, **kw)
+    return _tail(out, x.dtype, shared_expert_forward(x, shared, gate))
+
+
 def moe_workspace_bytes(table: ExpertTable, n_tokens: int, top_k: int, path: int = PATH_DECODE,
                         contrib: bool = False, col_blocks: int = 0) -> int:
     """Scratch bytes one `moe_forward` call of this size needs (to preallocate for graphs)."""
