@@ -55,11 +55,9 @@ struct GateUpParams {
 
 struct DownParams {
     int hidden, inter, gs_shift, top_k;
-    int64_t n_tokens;
     int64_t w_off, s_off, z_off;
     const PassEntry* passes;
     const int32_t* unit_start;
-    const int32_t* slot_order;
     int32_t* counters;
     const uint16_t* h_perm;
     const void* weights;
@@ -67,12 +65,7 @@ struct DownParams {
     bool w_round;
     int64_t w_tok_stride, w_slot_stride;
     const int32_t* w_index;
-    float* out;
-    int64_t out_stride;
-    float* ybuf_g;        // non-null: contributions to global [n][hidden] instead of shared memory
-    bool global_combine;  // with ybuf_g: the last CTA of each row tile sums it into `out`
-    int n_chunks;         // CTAs sharing one row tile (its expert passes interleaved over them)
-    int32_t* tile_done;   // [hidden / 16] tickets, zeroed by the plan kernel of the same call
+    float* ybuf_g;        // [n][hidden] weighted contributions, by row id (token * top_k + slot)
 };
 
 // What a warp needs about one unit of work: a pass of a live expert (and, for gate/up, a 16-row
@@ -364,29 +357,40 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
     cp_async_wait<0>();
 }
 
-// One (row tile, chunk) of the down projection; the kernel below loops a resident grid over them.
+// The down projection, pass-major like gate/up: unit u = (pass u / tiles, 16-row tile u % tiles)
+// dealt round-robin over every warp of one resident wave, so the eight warps of a CTA work on
+// the same pass (the same h rows, shared through L1) and no warp has more than one unit above
+// the average.  Each unit writes its 16 rows x (up to NB*8) weighted contributions to
+// ybuf_g[row id][hidden]; the slot-ordered combine (or the expert-parallel caller) sums them.
 template <int ACT, int SC, bool ZERO, int NB>
-__device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chunk) {
+__global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(DownParams p) {
     extern __shared__ uint4 ring[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
     uint4* my_ring = ring + warp * (kDnDepth * 2 * 32);
     __shared__ UnitQueue<NB, kDnDepth> queue;
-    float* ybuf = reinterpret_cast<float*>(ring + kWarps * kDnDepth * 2 * 32);
-    const int wstride = kWarps * p.n_chunks;   // passes: pg = chunk*kWarps + warp + q*wstride
+
+    grid_dependency_wait();
 
     const int n_live = p.counters[0];
-    const int n_pass = n_live > 0 ? p.unit_start[n_live] : 0;
-    const int pg0 = chunk * kWarps + warp;
-    const int my_units = pg0 < n_pass ? (n_pass - pg0 + wstride - 1) / wstride : 0;
+    if (n_live <= 0) return;
+    const int tiles = p.hidden / kTileRows;
+    const int total_units = p.unit_start[n_live] * tiles;
+    const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+    if (gw >= total_units) return;
+    const int my_units = (total_units - gw + nw - 1) / nw;
     const int spu = p.inter / kStageK;
     const int wpr = p.inter / 8;
     const int groups = p.inter >> p.gs_shift;
-    auto unit_at = [&](int i) { return load_unit<NB>(p.passes, pg0 + i * wstride, tile, g); };
+    auto unit_at = [&](int i) {
+        const int u = gw + i * nw;
+        const int pg = u / tiles;
+        return load_unit<NB>(p.passes, pg, u - pg * tiles, g);
+    };
 
+    // ── issue side: kDnDepth - 1 stages ahead of the consuming side ─────────────────────────
     int i_ui = 0, i_ks = 0, i_slot = 0, i_left = my_units * spu;
-    UnitInfo<NB> i_nxt{};
-    if (my_units > 0) i_nxt = unit_at(0);
+    UnitInfo<NB> i_nxt = unit_at(0);
     const int32_t* i_src = nullptr;
     bool i_ok = false;
     auto issue = [&]() {
@@ -396,7 +400,7 @@ __device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chu
                 queue.put(warp, i_ui % kDnDepth, lane, g, cur);
                 if (i_ui + 1 < my_units) i_nxt = unit_at(i_ui + 1);
                 i_ok = cur.ok;
-                i_src = cur.pk + p.w_off + int64_t(tile * kTileRows + g) * wpr + tig * 4;
+                i_src = cur.pk + p.w_off + int64_t(cur.tile * kTileRows + g) * wpr + tig * 4;
             }
             if (i_ok) {
                 uint4* dst = my_ring + i_slot * 64 + lane;
@@ -416,6 +420,7 @@ __device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chu
 #pragma unroll
     for (int s = 0; s < kDnDepth - 1; ++s) issue();
 
+    // ── consuming side ───────────────────────────────────────────────────────────────────
     float acc[NB][4];
 #pragma unroll
     for (int cb = 0; cb < NB; ++cb)
@@ -424,15 +429,16 @@ __device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chu
     UnitInfo<NB> cu{};
     int c_ui = 0, c_ks = 0, c_slot = 0;
     int hoff[NB];
-    const int row = tile * kTileRows + g;
-    const int sidx0 = static_cast<int>(p.s_off) + row * groups, sidx8 = sidx0 + 8 * groups;
-    const int zidx = static_cast<int>(p.z_off) + (row >> 3) * groups;
+    int sidx0 = 0, zidx = 0;
     const int kfirst = tig * 32;
     for (int s = my_units * spu; s > 0; --s) {
         issue();
         if (c_ks == 0) {
             __syncwarp();
             cu = queue.get(warp, c_ui % kDnDepth, g);
+            const int row = cu.tile * kTileRows + g;
+            sidx0 = static_cast<int>(p.s_off) + row * groups;
+            zidx = static_cast<int>(p.z_off) + (row >> 3) * groups;
 #pragma unroll
             for (int cb = 0; cb < NB; ++cb)
                 hoff[cb] = cu.col_row[cb] >= 0 ? cu.col_row[cb] * p.inter + kfirst : -1;
@@ -449,7 +455,7 @@ __device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chu
             const uint4 w0 = st[0], w8 = st[32];
             const int grp = (kh + kfirst) >> p.gs_shift;
             const uint32_t s0 = scale_pair<ACT, SC>(cu.sc, sidx0 + grp);
-            const uint32_t s8 = scale_pair<ACT, SC>(cu.sc, sidx8 + grp);
+            const uint32_t s8 = scale_pair<ACT, SC>(cu.sc, sidx0 + 8 * groups + grp);
             const uint32_t b0 = bias_pair<ACT, ZERO>(cu.zp, zidx + grp, g);
             const uint32_t b8 = bias_pair<ACT, ZERO>(cu.zp, zidx + groups + grp, g);
             float sp[NB][4];   // the stage's partial dots (see gate_up_kernel)
@@ -493,7 +499,7 @@ __device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chu
                         const int col = cb * 8 + 2 * tig + (i & 1);
                         const int rowid = __shfl_sync(0xffffffffu, cu.col_row[cb], (col - cb * 8) * 4);
                         if (col < cu.ncols) {
-                            const int r = g + 8 * (i >> 1);
+                            const int r = cu.tile * kTileRows + g + 8 * (i >> 1);
                             const int64_t t = rowid / p.top_k;
                             const int k = rowid - int(t) * p.top_k;
                             const int widx = p.w_index ? p.w_index[rowid] : k;
@@ -501,8 +507,7 @@ __device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chu
                                                            t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
                             float c = __fmul_rn(round_act<ACT>(acc[cb][i]), wv);
                             if (p.w_round) c = round_act<ACT>(c);
-                            if (p.ybuf_g) p.ybuf_g[int64_t(rowid) * p.hidden + tile * kTileRows + r] = c;
-                            else ybuf[rowid * kTileRows + r] = c;
+                            p.ybuf_g[int64_t(rowid) * p.hidden + r] = c;
                         }
                     }
                 }
@@ -516,55 +521,12 @@ __device__ __forceinline__ void down_tile(const DownParams& p, int tile, int chu
         }
     }
     cp_async_wait<0>();
-    if (p.ybuf_g && !p.global_combine) return;   // per-row contributions only (expert parallel)
-    __shared__ int s_last;
-    if (p.ybuf_g) {
-        // the last CTA of this row tile to finish sums it: publish, then take a ticket
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            s_last = atomicAdd(p.tile_done + tile, 1) == p.n_chunks - 1;
-        }
-        __syncthreads();
-        if (!s_last) return;
-        __threadfence();
-    } else {
-        __syncthreads();
-    }
-    // each token's 16 columns: contributions in ascending expert id, then slot
-    const int K = p.top_k;
-    for (int64_t idx = threadIdx.x; idx < p.n_tokens * kTileRows; idx += blockDim.x) {
-        const int64_t t = idx / kTileRows;
-        const int r = static_cast<int>(idx - t * kTileRows);
-        float a = 0.f;
-        for (int k = 0; k < K; ++k) {
-            const int rowid = p.slot_order[t * K + k];
-            if (rowid < 0) continue;
-            a += p.ybuf_g ? __ldcg(p.ybuf_g + int64_t(rowid) * p.hidden + tile * kTileRows + r)
-                          : ybuf[rowid * kTileRows + r];
-        }
-        p.out[t * p.out_stride + tile * kTileRows + r] = a;
-    }
-}
-
-// The down projection: a grid of at most one resident wave, each CTA taking (row tile, chunk)
-// work items in turn (a grid a fraction of a wave larger would run a second, mostly empty wave).
-template <int ACT, int SC, bool ZERO, int NB>
-__global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(DownParams p) {
-    grid_dependency_wait();
-    const int n_tiles = p.hidden / kTileRows;
-    const int items = n_tiles * p.n_chunks;
-    for (int it = blockIdx.x; it < items; it += gridDim.x) {
-        down_tile<ACT, SC, ZERO, NB>(p, it % n_tiles, it / n_tiles);
-        __syncthreads();   // the ring, queue and contribution buffer are reused by the next item
-    }
 }
 
 // ── host side ─────────────────────────────────────────────────────────────────────────────
 
 size_t gu_smem() { return size_t(kWarps) * kGuDepth * 4 * 32 * sizeof(uint4); }
-size_t dn_ring_smem() { return size_t(kWarps) * kDnDepth * 2 * 32 * sizeof(uint4); }
-constexpr size_t kDnSmemCap = 200 * 1024;
+size_t dn_smem() { return size_t(kWarps) * kDnDepth * 2 * 32 * sizeof(uint4); }
 
 template <typename Kernel, typename Params>
 cudaError_t launch_pdl(Kernel kernel, int grid, size_t smem, cudaStream_t s, const Params& prm) {
@@ -582,66 +544,66 @@ cudaError_t launch_pdl(Kernel kernel, int grid, size_t smem, cudaStream_t s, con
 }
 
 template <int ACT, int SC, bool ZERO, int NB>
-int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, size_t dn_smem,
-               cudaStream_t s, cudaEvent_t const* ev, bool timed) {
-    // Resident CTAs per SM of the persistent gate/up grid, from the occupancy calculator (the
-    // warp -> unit assignment is static, so the whole grid must be resident at once).
-    static int gu_blocks_per_sm = 0;
+int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaStream_t s,
+               cudaEvent_t const* ev, bool timed) {
+    // Resident CTAs per SM of the persistent grids, from the occupancy calculator (the warp ->
+    // unit assignment is static, so each whole grid must be resident at once).
+    static int gu_blocks_per_sm = 0, dn_blocks_per_sm = 0;
     if (gu_blocks_per_sm == 0) {
         cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(gu_smem()));
         cudaFuncSetAttribute(down_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kDnSmemCap));
-        int nblk = 0;
+                             static_cast<int>(dn_smem()));
+        int nblk = 0, ndn = 0;
         cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
             &nblk, gate_up_kernel<ACT, SC, ZERO, NB>, kWarps * 32, gu_smem());
-        if (oe != cudaSuccess || nblk < 1)
-            return fail(VY_ERR_CUDA, "gate/up occupancy: %s", cudaGetErrorString(oe));
+        if (oe == cudaSuccess)
+            oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ndn, down_kernel<ACT, SC, ZERO, NB>, kWarps * 32,
+                                                               dn_smem());
+        if (oe != cudaSuccess || nblk < 1 || ndn < 1)
+            return fail(VY_ERR_CUDA, "decode occupancy: %s", cudaGetErrorString(oe));
         gu_blocks_per_sm = nblk;
+        dn_blocks_per_sm = ndn;
     }
-    const int gu_grid = gu_blocks_per_sm * sm_count;
-    cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_grid, gu_smem(), s, gu);
+    cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_blocks_per_sm * sm_count, gu_smem(), s, gu);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
     if (timed) cudaEventRecord(ev[2], s);
-    const int dn_items = (dn.hidden / kTileRows) * dn.n_chunks, dn_slots = kDnBlocksPerSm[NB] * sm_count;
-    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn_items < dn_slots ? dn_items : dn_slots, dn_smem, s, dn);
+    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn_blocks_per_sm * sm_count, dn_smem(), s, dn);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "down launch: %s", cudaGetErrorString(e));
     return check_launch("vy_moe_decode");
 }
 
 template <int ACT, int SC, bool ZERO>
-int dispatch_nb(int nb, const GateUpParams& gu, const DownParams& dn, int sm_count, size_t dn_smem,
+int dispatch_nb(int nb, const GateUpParams& gu, const DownParams& dn, int sm_count,
                 cudaStream_t s, cudaEvent_t const* ev, bool timed) {
-    if (nb == 1) return run_decode<ACT, SC, ZERO, 1>(gu, dn, sm_count, dn_smem, s, ev, timed);
-    if (nb == 2) return run_decode<ACT, SC, ZERO, 2>(gu, dn, sm_count, dn_smem, s, ev, timed);
-    return run_decode<ACT, SC, ZERO, 4>(gu, dn, sm_count, dn_smem, s, ev, timed);
+    if (nb == 1) return run_decode<ACT, SC, ZERO, 1>(gu, dn, sm_count, s, ev, timed);
+    if (nb == 2) return run_decode<ACT, SC, ZERO, 2>(gu, dn, sm_count, s, ev, timed);
+    return run_decode<ACT, SC, ZERO, 4>(gu, dn, sm_count, s, ev, timed);
 }
 
 template <int ACT, int SC>
 int dispatch_zero(bool zero, int nb, const GateUpParams& gu, const DownParams& dn, int sm_count,
-                  size_t dn_smem, cudaStream_t s, cudaEvent_t const* ev, bool timed) {
-    return zero ? dispatch_nb<ACT, SC, true>(nb, gu, dn, sm_count, dn_smem, s, ev, timed)
-                : dispatch_nb<ACT, SC, false>(nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+                  cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+    return zero ? dispatch_nb<ACT, SC, true>(nb, gu, dn, sm_count, s, ev, timed)
+                : dispatch_nb<ACT, SC, false>(nb, gu, dn, sm_count, s, ev, timed);
 }
 
 template <int ACT>
 int dispatch_sc(int sc, bool zero, int nb, const GateUpParams& gu, const DownParams& dn, int sm_count,
-                size_t dn_smem, cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+                cudaStream_t s, cudaEvent_t const* ev, bool timed) {
     switch (sc) {
-        case VY_BF16: return dispatch_zero<ACT, VY_BF16>(zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
-        case VY_F16: return dispatch_zero<ACT, VY_F16>(zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
-        default: return dispatch_zero<ACT, VY_F32>(zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+        case VY_BF16: return dispatch_zero<ACT, VY_BF16>(zero, nb, gu, dn, sm_count, s, ev, timed);
+        case VY_F16: return dispatch_zero<ACT, VY_F16>(zero, nb, gu, dn, sm_count, s, ev, timed);
+        default: return dispatch_zero<ACT, VY_F32>(zero, nb, gu, dn, sm_count, s, ev, timed);
     }
 }
 
 struct DecodeLayout {
-    int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters, *tile_done;
+    int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters;
     PassEntry* passes;
     uint16_t *x_perm, *h_perm;
-    float* ybuf_g;
+    float* ybuf_g;   // the down projection's contributions (absent when the caller takes them)
     size_t bytes;
-    bool combine_in_cta;
-    int n_chunks;
 };
 
 // Column blocks (8 tokens each) one pass of a unit holds: the largest token count an expert
@@ -649,20 +611,7 @@ struct DecodeLayout {
 int nb_for(int64_t n_tokens) { return n_tokens <= 32 ? 1 : (n_tokens <= 64 ? 2 : 4); }
 int call_nb(const vy_moe_call* c) { return c->col_blocks ? c->col_blocks : nb_for(c->n_tokens); }
 
-// CTAs per down-projection row tile: as many as keep the whole grid resident at once (a grid a
-// fraction of a wave larger runs a second, mostly empty wave), but no more chunks than the call
-// can have live experts per warp.
-int down_chunks(const vy_moe_call* c, int sm_count) {
-    const int64_t n = c->n_tokens * c->top_k;
-    const int n_tiles = c->geom->hidden / kTileRows;
-    const int64_t max_live = n < c->n_experts ? n : c->n_experts;
-    int chunks = (kDnBlocksPerSm[call_nb(c)] * sm_count) / n_tiles;
-    const int cap = static_cast<int>((max_live + kWarps - 1) / kWarps);
-    if (chunks > cap) chunks = cap;
-    return chunks < 1 ? 1 : chunks;
-}
-
-DecodeLayout decode_layout(const vy_moe_call* c, void* base, int sm_count) {
+DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
     const int64_t n = c->n_tokens * c->top_k;
     const int E = c->n_experts;
     const int64_t H = c->geom->hidden, I = c->geom->inter;
@@ -674,19 +623,13 @@ DecodeLayout decode_layout(const vy_moe_call* c, void* base, int sm_count) {
     L.unit_start = cv.take<int32_t>(E + 1);
     L.slot_order = cv.take<int32_t>(n);
     L.counters = cv.take<int32_t>(4);
-    L.tile_done = cv.take<int32_t>(H / kTileRows);
     {
         const int64_t tpu = call_nb(c) * 8, max_live = n < E ? n : E;
         L.passes = cv.take<PassEntry>(n / tpu + max_live + 1);
     }
     L.x_perm = cv.take<uint16_t>(c->n_tokens * H);
     L.h_perm = cv.take<uint16_t>(n * I);
-    L.n_chunks = down_chunks(c, sm_count);
-    const size_t ybuf_bytes = size_t(n) * kTileRows * sizeof(float);
-    L.combine_in_cta = (c->contrib == nullptr) && L.n_chunks == 1 &&
-                       (dn_ring_smem() + ybuf_bytes <= kDnSmemCap);
-    L.ybuf_g = nullptr;
-    if (c->contrib == nullptr && !L.combine_in_cta) L.ybuf_g = cv.take<float>(n * H);
+    L.ybuf_g = c->contrib == nullptr ? cv.take<float>(n * H) : nullptr;
     L.bytes = cv.used;
     return L;
 }
@@ -752,7 +695,7 @@ extern "C" int vy_moe_error_flags(const vy_moe_call* c, int32_t path, int32_t* o
         flags = prefill_flags(c);
     } else {
         char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 255) & ~uintptr_t(255));
-        flags = decode_layout(c, base, 1).counters + 2;
+        flags = decode_layout(c, base).counters + 2;
     }
     const cudaError_t e = cudaMemcpyAsync(out, flags, sizeof(int32_t), cudaMemcpyDefault, as_stream(stream));
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "error-flag copy: %s", cudaGetErrorString(e));
@@ -762,8 +705,7 @@ extern "C" int vy_moe_error_flags(const vy_moe_call* c, int32_t path, int32_t* o
 extern "C" size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path) {
     if (!call || !call->geom) return 0;
     if (path == 1) return prefill_workspace_bytes(call);
-    // the layout depends on the SM count only through the chunk count; size for the largest
-    return decode_layout(call, nullptr, 1 << 20).bytes + 256;
+    return decode_layout(call, nullptr).bytes + 256;
 }
 
 extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
@@ -772,11 +714,11 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     if (!dev) return st;
     if ((st = validate_call(c)) != VY_OK) return st;
     if (c->n_tokens == 0) return ok();
-    DecodeLayout L = decode_layout(c, nullptr, dev->sm_count);
+    DecodeLayout L = decode_layout(c, nullptr);
     if (!c->workspace || c->workspace_bytes < L.bytes + 256)
         return fail(VY_ERR_WORKSPACE, "workspace %zu bytes, %zu needed", c->workspace_bytes, L.bytes + 256);
     char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 255) & ~uintptr_t(255));
-    L = decode_layout(c, base, dev->sm_count);
+    L = decode_layout(c, base);
     const vy_expert_geom& g = *c->geom;
     cudaStream_t s = as_stream(stream);
     const int nb = call_nb(c);
@@ -801,8 +743,6 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     pa.x_vec = aligned16(c->x) && (c->x_row_stride % 8 == 0);
     pa.hidden = g.hidden;
     pa.x_perm = L.x_perm;
-    pa.zero_ints = L.tile_done;
-    pa.zero_count = g.hidden / kTileRows;
     pa.expert_table = c->expert_table;
     pa.passes = L.passes;
     cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
@@ -838,13 +778,11 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     dn.inter = g.inter;
     dn.gs_shift = gs_shift;
     dn.top_k = c->top_k;
-    dn.n_tokens = c->n_tokens;
     dn.w_off = g.word_off[2];
     dn.s_off = g.scale_off[2];
     dn.z_off = g.zero_off[2];
     dn.passes = L.passes;
     dn.unit_start = L.unit_start;
-    dn.slot_order = L.slot_order;
     dn.counters = L.counters;
     dn.h_perm = L.h_perm;
     dn.weights = c->weights;
@@ -853,19 +791,18 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     dn.w_tok_stride = c->w_tok_stride;
     dn.w_slot_stride = c->w_slot_stride;
     dn.w_index = c->w_index;
-    dn.out = c->out;
-    dn.out_stride = c->out_row_stride;
     dn.ybuf_g = c->contrib ? c->contrib : L.ybuf_g;
-    dn.global_combine = c->contrib == nullptr && !L.combine_in_cta;
-    dn.n_chunks = L.n_chunks;
-    dn.tile_done = L.tile_done;
 
     const int sm_count = dev->sm_count;
-    const size_t dn_smem = dn_ring_smem() + (L.combine_in_cta ? size_t(c->n_tokens * c->top_k) * kTileRows * sizeof(float) : 0);
     const bool zero = g.has_zero != 0;
-    st = c->act_dtype == VY_BF16 ? dispatch_sc<VY_BF16>(g.scale_dtype, zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed)
-                                 : dispatch_sc<VY_F16>(g.scale_dtype, zero, nb, gu, dn, sm_count, dn_smem, s, ev, timed);
+    st = c->act_dtype == VY_BF16 ? dispatch_sc<VY_BF16>(g.scale_dtype, zero, nb, gu, dn, sm_count, s, ev, timed)
+                                 : dispatch_sc<VY_F16>(g.scale_dtype, zero, nb, gu, dn, sm_count, s, ev, timed);
     if (st != VY_OK) return st;
+    // each token's row: its slots' contributions in ascending expert id, then slot
+    if (!c->contrib &&
+        (st = launch_slot_combine(L.ybuf_g, L.slot_order, c->n_tokens, c->top_k, g.hidden, c->out,
+                                  c->out_row_stride, s)) != VY_OK)
+        return st;
     if (timed) cudaEventRecord(ev[3], s);
-    return ok();
+    return check_launch("vy_moe_decode");
 }
