@@ -182,9 +182,9 @@ typedef struct vy_expert_geom {
  *
  * Fields appended in ABI version 2 (zero keeps version-1 behaviour):
  *   col_blocks      tokens one decode pass of an expert carries, in blocks of 8: 1, 2 or 4 (0:
- *                   chosen from n_tokens).  An expert with more routed rows takes more passes
- *                   (its weights are read once per pass); a caller that knows the rows per expert
- *                   are few (e.g. a rank's share of an all-gathered batch) picks a small value.
+ *                   chosen by the library: 2 for at most 16 experts with at most 4 routed rows
+ *                   each on average, else 1).  An expert with more routed rows takes more passes
+ *                   (its weights are read once per pass, the later ones mostly from L2).
  *   expert_base     expert_ids[j] - expert_base indexes expert_table; ids outside
  *                   [expert_base, expert_base + n_experts) drop their slot (a rank's own range of a
  *                   global id space).

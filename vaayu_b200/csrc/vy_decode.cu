@@ -33,7 +33,11 @@ namespace {
 #ifndef VY_DN_DEPTH
 #define VY_DN_DEPTH 8
 #endif
-constexpr int kWarps = 8;
+#ifndef VY_GU_WARPS
+#define VY_GU_WARPS 8
+#endif
+constexpr int kWarps = 8;                 // down-projection warps per CTA
+constexpr int kGuWarps = VY_GU_WARPS;     // gate/up warps per CTA (two CTAs per SM)
 constexpr int kStageK = 128;             // K elements of one row per pipeline stage (64 bytes of codes)
 constexpr int kGuDepth = VY_GU_DEPTH;    // gate/up ring: stages in flight per warp (2 KB each)
 constexpr int kDnDepth = VY_DN_DEPTH;    // down ring: stages in flight per warp (1 KB each)
@@ -84,15 +88,15 @@ struct UnitInfo {
 // The per-warp hand-off of unit descriptions from the issue side to the consuming side: the
 // warp-uniform part once, the row ids per column.  Q slots cover the issue side's lookahead
 // (kDepth - 1 stages, so at most kDepth - 1 units when a unit has a single stage).
-template <int NB, int Q>
+template <int NB, int Q, int W = kWarps>
 struct UnitQueue {
     struct Head {
         const int32_t* pk;
         const void* sc;
         const int32_t* zp;
         int ncols, tile, ok;
-    } head[kWarps][Q];
-    int rows[kWarps][Q][NB * 8];
+    } head[W][Q];
+    int rows[W][Q][NB * 8];
 
     __device__ __forceinline__ void put(int warp, int slot, int lane, int g, const UnitInfo<NB>& u) {
         if (lane == 0) head[warp][slot] = Head{u.pk, u.sc, u.zp, u.ncols, u.tile, u.ok};
@@ -168,12 +172,12 @@ __device__ __forceinline__ void dequant_chunk(const uint4& w, uint32_t bias, uin
 }
 
 template <int ACT, int SC, bool ZERO, int NB>
-__global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(GateUpParams p) {
+__global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(GateUpParams p) {
     extern __shared__ uint4 ring[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
     uint4* my_ring = ring + warp * (kGuDepth * 4 * 32);
-    __shared__ UnitQueue<NB, kGuDepth> queue;
+    __shared__ UnitQueue<NB, kGuDepth, kGuWarps> queue;
 
     grid_dependency_wait();
     grid_dependents_launch();
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(kWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(G
     if (n_live <= 0) return;
     const int tiles = p.inter / kTileRows;
     const int total_units = p.unit_start[n_live] * tiles;
-    const int gw = blockIdx.x * kWarps + warp, nw = gridDim.x * kWarps;
+    const int gw = blockIdx.x * kGuWarps + warp, nw = gridDim.x * kGuWarps;
     if (gw >= total_units) return;
     const int my_units = (total_units - gw + nw - 1) / nw;
     const int spu = p.hidden / kStageK;
@@ -525,14 +529,14 @@ __global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(D
 
 // ── host side ─────────────────────────────────────────────────────────────────────────────
 
-size_t gu_smem() { return size_t(kWarps) * kGuDepth * 4 * 32 * sizeof(uint4); }
+size_t gu_smem() { return size_t(kGuWarps) * kGuDepth * 4 * 32 * sizeof(uint4); }
 size_t dn_smem() { return size_t(kWarps) * kDnDepth * 2 * 32 * sizeof(uint4); }
 
 template <typename Kernel, typename Params>
-cudaError_t launch_pdl(Kernel kernel, int grid, size_t smem, cudaStream_t s, const Params& prm) {
+cudaError_t launch_pdl(Kernel kernel, int grid, int warps, size_t smem, cudaStream_t s, const Params& prm) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kWarps * 32);
+    cfg.blockDim = dim3(warps * 32);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -556,7 +560,7 @@ int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaS
                              static_cast<int>(dn_smem()));
         int nblk = 0, ndn = 0;
         cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &nblk, gate_up_kernel<ACT, SC, ZERO, NB>, kWarps * 32, gu_smem());
+            &nblk, gate_up_kernel<ACT, SC, ZERO, NB>, kGuWarps * 32, gu_smem());
         if (oe == cudaSuccess)
             oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ndn, down_kernel<ACT, SC, ZERO, NB>, kWarps * 32,
                                                                dn_smem());
@@ -565,10 +569,10 @@ int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaS
         gu_blocks_per_sm = nblk;
         dn_blocks_per_sm = ndn;
     }
-    cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_blocks_per_sm * sm_count, gu_smem(), s, gu);
+    cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
     if (timed) cudaEventRecord(ev[2], s);
-    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn_blocks_per_sm * sm_count, dn_smem(), s, dn);
+    e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn_blocks_per_sm * sm_count, kWarps, dn_smem(), s, dn);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "down launch: %s", cudaGetErrorString(e));
     return check_launch("vy_moe_decode");
 }
@@ -606,10 +610,15 @@ struct DecodeLayout {
     size_t bytes;
 };
 
-// Column blocks (8 tokens each) one pass of a unit holds: the largest token count an expert
-// can have is n_tokens; empty blocks are skipped at run time, so NB only costs registers.
-int nb_for(int64_t n_tokens) { return n_tokens <= 32 ? 1 : (n_tokens <= 64 ? 2 : 4); }
-int call_nb(const vy_moe_call* c) { return c->col_blocks ? c->col_blocks : nb_for(c->n_tokens); }
+// Column blocks (8 tokens each) one pass of a unit holds.  One block wins nearly everywhere it
+// was measured (B200: cfg1 up to 16 rows per expert, cfg3, Mixtral from 6 rows per expert): the
+// lighter kernels keep more warps resident than a second pass over L2-warm weights costs.  Two
+// blocks win (3-7 %) only for few experts with at most 4 rows each; four never did.
+int nb_for(const vy_moe_call* c) {
+    const int64_t rows = c->n_tokens * c->top_k;
+    return (c->n_experts <= 16 && rows <= 4 * int64_t(c->n_experts)) ? 2 : 1;
+}
+int call_nb(const vy_moe_call* c) { return c->col_blocks ? c->col_blocks : nb_for(c); }
 
 DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
     const int64_t n = c->n_tokens * c->top_k;

@@ -1,11 +1,12 @@
 // vy_gemv_fp.cu -- FP8-e4m3 / FP4-e2m1 block-scaled dequant fused into a decode GEMV
 // (batch <= 16): y[t, n] = bf16(sum_k deq(W)[n, k] * x[t, k]), fp32 accumulation.
 //
-// One CTA = 16 weight rows; its 8 warps split K into 8 contiguous ranges (split-K inside the
-// CTA, so the grid has n/16 CTAs even for a single output tile row), each warp streams its
-// range with 128-bit no-allocate loads, dequantises into bf16 pairs in registers (exactly the
-// values vy_fp8_dequant / vy_fp4_dequant produce) and accumulates m16n8k16 tensor-core
-// fragments whose N dimension is the tokens.  The 8 partial tiles are summed in warp order in
+// One CTA = 16 weight rows; its 16 warps split K into 16 contiguous ranges (split-K inside the
+// CTA, so the grid has n/16 CTAs even for a single output tile row; two CTAs fit an SM at 64
+// registers a thread).  Each warp streams its range through its own cp.async ring in shared
+// memory, dequantises into bf16 pairs in registers (exactly the values vy_fp8_dequant /
+// vy_fp4_dequant produce) and accumulates m16n8k16 tensor-core fragments whose N dimension is
+// the tokens.  The partial tiles are summed in warp order in
 // shared memory: the result does not depend on scheduling.
 #include <cuda_fp8.h>
 
@@ -14,8 +15,14 @@
 namespace vy {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kUnroll = 4;
+#ifndef VY_GEMV_WARPS
+#define VY_GEMV_WARPS 16
+#endif
+#ifndef VY_GEMV_DEPTH
+#define VY_GEMV_DEPTH 4
+#endif
+constexpr int kWarps = VY_GEMV_WARPS;   // warps per CTA: the K split of one 16-row tile
+constexpr int kDepth = VY_GEMV_DEPTH;   // ring steps per warp (1 KB each; kDepth - 1 in flight)
 
 __device__ __forceinline__ float e4m3f(uint32_t b) {
     __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b & 0xFFu), __NV_E4M3);
@@ -89,13 +96,17 @@ struct GemvParams {
 
 // KIND 0: fp8 (16 B = 16 codes of a row per thread per step; a step covers 64 K per row)
 // KIND 1: fp4 (16 B = 32 codes; a step covers 128 K per row)
+// Each warp streams its K range through its own cp.async ring in shared memory (kDepth steps of
+// 1 KB: rows g and g + 8 of the tile, 16 B per lane each), kDepth - 1 steps ahead of the math.
 template <int KIND, int NB>
-__global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
+__global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_kernel(GemvParams p) {
     constexpr int kPerThread = KIND == 0 ? 16 : 32;    // K elements per thread per step
     constexpr int kStepK = 4 * kPerThread;             // K per step per row
+    extern __shared__ uint4 gv_ring[];                 // [kWarps][kDepth][2][32]
     __shared__ float part[kWarps][16][NB * 8];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
+    uint4* my_ring = gv_ring + warp * (kDepth * 64);
     const int64_t row0 = int64_t(blockIdx.x) * 16;
     const int64_t steps = p.k / kStepK;
     const int64_t per_warp = (steps + kWarps - 1) / kWarps;
@@ -114,93 +125,101 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
     const bool halves = KIND == 1 && (p.gs % 16) == 0;   // a thread's 32 fp4 codes: two whole groups
     const uint8_t* sc8 = reinterpret_cast<const uint8_t*>(p.scale);
 
+    // ── issue side: one step (rows A and B, 16 B per lane each) per call ──────────────────
+    int64_t i_s = s_lo;
+    int i_slot = 0;
+    auto issue = [&]() {
+        if (i_s < s_hi) {
+            const int64_t off = (i_s * kStepK + tig * kPerThread) / (KIND == 0 ? 1 : 2);
+            uint4* dst = my_ring + i_slot * 64 + lane;
+            if (okA) cp_async16(dst, wA + off);
+            if (okB) cp_async16(dst + 32, wB + off);
+        }
+        cp_async_commit();
+        ++i_s;
+        if (++i_slot == kDepth) i_slot = 0;
+    };
+#pragma unroll
+    for (int d = 0; d < kDepth - 1; ++d) issue();
+
     float acc[NB][4];
 #pragma unroll
     for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[cb][i] = 0.f;
 
-    for (int64_t s0 = s_lo; s0 < s_hi; s0 += kUnroll) {
-        uint4 va[kUnroll], vb[kUnroll];
+    int c_slot = 0;
+    for (int64_t s = s_lo; s < s_hi; ++s) {
+        issue();
+        cp_async_wait<kDepth - 1>();
+        const uint4* st = my_ring + c_slot * 64 + lane;
+        const uint4 va = okA ? st[0] : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 vb = okB ? st[32] : make_uint4(0u, 0u, 0u, 0u);
+        if (++c_slot == kDepth) c_slot = 0;
+        const uint32_t k0 = static_cast<uint32_t>(s * kStepK + tig * kPerThread);
+        float sa = 0.f, sb = 0.f;
+        uint32_t ha[2] = {0u, 0u}, hb[2] = {0u, 0u};   // fp4 group scales as bf16 pairs (exact)
+        if constexpr (KIND == 0) {
+            const uint32_t kb = kdiv(k0);
+            sa = okA ? block_scale(p.scale, p.scale_dtype, baseA + kb) : 0.f;
+            sb = okB ? block_scale(p.scale, p.scale_dtype, baseB + kb) : 0.f;
+        } else if (halves) {
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const int64_t s = s0 + u;
-            const int64_t off = (s * kStepK + tig * kPerThread) / (KIND == 0 ? 1 : 2);
-            va[u] = make_uint4(0, 0, 0, 0);
-            vb[u] = make_uint4(0, 0, 0, 0);
-            if (s < s_hi) {
-                if (okA) va[u] = ld_nc_v4(wA + off);
-                if (okB) vb[u] = ld_nc_v4(wB + off);
+            for (int hh = 0; hh < 2; ++hh) {
+                const uint32_t gi = kdiv(k0 + 16 * hh);
+                ha[hh] = okA ? bf16_pair(e4m3f(__ldg(sc8 + baseA + gi)), e4m3f(__ldg(sc8 + baseA + gi))) : 0u;
+                hb[hh] = okB ? bf16_pair(e4m3f(__ldg(sc8 + baseB + gi)), e4m3f(__ldg(sc8 + baseB + gi))) : 0u;
             }
         }
+        const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+        const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+        // mma step q covers this thread's elements 4q..4q+3 (fp8) / 4q..4q+3 (fp4)
+        constexpr int kSteps = kPerThread / 4;
 #pragma unroll
-        for (int u = 0; u < kUnroll; ++u) {
-            const int64_t s = s0 + u;
-            if (s >= s_hi) break;
-            const uint32_t k0 = static_cast<uint32_t>(s * kStepK + tig * kPerThread);
-            float sa = 0.f, sb = 0.f;
-            uint32_t ha[2] = {0u, 0u}, hb[2] = {0u, 0u};   // fp4 group scales as bf16 pairs (exact)
+        for (int q = 0; q < kSteps; ++q) {
+            uint32_t a0, a1, a2, a3;
             if constexpr (KIND == 0) {
-                const uint32_t kb = kdiv(k0);
-                sa = okA ? block_scale(p.scale, p.scale_dtype, baseA + kb) : 0.f;
-                sb = okB ? block_scale(p.scale, p.scale_dtype, baseB + kb) : 0.f;
-            } else if (halves) {
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const uint32_t gi = kdiv(k0 + 16 * hh);
-                    ha[hh] = okA ? bf16_pair(e4m3f(__ldg(sc8 + baseA + gi)), e4m3f(__ldg(sc8 + baseA + gi))) : 0u;
-                    hb[hh] = okB ? bf16_pair(e4m3f(__ldg(sc8 + baseB + gi)), e4m3f(__ldg(sc8 + baseB + gi))) : 0u;
+                const uint32_t xa = wa[q], xb = wb[q];   // 4 codes: elements 4q..4q+3
+                const float2 fa0 = e4m3x2f(xa), fa1 = e4m3x2f(xa >> 16);
+                const float2 fb0 = e4m3x2f(xb), fb1 = e4m3x2f(xb >> 16);
+                a0 = bf16_pair(__fmul_rn(fa0.x, sa), __fmul_rn(fa0.y, sa));
+                a2 = bf16_pair(__fmul_rn(fa1.x, sa), __fmul_rn(fa1.y, sa));
+                a1 = bf16_pair(__fmul_rn(fb0.x, sb), __fmul_rn(fb0.y, sb));
+                a3 = bf16_pair(__fmul_rn(fb1.x, sb), __fmul_rn(fb1.y, sb));
+            } else {
+                const uint32_t xa = (wa[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;   // 4 nibbles
+                const uint32_t xb = (wb[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
+                if (halves) {
+                    // e2m1 x e4m3 has at most 6 significant bits: the bf16 product is exact,
+                    // i.e. the same value the fp32 product rounded to bf16 gives
+                    uint32_t ea01, ea23, eb01, eb23;
+                    e2m1x4_bf16(xa, ea01, ea23);
+                    e2m1x4_bf16(xb, eb01, eb23);
+                    a0 = bf16x2_mul(ea01, ha[q >> 2]);
+                    a2 = bf16x2_mul(ea23, ha[q >> 2]);
+                    a1 = bf16x2_mul(eb01, hb[q >> 2]);
+                    a3 = bf16x2_mul(eb23, hb[q >> 2]);
+                } else {
+                    const uint32_t gi = kdiv(k0 + 4 * q);
+                    const float fa = okA ? e4m3f(__ldg(sc8 + baseA + gi)) : 0.f;
+                    const float fb = okB ? e4m3f(__ldg(sc8 + baseB + gi)) : 0.f;
+                    a0 = bf16_pair(__fmul_rn(e2m1f(xa), fa), __fmul_rn(e2m1f(xa >> 4), fa));
+                    a2 = bf16_pair(__fmul_rn(e2m1f(xa >> 8), fa), __fmul_rn(e2m1f(xa >> 12), fa));
+                    a1 = bf16_pair(__fmul_rn(e2m1f(xb), fb), __fmul_rn(e2m1f(xb >> 4), fb));
+                    a3 = bf16_pair(__fmul_rn(e2m1f(xb >> 8), fb), __fmul_rn(e2m1f(xb >> 12), fb));
                 }
             }
-            const uint32_t wa[4] = {va[u].x, va[u].y, va[u].z, va[u].w};
-            const uint32_t wb[4] = {vb[u].x, vb[u].y, vb[u].z, vb[u].w};
-            // mma step q covers this thread's elements 4q..4q+3 (fp8) / 4q..4q+3 (fp4)
-            constexpr int kSteps = kPerThread / 4;
 #pragma unroll
-            for (int q = 0; q < kSteps; ++q) {
-                uint32_t a0, a1, a2, a3;
-                if constexpr (KIND == 0) {
-                    const uint32_t xa = wa[q], xb = wb[q];   // 4 codes: elements 4q..4q+3
-                    const float2 fa0 = e4m3x2f(xa), fa1 = e4m3x2f(xa >> 16);
-                    const float2 fb0 = e4m3x2f(xb), fb1 = e4m3x2f(xb >> 16);
-                    a0 = bf16_pair(__fmul_rn(fa0.x, sa), __fmul_rn(fa0.y, sa));
-                    a2 = bf16_pair(__fmul_rn(fa1.x, sa), __fmul_rn(fa1.y, sa));
-                    a1 = bf16_pair(__fmul_rn(fb0.x, sb), __fmul_rn(fb0.y, sb));
-                    a3 = bf16_pair(__fmul_rn(fb1.x, sb), __fmul_rn(fb1.y, sb));
-                } else {
-                    const uint32_t xa = (wa[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;   // 4 nibbles
-                    const uint32_t xb = (wb[q >> 1] >> (16 * (q & 1))) & 0xFFFFu;
-                    if (halves) {
-                        // e2m1 x e4m3 has at most 6 significant bits: the bf16 product is exact,
-                        // i.e. the same value the fp32 product rounded to bf16 gives
-                        uint32_t ea01, ea23, eb01, eb23;
-                        e2m1x4_bf16(xa, ea01, ea23);
-                        e2m1x4_bf16(xb, eb01, eb23);
-                        a0 = bf16x2_mul(ea01, ha[q >> 2]);
-                        a2 = bf16x2_mul(ea23, ha[q >> 2]);
-                        a1 = bf16x2_mul(eb01, hb[q >> 2]);
-                        a3 = bf16x2_mul(eb23, hb[q >> 2]);
-                    } else {
-                        const uint32_t gi = kdiv(k0 + 4 * q);
-                        const float fa = okA ? e4m3f(__ldg(sc8 + baseA + gi)) : 0.f;
-                        const float fb = okB ? e4m3f(__ldg(sc8 + baseB + gi)) : 0.f;
-                        a0 = bf16_pair(__fmul_rn(e2m1f(xa), fa), __fmul_rn(e2m1f(xa >> 4), fa));
-                        a2 = bf16_pair(__fmul_rn(e2m1f(xa >> 8), fa), __fmul_rn(e2m1f(xa >> 12), fa));
-                        a1 = bf16_pair(__fmul_rn(e2m1f(xb), fb), __fmul_rn(e2m1f(xb >> 4), fb));
-                        a3 = bf16_pair(__fmul_rn(e2m1f(xb >> 8), fb), __fmul_rn(e2m1f(xb >> 12), fb));
-                    }
-                }
-#pragma unroll
-                for (int cb = 0; cb < NB; ++cb) {
-                    const int t = cb * 8 + g;
-                    uint2 xv = make_uint2(0u, 0u);
-                    if (t < p.n_tokens)
-                        xv = *reinterpret_cast<const uint2*>(p.x + int64_t(t) * p.x_stride + k0 + 4 * q);
-                    mma_16816<VY_BF16>(acc[cb], a0, a1, a2, a3, xv.x, xv.y);
-                }
+            for (int cb = 0; cb < NB; ++cb) {
+                const int t = cb * 8 + g;
+                uint2 xv = make_uint2(0u, 0u);
+                if (t < p.n_tokens)
+                    xv = *reinterpret_cast<const uint2*>(p.x + int64_t(t) * p.x_stride + k0 + 4 * q);
+                mma_16816<VY_BF16>(acc[cb], a0, a1, a2, a3, xv.x, xv.y);
             }
         }
     }
+    cp_async_wait<0>();
 #pragma unroll
     for (int cb = 0; cb < NB; ++cb)
 #pragma unroll
@@ -216,15 +235,28 @@ __global__ void __launch_bounds__(kWarps * 32) fp_gemv_kernel(GemvParams p) {
     }
 }
 
+constexpr size_t kRingBytes = size_t(kWarps) * kDepth * 64 * sizeof(uint4);
+
+template <int KIND, int NB>
+void launch_one(unsigned grid, const GemvParams& p, cudaStream_t s) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(fp_gemv_kernel<KIND, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kRingBytes));
+        configured = true;
+    }
+    fp_gemv_kernel<KIND, NB><<<grid, kWarps * 32, kRingBytes, s>>>(p);
+}
+
 int launch_gemv(int kind, const GemvParams& p, cudaStream_t s) {
     const unsigned grid = static_cast<unsigned>((p.n + 15) / 16);
     const bool two = p.n_tokens > 8;
     if (kind == 0) {
-        if (two) fp_gemv_kernel<0, 2><<<grid, kWarps * 32, 0, s>>>(p);
-        else fp_gemv_kernel<0, 1><<<grid, kWarps * 32, 0, s>>>(p);
+        if (two) launch_one<0, 2>(grid, p, s);
+        else launch_one<0, 1>(grid, p, s);
     } else {
-        if (two) fp_gemv_kernel<1, 2><<<grid, kWarps * 32, 0, s>>>(p);
-        else fp_gemv_kernel<1, 1><<<grid, kWarps * 32, 0, s>>>(p);
+        if (two) launch_one<1, 2>(grid, p, s);
+        else launch_one<1, 1>(grid, p, s);
     }
     return check_launch(kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv");
 }

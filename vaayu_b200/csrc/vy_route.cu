@@ -511,18 +511,28 @@ __global__ void __launch_bounds__(256) slot_combine_kernel(const float* __restri
                                                            const int32_t* __restrict__ slot_order,
                                                            int64_t n_tokens, int top_k, int hidden,
                                                            float* out, int64_t out_stride) {
+    constexpr int kBatch = 8;   // slots whose row ids, then contributions, are loaded together
     grid_dependency_wait();
     for (int64_t t = blockIdx.y; t < n_tokens; t += gridDim.y)
     for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < hidden; c += gridDim.x * blockDim.x * 4) {
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = 0; k < top_k; ++k) {
-            const int row = slot_order[t * top_k + k];
-            if (row < 0) continue;
-            const float4 v = *reinterpret_cast<const float4*>(contrib + int64_t(row) * hidden + c);
-            a.x += v.x;
-            a.y += v.y;
-            a.z += v.z;
-            a.w += v.w;
+        for (int k0 = 0; k0 < top_k; k0 += kBatch) {
+            int row[kBatch];
+            float4 v[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) row[j] = k0 + j < top_k ? __ldg(slot_order + t * top_k + k0 + j) : -1;
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j)
+                if (row[j] >= 0) v[j] = __ldcg(reinterpret_cast<const float4*>(contrib + int64_t(row[j]) * hidden + c));
+            // ascending expert id, then slot: the order the rows were filed in
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                if (row[j] < 0) continue;
+                a.x += v[j].x;
+                a.y += v[j].y;
+                a.z += v[j].z;
+                a.w += v[j].w;
+            }
         }
         float* o = out + t * out_stride + c;
         o[0] = a.x;

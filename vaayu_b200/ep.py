@@ -151,11 +151,13 @@ class ExpertParallelLayer:
             row += (-row) % 16                       # 16-byte rows: the activation views stay aligned
             P = self.world
             ws = None
-            # rows per local expert: the rank's share of the gathered slots over its experts
+            # column blocks per decode pass: one unless few experts each get at most 4 rows (the
+            # rank's share of the gathered slots over its experts; measured on B200, as in the
+            # library's own default, which cannot see the global expert count)
             nb = self.col_blocks
             if nb is None:
                 expect = T * K * P / max(1, self.n_experts)
-                nb = 1 if 1.5 * expect <= 8 else (2 if 1.5 * expect <= 16 else 4)
+                nb = 2 if (self.per_rank <= 16 and expect <= 4) else 1
             if self.table is not None:
                 from .packed_expert_kernels import PATH_DECODE, moe_workspace_bytes
                 ws = torch.empty(moe_workspace_bytes(self.table, P * T, K, path=PATH_DECODE, col_blocks=nb),

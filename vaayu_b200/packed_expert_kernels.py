@@ -42,6 +42,8 @@ from .moe_patch import blob_layout, zero_layout
 _ROLES = ("gate", "down", "up")
 _DTYPE_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 PATH_DECODE, PATH_PREFILL = 0, 1
+# average routed rows per expert above which moe_forward's default path is the tcgen05 prefill
+PREFILL_ROWS_PER_EXPERT = 12
 
 
 def _layout(geom) -> dict:
@@ -598,7 +600,8 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     it is dropped); routing_weights [T, K] (strided views fine); out [T, hidden] fp32, or
     `contrib` [T*K, hidden] fp32 for the per-row weighted contributions (expert-parallel combine
     on the home rank).  path: PATH_DECODE (token-batched GEMV) or PATH_PREFILL (tcgen05); default
-    by call size.  expert_base: expert_ids are global ids and the table holds [expert_base,
+    by call size (prefill above 12 routed rows per expert on average: the B200 crossover measured
+    on the cfg1, cfg3 and Mixtral shapes lies between 8 and 16).  expert_base: expert_ids are global ids and the table holds [expert_base,
     expert_base + n) (others drop their slot); expert_ids may be a row-strided view.  col_blocks:
     tokens per decode pass of an expert in blocks of 8 (1, 2, 4; 0 = from the call size).
     Nothing here synchronises with the host -- except `check=True`, which reads the call's device
@@ -614,7 +617,8 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     if out is None and contrib is None:
         out = torch.empty(n_tok, table.hidden, dtype=torch.float32, device=dev)
     if path is None:
-        path = PATH_PREFILL if (n_tok * top_k >= 4 * table.n_experts and prefill_available()) else PATH_DECODE
+        path = PATH_PREFILL if (n_tok * top_k > PREFILL_ROWS_PER_EXPERT * table.n_experts
+                                and prefill_available()) else PATH_DECODE
     with torch.cuda.device(dev):
         c = _make_call(table.geom_s, x, n_tok, top_k, table.n_experts, table.table.data_ptr(),
                        ids.data_ptr(), ids_code, routing_weights, routing_weights.stride(0),
