@@ -283,19 +283,7 @@ def block_scaled_bench(args, device):
     (e2m1, an e4m3 scale per 16) of the same shape, each dequantised to bf16 and fused into a
     decode GEMV at batch 1 and 16.  Two weight copies rotate so every call reads from HBM."""
     from vaayu_b200 import block_scaled as bs
-    N, K = 4096, 14336
-    g = torch.Generator(device=device).manual_seed(4)
-    fp8, fp4 = [], []
-    for _ in range(2):
-        w = torch.randn(N, K, generator=g, device=device)
-        amax = w.abs().reshape(N // 128, 128, K // 128, 128).amax(dim=(1, 3)).clamp_min(1e-6)
-        scale = (amax / 448.0).float()
-        q = (w / scale.repeat_interleave(128, 0).repeat_interleave(128, 1)).to(torch.float8_e4m3fn)
-        fp8.append((q, scale))
-        codes = torch.randint(0, 256, (N, K // 2), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
-        sc = (torch.rand(N, K // 16, generator=g, device=device) * 2 + 0.25).to(torch.float8_e4m3fn)
-        fp4.append((codes, sc))
-        del w, q
+    N, K, g, fp8, fp4 = cfg4_weights(device)
     peak, src = hbm_peak()
     steps = max(5, min(args.steps, 20))
     res = {}
@@ -325,6 +313,39 @@ def block_scaled_bench(args, device):
             "steps": steps, "results": res, "gpu_launches": 6 * steps}
 
 
+def cfg4_weights(device, copies=2):
+    """Configuration 4's weights: [4096, 14336] FP8-e4m3 with an fp32 scale per 128 x 128 block and
+    NVFP4 (random e2m1 codes, an e4m3 scale per 16), `copies` of each, seeded."""
+    N, K = 4096, 14336
+    g = torch.Generator(device=device).manual_seed(4)
+    fp8, fp4 = [], []
+    for _ in range(copies):
+        w = torch.randn(N, K, generator=g, device=device)
+        amax = w.abs().reshape(N // 128, 128, K // 128, 128).amax(dim=(1, 3)).clamp_min(1e-6)
+        scale = (amax / 448.0).float()
+        q = (w / scale.repeat_interleave(128, 0).repeat_interleave(128, 1)).to(torch.float8_e4m3fn)
+        fp8.append((q, scale))
+        codes = torch.randint(0, 256, (N, K // 2), generator=g, device=device, dtype=torch.int32).to(torch.uint8)
+        sc = (torch.rand(N, K // 16, generator=g, device=device) * 2 + 0.25).to(torch.float8_e4m3fn)
+        fp4.append((codes, sc))
+        del w, q
+    return N, K, g, fp8, fp4
+
+
+def gemv_profile(device):
+    """Three FP8 then three FP4 configuration-4 GEMVs at batch 1 (the launches an ncu capture reads)."""
+    from vaayu_b200 import block_scaled as bs
+    N, K, g, fp8, fp4 = cfg4_weights(device, copies=1)
+    x = torch.randn(1, K, generator=g, device=device).to(torch.bfloat16)
+    o = torch.empty(1, N, dtype=torch.bfloat16, device=device)
+    for _ in range(3):
+        bs.fp8_gemv(x, *fp8[0], out=o)
+    for _ in range(3):
+        bs.fp4_gemv(x, *fp4[0], out=o)
+    torch.cuda.synchronize(device)
+    print(json.dumps({"profile": "gemv", "n": N, "k": K, "tokens": 1}))
+
+
 def time_steps(fn, steps, device):
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -347,6 +368,8 @@ def run_ours(args, rank, world, local):
         return ep.run_bench(args, rank, world, local, CFG3 if args.workload == "cfg3" else wl)
     if args.profile == "prefill":
         return prefill_bench(args, device)
+    if args.profile == "gemv":
+        return gemv_profile(device)
 
     layers = [pk.ExpertTable(make_layer(1000 * l, wl, device)) for l in range(args.layers)]
     batches = {}
@@ -577,8 +600,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--layers", type=int, default=8)
-    ap.add_argument("--profile", nargs="?", const="decode", choices=("decode", "prefill"), default=None,
-                    help="only the timed loop of the decode (default) or prefill step, for ncu")
+    ap.add_argument("--profile", nargs="?", const="decode", choices=("decode", "prefill", "gemv"), default=None,
+                    help="only the timed loop of the decode (default) or prefill step, or three FP8 then "
+                         "three FP4 configuration-4 GEMVs at batch 1, for ncu")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the configuration-2 prefill measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
