@@ -271,9 +271,18 @@ def run_bench(args, rank, world, local, wl):
 
     # each layer's step (pack, all-gather, kernels, all-to-all, combine) as one CUDA graph over
     # static input buffers; eager calls when capture is not possible here
-    xs = [b[0].clone() for b in batches]
-    ws_ = [b[1].clone() for b in batches]
-    ids_ = [b[2].clone() for b in batches]
+    # (each layer's inputs are views of one device record, so the end-to-end step moves them with
+    # a single host-to-device copy)
+    nbytes, views = bench.record_layout(batches[0])
+    drecs = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(L)]
+    xs, ws_, ids_ = [], [], []
+    for l in range(L):
+        xv, wv, iv = views(drecs[l])
+        for v, src in zip((xv, wv, iv), batches[l]):
+            v.copy_(src)
+        xs.append(xv)
+        ws_.append(wv)
+        ids_.append(iv)
     graphs = []
     for l in range(L):
         for _ in range(2):
@@ -308,15 +317,12 @@ def run_bench(args, rank, world, local, wl):
     bench.barrier(world)
     ms = bench.max_over_ranks(ms, world)
 
-    pin = [(x.cpu().pin_memory(), w.cpu().pin_memory(), i.cpu().pin_memory()) for x, w, i in batches]
+    pin = [bench.pinned_record(b, nbytes, views) for b in batches]
     out_h = torch.empty(T, wl["hidden"], dtype=torch.float32 if shared is None else torch.bfloat16).pin_memory()
 
     def e2e_step(i):
         l = i % L
-        xh, wh, ih = pin[l]
-        xs[l].copy_(xh, non_blocking=True)
-        ws_[l].copy_(wh, non_blocking=True)
-        ids_[l].copy_(ih, non_blocking=True)
+        drecs[l].copy_(pin[l], non_blocking=True)
         if graphs:
             graphs[l].replay()
         else:
@@ -328,7 +334,7 @@ def run_bench(args, rank, world, local, wl):
     bench.barrier(world)
     e2e_ms = bench.max_over_ranks(bench.time_steps(e2e_step, args.steps, device), world)
     bench.barrier(world)
-    h2d = sum(t.numel() * t.element_size() for t in (xs[0], ws_[0], ids_[0]))
+    h2d = nbytes                      # the record copied each step (its fields padded to 16 bytes)
     used_graphs = bool(graphs)
     del graphs               # graphs holding NCCL calls go before the process group does
     torch.cuda.synchronize(device)
