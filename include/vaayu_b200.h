@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define VY_ABI_VERSION 2
+#define VY_ABI_VERSION 3
 
 enum vy_status {
     VY_OK = 0,
@@ -189,6 +189,17 @@ typedef struct vy_expert_geom {
  *                   [expert_base, expert_base + n_experts) drop their slot (a rank's own range of a
  *                   global id space).
  *   ids_row_stride  elements between consecutive tokens' rows of expert_ids (0: top_k).
+ *
+ * Fields appended in ABI version 3 (zero keeps version-2 behaviour):
+ *   shared_last     1: slot top_k - 1 of every token is the block's always-on shared expert (an
+ *                   entry of expert_table like any other, routed with weight 1 or its sigmoid
+ *                   gate), and the layer ends with the model's epilogue
+ *                     result[t] = act(act(sum of the routed slots' c) + act(c of the shared slot))
+ *                   (vaayu/packed_expert_kernels.py:502-508: out.to(act) + shared.to(act)), the
+ *                   routed sum in ascending expert index as above.  `out` (optional here)
+ *                   receives that routed fp32 sum; `contrib` must be NULL.
+ *   result          [n_tokens, hidden] act dtype, written when shared_last is 1.
+ *   result_row_stride  elements between result rows (>= hidden).
  */
 typedef struct vy_moe_call {
     const vy_expert_geom* geom;
@@ -226,6 +237,11 @@ typedef struct vy_moe_call {
     int32_t col_blocks;
     int32_t expert_base;
     int64_t ids_row_stride;
+    /* ABI version 3 */
+    int32_t shared_last;
+    int32_t reserved2;
+    void* result;
+    int64_t result_row_stride;
 } vy_moe_call;
 
 /*

@@ -345,3 +345,32 @@ def test_the_shared_expert_joins_like_the_model_epilogue(gated):
     rms = float(np.sqrt(np.mean(ref ** 2)))
     bound = 2.0 ** -7 * (np.abs(rb) + np.abs(sb) + np.abs(ref)) + 1e-3 * rms
     assert np.all(np.abs(g - ref) <= bound)
+
+
+@pytest.mark.parametrize("path", [vb.PATH_DECODE, vb.PATH_PREFILL], ids=["decode", "prefill"])
+@pytest.mark.parametrize("gated", [False, True], ids=["ungated", "gated"])
+@pytest.mark.parametrize("wdt", [torch.float32, torch.bfloat16], ids=["w-fp32", "w-bf16"])
+def test_the_fused_shared_expert_equals_two_calls_bit_for_bit(path, gated, wdt):
+    """One layer call with the shared expert as every token's extra slot (shared_last) equals the
+    routed layer and the shared expert as separate calls on the same path, joined by the model's
+    epilogue out.to(bf16) + shared.to(bf16) -- bit for bit, the routed fp32 sum included."""
+    if path == vb.PATH_PREFILL and not pk.prefill_available():
+        pytest.skip("prefill kernels not built")
+    routed, x, idx, w = _batched(1024, 512, 128, 8, 2, 37, seed=23)
+    w = w.to(wdt)
+    shared = pk.ExpertTable(T.make_blobs(1024, 512, 1, gs=128, seed=77))
+    table = pk.ExpertTable(routed)
+    gate = torch.sigmoid(torch.randn(37, 1, generator=torch.Generator().manual_seed(9))).to(torch.bfloat16).cuda() \
+        if gated else None
+    out = torch.empty(37, 1024, device="cuda")
+    got = vb.moe_forward_with_shared(x, idx, w, table, shared, gate=gate, out=out, path=path)
+    r = vb.moe_forward(x, idx, w, table, path=path)
+    sw = gate.reshape(37, 1) if gated else torch.ones(37, 1, device="cuda")
+    s = vb.moe_forward(x, torch.zeros(37, 1, dtype=torch.int32, device="cuda"), sw, shared, path=path)
+    assert got.dtype == torch.bfloat16
+    assert torch.equal(out, r)
+    assert torch.equal(got, r.to(torch.bfloat16) + s.to(torch.bfloat16))
+    # the two-call form of the same API agrees too
+    two = vb.moe_forward_with_shared(x, idx, w, table, shared, gate=gate, path=path, fused=False)
+    if path == vb.PATH_DECODE:
+        assert torch.equal(got, two)

@@ -39,7 +39,8 @@ class MoeCall(ctypes.Structure):
                 ("w_slot_stride", I64T), ("w_index", P), ("out", P), ("out_row_stride", I64T),
                 ("contrib", P), ("h_out", P), ("workspace", P), ("workspace_bytes", SZ),
                 ("stage_events", P), ("n_stage_events", I32T), ("reserved1", I32T),
-                ("col_blocks", I32T), ("expert_base", I32T), ("ids_row_stride", I64T)]
+                ("col_blocks", I32T), ("expert_base", I32T), ("ids_row_stride", I64T),
+                ("shared_last", I32T), ("reserved2", I32T), ("result", P), ("result_row_stride", I64T)]
 
 
 # name -> (restype, argtypes); every symbol include/vaayu_b200.h declares

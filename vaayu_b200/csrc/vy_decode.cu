@@ -680,13 +680,20 @@ int validate_call(const vy_moe_call* c) {
     if (c->n_tokens * int64_t(g.hidden) >= (int64_t(1) << 31) || n * int64_t(g.inter) >= (int64_t(1) << 31) ||
         n * int64_t(g.hidden) >= (int64_t(1) << 31))
         return fail(VY_ERR_UNSUPPORTED, "call too large for 32-bit element offsets");
+    if (c->shared_last != 0 && c->shared_last != 1)
+        return fail(VY_ERR_INVALID, "shared_last %d (0 or 1)", c->shared_last);
+    if (c->shared_last && (c->contrib || c->top_k < 2))
+        return fail(VY_ERR_INVALID, "shared_last needs the layer's own combine (contrib NULL) and top_k >= 2");
     if (c->n_tokens > 0) {
         if (!c->x || !c->expert_table || !c->expert_ids || !c->weights)
             return fail(VY_ERR_INVALID, "null input pointer");
-        if (!c->out && !c->contrib) return fail(VY_ERR_INVALID, "neither out nor contrib given");
+        if (!c->out && !c->contrib && !c->shared_last) return fail(VY_ERR_INVALID, "neither out nor contrib given");
         if (c->x_row_stride < g.hidden) return fail(VY_ERR_INVALID, "x row stride %lld", (long long)c->x_row_stride);
         if (c->out && !c->contrib && c->out_row_stride < g.hidden)
             return fail(VY_ERR_INVALID, "out row stride %lld", (long long)c->out_row_stride);
+        if (c->shared_last && (!c->result || c->result_row_stride < g.hidden))
+            return fail(VY_ERR_INVALID, "shared_last: result %p, row stride %lld", c->result,
+                        (long long)c->result_row_stride);
     }
     return VY_OK;
 }
@@ -808,10 +815,7 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
                                  : dispatch_sc<VY_F16>(g.scale_dtype, zero, nb, gu, dn, sm_count, s, ev, timed);
     if (st != VY_OK) return st;
     // each token's row: its slots' contributions in ascending expert id, then slot
-    if (!c->contrib &&
-        (st = launch_slot_combine(L.ybuf_g, L.slot_order, c->n_tokens, c->top_k, g.hidden, c->out,
-                                  c->out_row_stride, s)) != VY_OK)
-        return st;
+    if (!c->contrib && (st = launch_layer_combine(c, L.ybuf_g, L.slot_order, s)) != VY_OK) return st;
     if (timed) cudaEventRecord(ev[3], s);
     return check_launch("vy_moe_decode");
 }

@@ -55,6 +55,9 @@ int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream);
 // that order; launched with programmatic stream serialisation.
 int launch_slot_combine(const float* contrib, const int32_t* slot_order, int64_t n_tokens, int top_k, int hidden,
                         float* out, int64_t out_stride, cudaStream_t s);
+// A layer call's final combine: launch_slot_combine, or with c->shared_last the shared-expert
+// epilogue into c->result (and the routed sum into c->out when given).
+int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32_t* slot_order, cudaStream_t s);
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
                    cudaStream_t stream);

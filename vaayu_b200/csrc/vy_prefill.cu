@@ -788,9 +788,7 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
         if (timed) cudaEventRecord(ev[3], s);
         return check_launch("vy_moe_prefill");
     }
-    if ((st = launch_slot_combine(L.contrib, L.slot_order, c->n_tokens, c->top_k, g.hidden, c->out,
-                                  c->out_row_stride, s)) != VY_OK)
-        return st;
+    if ((st = launch_layer_combine(c, L.contrib, L.slot_order, s)) != VY_OK) return st;
     if (timed) cudaEventRecord(ev[3], s);
     return check_launch("vy_moe_prefill");
 }

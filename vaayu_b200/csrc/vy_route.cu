@@ -560,6 +560,89 @@ int launch_slot_combine(const float* contrib, const int32_t* slot_order, int64_t
     return VY_OK;
 }
 
+// The same sum over a token's routed slots, then the model's epilogue with its shared expert in
+// slot top_k - 1: result[t] = act(act(routed sum) + act(shared c))
+// (vaayu/packed_expert_kernels.py:502-508).  `out`, when given, receives the routed fp32 sum.
+template <int ACT>
+__global__ void __launch_bounds__(256) shared_combine_kernel(const float* __restrict__ contrib,
+                                                             const int32_t* __restrict__ slot_order,
+                                                             int64_t n_tokens, int top_k, int hidden,
+                                                             float* out, int64_t out_stride,
+                                                             uint16_t* result, int64_t result_stride) {
+    constexpr int kBatch = 8;
+    grid_dependency_wait();
+    for (int64_t t = blockIdx.y; t < n_tokens; t += gridDim.y)
+    for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < hidden; c += gridDim.x * blockDim.x * 4) {
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), sh = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k0 = 0; k0 < top_k; k0 += kBatch) {
+            int row[kBatch];
+            float4 v[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) row[j] = k0 + j < top_k ? __ldg(slot_order + t * top_k + k0 + j) : -1;
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j)
+                if (row[j] >= 0) v[j] = __ldcg(reinterpret_cast<const float4*>(contrib + int64_t(row[j]) * hidden + c));
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                if (row[j] < 0) continue;
+                if (row[j] % top_k == top_k - 1) {   // the shared expert's slot
+                    sh = v[j];
+                    continue;
+                }
+                a.x += v[j].x;
+                a.y += v[j].y;
+                a.z += v[j].z;
+                a.w += v[j].w;
+            }
+        }
+        if (out) {
+            float* o = out + t * out_stride + c;
+            o[0] = a.x;
+            o[1] = a.y;
+            o[2] = a.z;
+            o[3] = a.w;
+        }
+        const float ra[4] = {a.x, a.y, a.z, a.w}, rs[4] = {sh.x, sh.y, sh.z, sh.w};
+        uint16_t* r = result + t * result_stride + c;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            r[i] = static_cast<uint16_t>(act_bits<ACT>(round_act<ACT>(ra[i]) + round_act<ACT>(rs[i])));
+    }
+}
+
+int launch_shared_combine(const float* contrib, const int32_t* slot_order, int64_t n_tokens, int top_k, int hidden,
+                          float* out, int64_t out_stride, void* result, int64_t result_stride, int act,
+                          cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((hidden / 4 + 255) / 256),
+                       static_cast<unsigned>(n_tokens < 65535 ? n_tokens : 65535));
+    cfg.blockDim = dim3(256);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    uint16_t* res = static_cast<uint16_t*>(result);
+    cudaError_t e = act == VY_BF16
+        ? cudaLaunchKernelEx(&cfg, shared_combine_kernel<VY_BF16>, contrib, slot_order, n_tokens, top_k, hidden,
+                             out, out_stride, res, result_stride)
+        : cudaLaunchKernelEx(&cfg, shared_combine_kernel<VY_F16>, contrib, slot_order, n_tokens, top_k, hidden,
+                             out, out_stride, res, result_stride);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "shared-expert combine launch: %s", cudaGetErrorString(e));
+    return VY_OK;
+}
+
+// The layer's final combine: the routed fp32 sum into `out`, or with shared_last the epilogue
+// with the shared expert into `result` as well.
+int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32_t* slot_order, cudaStream_t s) {
+    const int hidden = c->geom->hidden;
+    if (c->shared_last)
+        return launch_shared_combine(contrib, slot_order, c->n_tokens, c->top_k, hidden, c->out, c->out_row_stride,
+                                     c->result, c->result_row_stride, c->act_dtype, s);
+    return launch_slot_combine(contrib, slot_order, c->n_tokens, c->top_k, hidden, c->out, c->out_row_stride, s);
+}
+
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
                    cudaStream_t stream) {

@@ -262,8 +262,18 @@ def run_bench(args, rank, world, local, wl):
         sh_out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
         sh_ws = torch.empty(moe_workspace_bytes(shared[0], T, 1, path=PATH_DECODE), dtype=torch.uint8, device=device)
         result = torch.empty(T, wl["hidden"], dtype=torch.bfloat16, device=device)
+        if world == 1:
+            # one GPU holds every expert: the shared expert rides in the same layer call as every
+            # token's extra slot, the epilogue applied by the layer's combine
+            from .packed_expert_kernels import _with_shared, moe_forward_with_shared
+            fused_ws = torch.empty(moe_workspace_bytes(_with_shared(layers[0].table, shared[0]), T, K + 1,
+                                                       path=PATH_DECODE), dtype=torch.uint8, device=device)
 
     def layer_step(l, x, idx, w):
+        if shared is not None and world == 1:
+            moe_forward_with_shared(x, idx, w, layers[l].table, shared[l], out=out, result=result,
+                                    path=PATH_DECODE, workspace=fused_ws)
+            return
         layers[l].forward(x, idx, w, out)
         if shared is not None:
             shared_expert_forward(x, shared[l], out=sh_out, workspace=sh_ws)

@@ -593,7 +593,7 @@ def _check_flags(c, path, dev) -> None:
 
 def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *, path=None,
                 contrib=None, h_out=None, w_index=None, workspace=None, expert_base=0, col_blocks=0,
-                check=False):
+                check=False, shared_last=False, result=None):
     """The layer over a resident `ExpertTable` with the routing already on the device.
 
     x [T, hidden] act dtype; expert_ids [T, K] int32/int64 (indices into `table`; an id outside
@@ -604,6 +604,10 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     on the cfg1, cfg3 and Mixtral shapes lies between 8 and 16).  expert_base: expert_ids are global ids and the table holds [expert_base,
     expert_base + n) (others drop their slot); expert_ids may be a row-strided view.  col_blocks:
     tokens per decode pass of an expert in blocks of 8 (1, 2, 4; 0 = from the call size).
+    shared_last: slot K - 1 of every token is the block's shared expert (a table entry routed with
+    weight 1 or its sigmoid gate); the call then ends with the model's epilogue
+    result = act(act(routed fp32 sum) + act(shared contribution)) into `result` [T, hidden] act
+    dtype (allocated when None) and returns it, `out` (optional) receiving the routed sum.
     Nothing here synchronises with the host -- except `check=True`, which reads the call's device
     error flags afterwards and raises RuntimeError when any is set."""
     dev = _lib.require_cuda(x, expert_ids, routing_weights, out, contrib, what="moe_forward")
@@ -614,7 +618,14 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     n_tok, top_k = expert_ids.shape
     ids = expert_ids if expert_ids.stride(1) == 1 else expert_ids.contiguous()
     ids_code = _lib.DTYPE_CODE[ids.dtype]
-    if out is None and contrib is None:
+    if shared_last:
+        if contrib is not None:
+            raise RuntimeError("moe_forward: shared_last needs the layer's own combine (no contrib)")
+        if result is None:
+            result = torch.empty(n_tok, table.hidden, dtype=x.dtype, device=dev)
+        elif result.dtype != x.dtype or result.stride(-1) != 1:
+            raise RuntimeError("moe_forward: result must be [T, hidden] in the activation dtype")
+    elif out is None and contrib is None:
         out = torch.empty(n_tok, table.hidden, dtype=torch.float32, device=dev)
     if path is None:
         path = PATH_PREFILL if (n_tok * top_k > PREFILL_ROWS_PER_EXPERT * table.n_experts
@@ -625,10 +636,13 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
                        routing_weights.stride(1), _lib.ptr(w_index), out, contrib, h_out)
         c.expert_base, c.col_blocks = int(expert_base), int(col_blocks)
         c.ids_row_stride = ids.stride(0)
+        if shared_last:
+            c.shared_last = 1
+            c.result, c.result_row_stride = result.data_ptr(), (result.stride(0) if result.dim() == 2 else table.hidden)
         _enqueue(c, path, dev, workspace)
         if check:
             _check_flags(c, path, dev)
-    return out
+    return result if shared_last else out
 
 
 def shared_expert_forward(x, shared: ExpertTable, gate=None, out=None, *, workspace=None):
@@ -644,13 +658,61 @@ def shared_expert_forward(x, shared: ExpertTable, gate=None, out=None, *, worksp
     return moe_forward(x, ids, w, shared, out=out, path=PATH_DECODE, workspace=workspace)
 
 
+_SHARED_BUFS: dict = {}
+
+
+def _with_shared(table: ExpertTable, shared: ExpertTable) -> ExpertTable:
+    """`table` with `shared`'s expert appended as entry n_experts (cached on the table)."""
+    cache = table.__dict__.setdefault("_shared_ext", {})
+    hit = cache.get(id(shared))
+    if hit is None or hit[0] is not shared:
+        hit = (shared, ExpertTable(list(table.blobs) + list(shared.blobs)))
+        cache[id(shared)] = hit
+    return hit[1]
+
+
+def _shared_inputs(expert_ids, routing_weights, gate, n_experts):
+    """[T, K + 1] ids and weights: the routed slots, then the shared expert (index n_experts,
+    weight 1 or the gate) -- reused buffers whose constant column is written once."""
+    T, K = expert_ids.shape
+    key = (T, K, expert_ids.dtype, routing_weights.dtype, expert_ids.device, n_experts, gate is None)
+    bufs = _SHARED_BUFS.get(key)
+    if bufs is None:
+        ids = torch.full((T, K + 1), n_experts, dtype=expert_ids.dtype, device=expert_ids.device)
+        w = torch.ones(T, K + 1, dtype=routing_weights.dtype, device=routing_weights.device)
+        bufs = _SHARED_BUFS[key] = (ids, w)
+    ids, w = bufs
+    ids[:, :K].copy_(expert_ids)
+    w[:, :K].copy_(routing_weights)
+    if gate is not None:
+        w[:, K].copy_(gate.reshape(T))
+    return ids, w
+
+
 def moe_forward_with_shared(x, expert_ids, routing_weights, table: ExpertTable, shared: ExpertTable,
-                            gate=None, out=None, **kw):
+                            gate=None, out=None, *, fused=True, result=None, **kw):
     """The routed layer plus the shared expert, combined as the reference's epilogue does
     (`_tail`, vaayu/packed_expert_kernels.py:502-508): out.to(act) + shared.to(act).  Returns the
-    act-dtype result; `out` (optional) receives the routed fp32 sum."""
+    act-dtype result; `out` (optional) receives the routed fp32 sum.
+
+    fused (default): ONE layer call -- the shared expert is appended to the table as an always-
+    routed extra slot of every token (weight 1, or the gate in the routing weights' dtype) and the
+    layer's combine applies the epilogue; bit-identical to the two-call form.  It is taken when the
+    shared expert has the routed experts' geometry and format, the gate converts exactly to the
+    routing-weight dtype, and no expert_base / contrib / w_index is given; otherwise the shared
+    expert runs as its own call (`shared_expert_forward`)."""
+    exact_gate = gate is None or routing_weights.dtype in (torch.float32, gate.dtype)
+    if (fused and exact_gate and shared.n_experts == 1 and shared.geom == table.geom
+            and shared.scale_dtype == table.scale_dtype and shared.has_zero == table.has_zero
+            and not kw.get("expert_base") and kw.get("contrib") is None and kw.get("w_index") is None):
+        ids, w = _shared_inputs(expert_ids, routing_weights, gate, table.n_experts)
+        return moe_forward(x, ids, w, _with_shared(table, shared), out=out, shared_last=True, result=result, **kw)
     out = moe_forward(x, expert_ids, routing_weights, table, out=out, **kw)
-    return _tail(out, x.dtype, shared_expert_forward(x, shared, gate))
+    res = _tail(out, x.dtype, shared_expert_forward(x, shared, gate))
+    if result is not None:
+        result.copy_(res)
+        return result
+    return res
 
 
 def moe_workspace_bytes(table: ExpertTable, n_tokens: int, top_k: int, path: int = PATH_DECODE,
