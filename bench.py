@@ -43,7 +43,7 @@ WORKLOAD = dict(name="cfg1: Qwen3-30B-A3B-shaped int4 MoE layer, decode", hidden
                 experts=128, top_k=8, tokens=32, group=128)
 CFG3 = dict(name="cfg3: DeepSeek-V3-shaped int4 MoE layer (256 routed experts, top-8, 1 shared), "
                  "expert-parallel decode", hidden=7168, inter=2048, experts=256, top_k=8, tokens=64,
-            group=128, shared=1)
+            group=128, shared=1, zeros=True)   # zero points U{0..15} per (row, group), as configuration 3 asks
 PREFILL = dict(name="cfg2: Mixtral-8x7B-shaped int4 MoE layer, prefill", hidden=4096, inter=14336,
                experts=8, top_k=2, tokens=2048, group=128, skew=0.9)
 PEAKS = ROOT / "MEASURED_PEAKS.json"
@@ -159,7 +159,7 @@ def make_layer(seed, wl, device, experts_slice=None):
     blobs = []
     lo, hi = experts_slice or (0, wl["experts"])
     for e in range(wl["experts"]):
-        by_role = synthetic.make_expert(wl["hidden"], wl["inter"], g, group=wl["group"])
+        by_role = synthetic.make_expert(wl["hidden"], wl["inter"], g, group=wl["group"], zeros=wl.get("zeros", False))
         if lo <= e < hi:
             blobs.append(vb.build_expert_blob(by_role))
     return blobs
@@ -490,6 +490,19 @@ def run_ours(args, rank, world, local):
     h2d = nbytes                      # the record copied each step (its fields padded to 16 bytes)
     d2h = out_h.numel() * out_h.element_size()
 
+    # the same step with explicit zero points (asymmetric int4, z ~ U{0..15} per row and group; the
+    # headline keeps the reference's symmetric format)
+    zl = [pk.ExpertTable(make_layer(1000 * l, dict(wl, zeros=True), device)) for l in range(L)]
+    zstep = lambda i: vb.moe_forward(batches[T][i % L][0], batches[T][i % L][2], batches[T][i % L][1], zl[i % L],
+                                     out=out, path=vb.PATH_DECODE, workspace=ws)
+    for i in range(3):
+        zstep(i)
+    zms = time_steps(zstep, args.steps, device)
+    zb = statistics.mean(unique_bytes(zl[l], batches[T][l][2])[0] for l in range(L))
+    sweep[f"T={T}, zero points"] = {"tokens_per_s": T / (zms / 1e3), "ms_per_step": zms,
+                                    "layer_GBps": zb / (zms / 1e3) / 1e9}
+    del zl
+
     cpu = cpu_baseline(layers[0], batches[T][0], wl) if rank == 0 and not args.no_cpu else None
     del layers, batches
     torch.cuda.empty_cache()
@@ -516,7 +529,7 @@ def run_ours(args, rank, world, local):
                   "stage_ms": {k: statistics.mean(v) for k, v in stage.items()}},
         "sweep": sweep,
         "cpu_baseline": cpu,
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 4 * args.steps,   # plan, gate/up, down, ordered combine per step
         "clocks": clocks.summary(),
         "prefill": prefill,
         "block_scaled": blocks,

@@ -374,6 +374,8 @@ def run_bench(args, rank, world, local, wl):
                          "peak": peak, "unit": "GB/s", "frac": None, "peak_source": peak_kind,
                          "traffic": None},
             "cpu_baseline": None,
-            "gpu_launches": 4 * args.steps,
+            # plan, gate/up, down and the rank-ordered sum (one GPU: the layer's combine), plus the
+            # separate shared-expert call's four on several GPUs
+            "gpu_launches": (4 + (4 if shared is not None and world > 1 else 0)) * args.steps,
             "clocks": clocks.summary(),
         }))
