@@ -151,16 +151,18 @@ class ClockSampler:
 
 # ── workload ─────────────────────────────────────────────────────────────────────────────
 
-def make_layer(seed, wl, device, experts_slice=None):
-    """One layer's expert blobs (generated on the device from a seeded CUDA generator)."""
+def make_layer(seed, wl, device, experts_slice=None, keep=None):
+    """One layer's expert blobs (generated on the device from a seeded CUDA generator): all of
+    them, the range `experts_slice` = (lo, hi), or the ids in `keep`, in ascending id."""
     import vaayu_b200 as vb
     from vaayu_b200 import synthetic
     g = torch.Generator(device=device).manual_seed(seed)
     blobs = []
     lo, hi = experts_slice or (0, wl["experts"])
+    keep = set(keep) if keep is not None else set(range(lo, hi))
     for e in range(wl["experts"]):
         by_role = synthetic.make_expert(wl["hidden"], wl["inter"], g, group=wl["group"], zeros=wl.get("zeros", False))
-        if lo <= e < hi:
+        if e in keep:
             blobs.append(vb.build_expert_blob(by_role))
     return blobs
 
@@ -384,6 +386,9 @@ def run_ours(args, rank, world, local):
     device = torch.device("cuda", local)
     wl = dict(WORKLOAD)
     T, K = wl["tokens"], wl["top_k"]
+    if args.workload == "cfg2":
+        from vaayu_b200 import ep
+        return ep.run_prefill_bench(args, rank, world, local, PREFILL)
     if world > 1 or args.workload == "cfg3":
         from vaayu_b200 import ep
         return ep.run_bench(args, rank, world, local, CFG3 if args.workload == "cfg3" else wl)
@@ -639,9 +644,11 @@ def main():
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the configuration-2 prefill measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
-    ap.add_argument("--workload", default="cfg1", choices=("cfg1", "cfg3"),
+    ap.add_argument("--workload", default="cfg1", choices=("cfg1", "cfg2", "cfg3"),
                     help="cfg1 (default): the headline decode workload (expert-parallel for N > 1); "
-                         "cfg3: DeepSeek-V3 shape, expert-parallel at any N")
+                         "cfg2: the Mixtral-shaped 2048-token prefill, experts and tokens split over N "
+                         "GPUs (strong scaling, dispatch mode); cfg3: DeepSeek-V3 shape, "
+                         "expert-parallel at any N")
     ap.add_argument("--ep-col-blocks", type=int, default=None, choices=(1, 2, 4),
                     help="tokens per expert pass (x8) in the expert-parallel step; default by load")
     args = ap.parse_args()

@@ -39,7 +39,7 @@ def _geom():
     return (4, 32, (("gate", I, H), ("down", H, I), ("up", I, H)))
 
 
-def _worker(rank, port, result_dir):
+def _worker(rank, port, result_dir, placement="contiguous"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=2)
     try:
@@ -48,7 +48,7 @@ def _worker(rank, port, result_dir):
         from vaayu_b200.ep import ExpertParallelLayer
         experts, toks = _setup()
         per = E // 2
-        local = experts[rank * per:(rank + 1) * per]
+        local = experts[rank * per:(rank + 1) * per] if placement == "contiguous" else experts[rank::2]
 
         def compute(x_rows, local_ids, w_rows):
             if x_rows.shape[0] == 0:
@@ -70,7 +70,8 @@ def _worker(rank, port, result_dir):
             uneven_refused = False
         except ValueError:
             uneven_refused = True
-        layer = ExpertParallelLayer(None, E, compute=compute, combine_fn=combine, hidden=H, mode="dispatch")
+        layer = ExpertParallelLayer(None, E, compute=compute, combine_fn=combine, hidden=H, mode="dispatch",
+                                    placement=placement)
         x, ids, w = toks[rank]
         got = layer.forward(x, ids, w)
         ref = O.moe_layer(_geom(), experts, TH.to_np(x), O.BF16, ids.numpy(), w.numpy(), O.F32, O.F16)
@@ -81,8 +82,9 @@ def _worker(rank, port, result_dir):
         dist.destroy_process_group()
 
 
-def test_dispatch_mode_equals_one_process_bit_for_bit(tmp_path):
-    mp.spawn(_worker, args=(_free_port(), str(tmp_path)), nprocs=2, join=True)
+@pytest.mark.parametrize("placement", ["contiguous", "interleaved"])
+def test_dispatch_mode_equals_one_process_bit_for_bit(tmp_path, placement):
+    mp.spawn(_worker, args=(_free_port(), str(tmp_path), placement), nprocs=2, join=True)
     for r in range(2):
         ok, err, uneven_refused = np.load(tmp_path / f"rank{r}.npy")
         assert ok, f"rank {r}: max |diff| {err}"

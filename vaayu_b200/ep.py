@@ -22,20 +22,25 @@ Layout: rank r holds the contiguous expert range [r * E/P, (r+1) * E/P) as a res
 
 "dispatch" (large batches, where replicating every token to every rank would move too much):
 
-  1. every (token, slot) row is addressed to the rank owning its expert; the per-destination row
-     counts cross with one all-to-all (and come to the host: they size the variable exchange);
-  2. the rows' activations, local expert ids and routing weights cross with all-to-all
-     (NCCL over NVLink; peer data always lands in this GPU's own memory before a kernel reads it);
+  1. every (token, slot) row is addressed to the rank owning its expert, into a fixed-capacity
+     slot range per destination (T * K slots, enough for any routing; empty slots carry expert
+     id -1), so the exchange needs no row counts on the host;
+  2. the rows' activations, local expert ids and routing weights cross with equal-split
+     all-to-alls (NCCL over NVLink; peer data always lands in this GPU's own memory before a
+     kernel reads it);
   3. each rank computes every received row's weighted contribution with the local kernels
-     (`moe_forward(..., contrib=...)`, top_k = 1 per received row);
-  4. the contributions (fp32) travel back with the reverse all-to-all and are put back in
+     (`moe_forward(..., contrib=...)`, top_k = 1 per received row; the routing plan drops the
+     empty slots);
+  4. the contributions (fp32) travel back with the reverse all-to-all and are read out in
      (token, slot) order;
   5. the home rank sums each token's contributions in ascending GLOBAL expert id, then slot
      (`combine`) -- `accumulate_expert_outputs`' order (vaayu/moe_patch.py:914-940).
 
 A row's contribution does not depend on the rows it is computed with, and step 5 is the same fp32
 sum in the same order as on one GPU, so the dispatch-mode result equals the single-GPU result
-bit for bit.  The reference is single-GPU; this module has no counterpart there.
+bit for bit when both run the same kernels (`path`: the decode GEMVs or the prefill GEMMs; by
+default each side picks by its own call size).  The reference is single-GPU; this module has no
+counterpart there.
 """
 from __future__ import annotations
 
@@ -57,15 +62,24 @@ class ExpertParallelLayer:
     combine_fn    optional (contrib [T*K, H], global ids [T, K]) -> out [T, H]; default `combine`
     layer_fn      optional (x [N, H], local ids [N, K] with -1 for other ranks' slots, w [N, K])
                   -> per-token partial sums [N, H] fp32; replicate mode; default: the CUDA kernels
+    placement     "contiguous" (rank r holds [r E/P, (r+1) E/P)) or, in dispatch mode only,
+                  "interleaved" (rank r holds experts r, r + P, r + 2P, ...: round-robin, which
+                  spreads load that grows or shrinks with the expert index); local_blobs are the
+                  rank's experts in ascending global id either way
     """
 
     def __init__(self, local_blobs, n_experts: int, group=None, compute: Optional[Callable] = None,
                  combine_fn: Optional[Callable] = None, hidden: Optional[int] = None,
                  mode: str = "auto", replicate_max_tokens: int = 256,
-                 layer_fn: Optional[Callable] = None, col_blocks: Optional[int] = None):
+                 layer_fn: Optional[Callable] = None, col_blocks: Optional[int] = None,
+                 path: Optional[int] = None, placement: str = "contiguous"):
         if mode not in ("auto", "replicate", "dispatch"):
             raise ValueError(f"mode {mode!r}")
+        if placement not in ("contiguous", "interleaved") or (placement == "interleaved" and mode != "dispatch"):
+            raise ValueError(f"placement {placement!r} with mode {mode!r} (interleaved needs dispatch mode)")
+        self.interleaved = placement == "interleaved"
         self.mode = mode
+        self.path = path      # dispatch mode's local kernels: None = moe_forward's size rule
         self.replicate_max_tokens = replicate_max_tokens
         self.col_blocks = col_blocks
         self._layer_fn = layer_fn
@@ -96,49 +110,82 @@ class ExpertParallelLayer:
         dist.all_to_all_single(out, inp, output_split_sizes=out_splits,
                                input_split_sizes=in_splits, group=self.group)
 
+    def _dispatch_buffers(self, T, K, x, weights):
+        """Fixed-capacity exchange buffers: `cap` = T * K slots per destination, enough for any
+        routing (a token may even name one expert twice)."""
+        key = ("dispatch", T, K, x.dtype, weights.dtype, x.device)
+        b = self._bufs.get(key)
+        if b is None:
+            P, H, dev = self.world, x.shape[1], x.device
+            cap = T * K
+            b = dict(cap=cap,
+                     send_x=torch.empty(P * cap, H, dtype=x.dtype, device=dev),
+                     send_id=torch.empty(P * cap, dtype=torch.int32, device=dev),
+                     send_w=torch.empty(P * cap, dtype=torch.float32, device=dev),
+                     recv_x=torch.empty(P * cap, H, dtype=x.dtype, device=dev),
+                     recv_id=torch.empty(P * cap, dtype=torch.int32, device=dev),
+                     recv_w=torch.empty(P * cap, dtype=torch.float32, device=dev),
+                     contrib=torch.empty(P * cap, H, dtype=torch.float32, device=dev),
+                     back=torch.empty(P * cap, H, dtype=torch.float32, device=dev),
+                     tok=torch.arange(T * K, device=dev) // K,
+                     ranks=torch.arange(P, device=dev).view(1, P))
+            self._bufs[key] = b
+        return b
+
     def dispatch(self, x, ids, weights):
-        """(recv_x, recv_local_ids, recv_w, plan) -- the rows this rank computes."""
+        """(recv_x, recv_local_ids, recv_w, plan) -- the rows this rank computes.  Row j of
+        (token, slot) order goes to slot `dest * cap + pos` of the send buffer (pos: its rank among
+        the rows for the same destination, in row order); empty slots carry expert id -1, which
+        the routing plan drops.  Equal-split exchanges: no host round trip, graph-capturable."""
         T, K = ids.shape
-        dev = x.device
+        P = self.world
+        b = self._dispatch_buffers(T, K, x, weights)
+        cap = b["cap"]
         flat = ids.reshape(-1).to(torch.int64)
-        dest = torch.div(flat, self.per_rank, rounding_mode="floor")
-        order = torch.argsort(dest, stable=True)                 # rows grouped by destination
-        send_counts = torch.bincount(dest, minlength=self.world)
-        recv_counts = torch.empty_like(send_counts)
-        self._a2a(recv_counts, send_counts, None, None)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()     # host: sizes the exchange
-        rows = order
-        send_x = x.index_select(0, torch.div(rows, K, rounding_mode="floor"))
-        send_meta = torch.stack([(flat[rows] - dest[rows] * self.per_rank).to(torch.float32),
-                                 weights.reshape(-1)[rows].to(torch.float32)], dim=1)
-        n_recv = int(sum(rc))
-        recv_x = torch.empty(n_recv, x.shape[1], dtype=x.dtype, device=dev)
-        recv_meta = torch.empty(n_recv, 2, dtype=torch.float32, device=dev)
-        self._a2a(recv_x, send_x, rc, sc)
-        self._a2a(recv_meta, send_meta, rc, sc)
-        recv_ids = recv_meta[:, 0].to(torch.int32).view(-1, 1)
-        recv_w = recv_meta[:, 1].view(-1, 1)
+        if self.interleaved:       # expert e lives on rank e % P as local expert e // P
+            dest = torch.remainder(flat, P)
+            local = torch.div(flat, P, rounding_mode="floor")
+        else:
+            dest = torch.div(flat, self.per_rank, rounding_mode="floor")
+            local = flat - dest * self.per_rank
+        # rank among the rows bound for the same destination (a running count; no host check)
+        hit = (dest.view(-1, 1) == b["ranks"]).to(torch.int32)
+        pos = hit.cumsum(0).gather(1, dest.view(-1, 1)).view(-1) - 1
+        slot = dest * cap + pos
+        b["send_id"].fill_(-1)
+        b["send_id"].index_copy_(0, slot, local.to(torch.int32))
+        b["send_w"].index_copy_(0, slot, weights.reshape(-1).to(torch.float32))
+        b["send_x"].index_copy_(0, slot, x.index_select(0, b["tok"]))
+        self._a2a(b["recv_id"], b["send_id"], None, None)
+        self._a2a(b["recv_w"], b["send_w"], None, None)
+        self._a2a(b["recv_x"], b["send_x"], None, None)
+        recv_w = b["recv_w"].view(-1, 1)
         if weights.dtype != torch.float32:
             # the exchange carries fp32; the routing weight keeps its own dtype for the rounding rule
             recv_w = recv_w.to(weights.dtype)
-        return recv_x, recv_ids, recv_w, (order, sc, rc, T, K)
+        return b["recv_x"], b["recv_id"].view(-1, 1), recv_w, (slot, b)
 
-    def compute(self, recv_x, recv_ids, recv_w):
+    def compute(self, recv_x, recv_ids, recv_w, plan=None):
+        """Contributions [P * cap, H] fp32 of the received rows (slots with id -1 stay unwritten:
+        their rows are never read back)."""
+        b = plan[1] if plan is not None else None
+        contrib = b["contrib"] if b is not None else torch.empty(recv_x.shape[0], self.hidden, dtype=torch.float32,
+                                                                    device=recv_x.device)
         if self._compute is not None:
-            return self._compute(recv_x, recv_ids, recv_w)
-        from .packed_expert_kernels import PATH_DECODE, moe_forward
-        contrib = torch.empty(recv_x.shape[0], self.hidden, dtype=torch.float32, device=recv_x.device)
+            live = (recv_ids.view(-1) >= 0).nonzero().view(-1)    # a host-side callback sees only real rows
+            if live.numel():
+                contrib[live] = self._compute(recv_x[live], recv_ids[live], recv_w[live]).to(contrib.device)
+            return contrib
+        from .packed_expert_kernels import moe_forward
         if recv_x.shape[0]:
-            moe_forward(recv_x, recv_ids, recv_w, self.table, contrib=contrib, path=PATH_DECODE)
+            moe_forward(recv_x, recv_ids, recv_w, self.table, contrib=contrib, path=self.path)
         return contrib
 
     def gather_back(self, contrib, plan):
-        order, sc, rc, T, K = plan
-        back = torch.empty(T * K, contrib.shape[1], dtype=contrib.dtype, device=contrib.device)
-        self._a2a(back, contrib, sc, rc)
-        rows = torch.empty_like(back)
-        rows[order] = back                                       # (token, slot) order again
-        return rows
+        """This rank's rows' contributions back from their experts' ranks, in (token, slot) order."""
+        slot, b = plan
+        self._a2a(b["back"], contrib, None, None)
+        return b["back"].index_select(0, slot)
 
     # ── replicate mode ───────────────────────────────────────────────────────────────────
     def _buffers(self, T, K, x, weights):
@@ -223,7 +270,7 @@ class ExpertParallelLayer:
         if mode == "replicate":
             return self.replicate_forward(x, ids, weights, out)
         recv_x, recv_ids, recv_w, plan = self.dispatch(x, ids, weights)
-        contrib = self.compute(recv_x, recv_ids, recv_w)
+        contrib = self.compute(recv_x, recv_ids, recv_w, plan)
         rows = self.gather_back(contrib, plan)
         if self._combine is not None:
             res = self._combine(rows, ids)
@@ -377,5 +424,128 @@ def run_bench(args, rank, world, local, wl):
             # plan, gate/up, down and the rank-ordered sum (one GPU: the layer's combine), plus the
             # separate shared-expert call's four on several GPUs
             "gpu_launches": (4 + (4 if shared is not None and world > 1 else 0)) * args.steps,
+            "clocks": clocks.summary(),
+        }))
+
+
+def run_prefill_bench(args, rank, world, local, wl):
+    """bench.py's configuration-2 arm at any N (strong scaling): the one-GPU prefill bench's
+    2048-token batches (same seeds), rank r holding tokens [r T/N, (r + 1) T/N) and experts
+    r, r + N, r + 2N, ...; dispatch mode -- the rows to their experts' ranks by all-to-all (a fixed
+    capacity per destination, no host round trip), the local tcgen05 prefill GEMMs, contributions
+    back by the reverse all-to-all, the ascending-global-expert combine on each token's home rank.
+    Each layer step is one CUDA graph."""
+    import json
+
+    import bench
+    from . import synthetic
+    device = torch.device("cuda", local)
+    E, T, K, H, I = wl["experts"], wl["tokens"], wl["top_k"], wl["hidden"], wl["inter"]
+    if E % world or T % world:
+        raise ValueError(f"configuration 2 splits {E} experts and {T} tokens evenly: not over {world} GPUs")
+    per, tl = E // world, T // world
+    L = 2
+    # round-robin placement: the benchmark's router skew grows with the expert index, which
+    # contiguous ranges would hand to the last rank
+    layers = [ExpertParallelLayer(bench.make_layer(2000 + l, wl, device, keep=range(rank, E, world)), E,
+                                  mode="dispatch", placement="interleaved") for l in range(L)]
+    batches = []
+    for l in range(L):
+        g = torch.Generator(device=device).manual_seed(20_000 + l)
+        x, w, idx = synthetic.make_tokens(T, H, E, K, g, skew=wl["skew"])
+        sl = slice(rank * tl, (rank + 1) * tl)
+        batches.append((x[sl].contiguous(), w[sl].contiguous(), idx[sl].contiguous()))
+    out = torch.empty(tl, H, dtype=torch.float32, device=device)
+    # each layer's inputs are views of one device record (the end-to-end step fills it with one copy)
+    nbytes, views = bench.record_layout(batches[0])
+    drecs = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(L)]
+    dviews = []
+    for l in range(L):
+        vs = views(drecs[l])
+        for v, src in zip(vs, batches[l]):
+            v.copy_(src)
+        dviews.append(vs)
+
+    def layer_step(l):
+        xv, wv, iv = dviews[l]
+        layers[l].forward(xv, iv, wv, out)
+
+    for l in range(L):
+        for _ in range(2):
+            layer_step(l)
+    torch.cuda.synchronize(device)
+    bench.barrier(world)
+    graphs = []
+    try:   # the dispatch is free of host round trips: one CUDA graph per layer step
+        for l in range(L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                layer_step(l)
+            graphs.append(g)
+        torch.cuda.synchronize(device)
+    except Exception as e:  # noqa: BLE001 - report and run eagerly
+        graphs = []
+        if rank == 0:
+            print(f"# EP graph capture unavailable, eager steps: {e}", flush=True)
+    bench.barrier(world)
+
+    def step(i):
+        if graphs:
+            graphs[i % L].replay()
+        else:
+            layer_step(i % L)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    steps = max(5, min(args.steps, 20))
+    bench.barrier(world)
+    with bench.ClockSampler(local) as clocks:
+        ms = bench.time_steps(step, steps, device)
+    bench.barrier(world)
+    ms = bench.max_over_ranks(ms, world)
+
+    pin = [bench.pinned_record(b, nbytes, views) for b in batches]
+    out_h = torch.empty(tl, H, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        l = i % L
+        drecs[l].copy_(pin[l], non_blocking=True)
+        step(i)
+        out_h.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    bench.barrier(world)
+    e2e_ms = bench.max_over_ranks(bench.time_steps(e2e_step, steps, device), world)
+    bench.barrier(world)
+    used_graphs = bool(graphs)
+    del graphs               # graphs holding NCCL calls go before the process group does
+    torch.cuda.synchronize(device)
+    flops = 2.0 * T * K * 3 * H * I
+    burst, sustained, src = bench.bf16_peak()
+    achieved = flops / (ms / 1e3) / 1e12 / world           # per GPU
+    if rank == 0:
+        print(json.dumps({
+            "metric": bench.METRIC, "value": T / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1), "
+                    f"router logits skewed by linspace(0, {wl['skew']}, {E}))",
+            "config": {"workload": wl["name"], "hidden": H, "expert_intermediate": I, "experts": E,
+                       "top_k": K, "tokens_total": T, "tokens_per_gpu": tl, "group_size": wl["group"],
+                       "layers_rotated": L, "l2": "inputs larger than L2 (each layer's expert weights: ~730 MB)",
+                       "parallelism": f"ep{world}: {per} experts per GPU (round-robin); dispatch mode: "
+                                      f"fixed-capacity all-to-alls of rows and contributions, "
+                                      f"ascending-global-expert combine",
+                       "cuda_graphs": used_graphs},
+            "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
+                    "d2h_bytes_per_step": out_h.numel() * out_h.element_size(), "ms_per_step": e2e_ms},
+            "roofline": {"kernel": "layer (expert parallel, communication included)", "bound": "tensor",
+                         "achieved": achieved, "peak": burst, "unit": "TFLOP/s", "frac": achieved / burst,
+                         "peak_source": f"{src} (burst), per GPU", "traffic": None},
+            "cpu_baseline": None,
+            # plan, gather, gate/up GEMM, down GEMM (contributions) and the home-rank combine
+            "gpu_launches": 5 * steps,
             "clocks": clocks.summary(),
         }))
