@@ -2,7 +2,7 @@
 
 Run in a container that holds the reference project (read-only) and compressed-tensors:
 
-    python tests/golden/make_golden.py [path/to/reference]
+    python tests/golden/make_golden.py <path to the reference project>
 
 The reference's package `vaayu/__init__.py` pulls in `accelerate`; a namespace stub for `vaayu`
 skips that file so `vaayu.moe_patch`, `vaayu.packed_expert_kernels` and the DeepSeek-V4 modeling
@@ -271,7 +271,9 @@ def gen_asym(ct, out):
 
 
 def main():
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path to the reference project>")
+    root = Path(sys.argv[1])
     mp, pk, ds = _import_reference(root)
     import compressed_tensors.compressors.pack_quantized.helpers as ct
     torch.set_num_threads(8)
