@@ -200,6 +200,10 @@ typedef struct vy_expert_geom {
  *                   receives that routed fp32 sum; `contrib` must be NULL.
  *   result          [n_tokens, hidden] act dtype, written when shared_last is 1.
  *   result_row_stride  elements between result rows (>= hidden).
+ *   k_splits        decode: warps sharing one gate/up unit's K range -- 0: the library's choice
+ *                   (more than one only when a call has few units per warp, e.g. 1-4 tokens),
+ *                   1: none, 2 / 4 / 8: that many (dividing hidden / 128).  The result does not
+ *                   depend on it (each unit's per-stage partials are added in stage order).
  */
 typedef struct vy_moe_call {
     const vy_expert_geom* geom;
@@ -239,7 +243,7 @@ typedef struct vy_moe_call {
     int64_t ids_row_stride;
     /* ABI version 3 */
     int32_t shared_last;
-    int32_t reserved2;
+    int32_t k_splits;
     void* result;
     int64_t result_row_stride;
 } vy_moe_call;

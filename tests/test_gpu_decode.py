@@ -374,3 +374,29 @@ def test_the_fused_shared_expert_equals_two_calls_bit_for_bit(path, gated, wdt):
     two = vb.moe_forward_with_shared(x, idx, w, table, shared, gate=gate, path=path, fused=False)
     if path == vb.PATH_DECODE:
         assert torch.equal(got, two)
+
+
+@pytest.mark.parametrize("tokens", [1, 3])
+def test_split_k_gate_up_is_bit_identical_to_one_warp_per_unit(tokens):
+    """Few-token calls share each gate/up unit's K range among warps; the per-stage partial dots
+    are added in stage order by the last split, so every split count gives the same bits."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 64, 8, tokens, seed=31)
+    table = pk.ExpertTable(blobs)
+    outs = {s: vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=s) for s in (1, 2, 4, 8)}
+    auto = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE)
+    for s in (2, 4, 8):
+        assert torch.equal(outs[s], outs[1]), f"k_splits={s}"
+    assert torch.equal(auto, outs[1])
+    ref = T.oracle_layer(blobs, x, idx, w)
+    assert T.rel_l2(outs[1].cpu().numpy(), ref) <= 1e-3
+
+
+def test_a_token_gets_the_same_bits_alone_and_in_a_batch():
+    """Decode rows are independent: a token's output from a one-token call (split K) equals its
+    row inside a 32-token call (no split)."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 64, 8, 32, seed=37)
+    table = pk.ExpertTable(blobs)
+    batch = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE)
+    for t in (0, 5, 31):
+        one = vb.moe_forward(x[t:t + 1], idx[t:t + 1], w[t:t + 1], table, path=vb.PATH_DECODE)
+        assert torch.equal(one[0], batch[t]), f"token {t}"

@@ -40,7 +40,7 @@ class MoeCall(ctypes.Structure):
                 ("contrib", P), ("h_out", P), ("workspace", P), ("workspace_bytes", SZ),
                 ("stage_events", P), ("n_stage_events", I32T), ("reserved1", I32T),
                 ("col_blocks", I32T), ("expert_base", I32T), ("ids_row_stride", I64T),
-                ("shared_last", I32T), ("reserved2", I32T), ("result", P), ("result_row_stride", I64T)]
+                ("shared_last", I32T), ("k_splits", I32T), ("result", P), ("result_row_stride", I64T)]
 
 
 # name -> (restype, argtypes); every symbol include/vaayu_b200.h declares

@@ -11,12 +11,15 @@
 //                   reference's exact rounding of every weight) and feeds them to m16n8k16
 //                   tensor-core fragments (fp32 accumulate) whose N dimension is the tokens.
 //                   Epilogue: g, u, SiLU, product, each rounded to the activation dtype, into
-//                   h (stored in the pair-permuted order the down kernel reads).
-//   down_kernel     one CTA = 16 output rows of the down projection; its warps walk the live
-//                   experts, compute y = h . Wd^T for every routed row, multiply by the routing
-//                   weight and park the fp32 contribution in shared memory; the CTA then sums
-//                   each token's contributions in ascending expert id and writes its 16
-//                   columns of `out` -- no atomics, no second pass over HBM.
+//                   h (stored in the pair-permuted order the down kernel reads).  A call with
+//                   few units per warp splits each unit's K range over 2-8 warps: they store
+//                   their stages' partial dots and the last to finish adds all of them in stage
+//                   order, so the result does not depend on the split.
+//   down_kernel     one warp = 16 output rows of the down projection for one pass of a live
+//                   expert (units dealt pass-major over every warp), y = h . Wd^T for every
+//                   routed row, times the routing weight, into fp32 contributions by row id.
+//   combine         (vy_route.cu) each token's contributions summed in ascending expert id,
+//                   then slot -- no atomics on the sums.
 //
 // The dequantised operand never touches shared memory, which is what keeps this path on HBM
 // bandwidth: a tcgen05 GEMM would have to write every dequantised weight to shared memory and
@@ -55,6 +58,9 @@ struct GateUpParams {
     const uint16_t* x_perm;
     uint16_t* h_perm;
     uint16_t* h_out;
+    int k_splits;         // warps sharing one unit's K range (1: none)
+    float* partial;       // k_splits > 1: [unit][stage][lane][8 NB] per-stage partial dots
+    int32_t* tickets;     // k_splits > 1: [unit] finished splits, zeroed by the plan kernel
 };
 
 struct DownParams {
@@ -81,6 +87,8 @@ struct UnitInfo {
     const int32_t* zp;
     int ncols;
     int tile;
+    int split;         // gate/up with split K: which share of the unit's K range
+    int unit;          // gate/up with split K: pass * tiles + tile
     int col_row[NB];   // row id of this lane's column (cb * 8 + g) in each block, -1 if none
     bool ok;
 };
@@ -94,12 +102,12 @@ struct UnitQueue {
         const int32_t* pk;
         const void* sc;
         const int32_t* zp;
-        int ncols, tile, ok;
+        int ncols, tile, split, unit, ok;
     } head[W][Q];
     int rows[W][Q][NB * 8];
 
     __device__ __forceinline__ void put(int warp, int slot, int lane, int g, const UnitInfo<NB>& u) {
-        if (lane == 0) head[warp][slot] = Head{u.pk, u.sc, u.zp, u.ncols, u.tile, u.ok};
+        if (lane == 0) head[warp][slot] = Head{u.pk, u.sc, u.zp, u.ncols, u.tile, u.split, u.unit, u.ok};
         if ((lane & 3) == 0)
 #pragma unroll
             for (int cb = 0; cb < NB; ++cb) rows[warp][slot][cb * 8 + g] = u.col_row[cb];
@@ -112,6 +120,8 @@ struct UnitQueue {
         u.zp = h.zp;
         u.ncols = h.ncols;
         u.tile = h.tile;
+        u.split = h.split;
+        u.unit = h.unit;
         u.ok = h.ok;
 #pragma unroll
         for (int cb = 0; cb < NB; ++cb) u.col_row[cb] = rows[warp][slot][cb * 8 + g];
@@ -128,6 +138,8 @@ __device__ __forceinline__ UnitInfo<NB> load_unit(const PassEntry* passes, int p
     u.zp = reinterpret_cast<const int32_t*>(pe.zp);
     u.ncols = pe.ncols;
     u.tile = tile;
+    u.split = 0;
+    u.unit = 0;
 #pragma unroll
     for (int cb = 0; cb < NB; ++cb) {
         const int col = cb * 8 + g;
@@ -171,7 +183,7 @@ __device__ __forceinline__ void dequant_chunk(const uint4& w, uint32_t bias, uin
             a[wi][j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[wi], j), bias), scale);
 }
 
-template <int ACT, int SC, bool ZERO, int NB>
+template <int ACT, int SC, bool ZERO, int NB, bool SPLIT>
 __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel(GateUpParams p) {
     extern __shared__ uint4 ring[];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -185,22 +197,31 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
     const int n_live = p.counters[0];
     if (n_live <= 0) return;
     const int tiles = p.inter / kTileRows;
-    const int total_units = p.unit_start[n_live] * tiles;
+    const int S = SPLIT ? p.k_splits : 1;          // 2, 4 or 8 in the split variant
+    const int total_units = p.unit_start[n_live] * tiles * S;
     const int gw = blockIdx.x * kGuWarps + warp, nw = gridDim.x * kGuWarps;
     if (gw >= total_units) return;
     const int my_units = (total_units - gw + nw - 1) / nw;
-    const int spu = p.hidden / kStageK;
+    const int spu = p.hidden / kStageK;            // stages of a whole unit
+    const int sps = spu / S;                       // stages of one split
     const int wpr = p.hidden / 8;
     const int groups = p.hidden >> p.gs_shift;
 
+    // unit u: split u % S of (pass, tile) = u / S; the S splits of a tile go to adjacent warps
     auto unit_at = [&](int i) {
         const int u = gw + i * nw;
-        const int pg = u / tiles;
-        return load_unit<NB>(p.passes, pg, u - pg * tiles, g);
+        const int ut = u / S;
+        const int pg = ut / tiles;
+        UnitInfo<NB> r = load_unit<NB>(p.passes, pg, ut - pg * tiles, g);
+        if constexpr (SPLIT) {
+            r.split = u - ut * S;
+            r.unit = ut;
+        }
+        return r;
     };
 
     // ── issue side: kGuDepth - 1 stages ahead of the consuming side ─────────────────────────
-    int i_ui = 0, i_ks = 0, i_slot = 0, i_left = my_units * spu;
+    int i_ui = 0, i_ks = 0, i_slot = 0, i_left = my_units * sps;
     UnitInfo<NB> i_nxt = unit_at(0);
     const int32_t* i_src_g = nullptr;
     const int32_t* i_src_u = nullptr;
@@ -212,7 +233,8 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
                 queue.put(warp, i_ui % kGuDepth, lane, g, cur);
                 if (i_ui + 1 < my_units) i_nxt = unit_at(i_ui + 1);
                 i_ok = cur.ok;
-                const int64_t row_off = int64_t(cur.tile * kTileRows + g) * wpr + tig * 4;
+                const int64_t row_off = int64_t(cur.tile * kTileRows + g) * wpr + tig * 4 +
+                                        (SPLIT ? cur.split * sps * 16 : 0);
                 i_src_g = cur.pk + p.w_off[0] + row_off;
                 i_src_u = cur.pk + p.w_off[1] + row_off;
             }
@@ -225,7 +247,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
             }
             i_src_g += 16;
             i_src_u += 16;
-            if (++i_ks == spu) {
+            if (++i_ks == sps) {
                 i_ks = 0;
                 ++i_ui;
             }
@@ -249,7 +271,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
     int sidx[4];      // scale element index of rows g, g+8 of gate, up at this thread's K offset
     int zidx[2];      // zero word index (rows g and g+8 share a nibble position) of gate, up
     const int kfirst = tig * 32;
-    for (int s = my_units * spu; s > 0; --s) {
+    for (int s = my_units * sps; s > 0; --s) {
         issue();
         if (c_ks == 0) {
             __syncwarp();
@@ -268,7 +290,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
         }
         cp_async_wait<kGuDepth - 1>();
         if (cu.ok) {
-            const int kx = c_ks * kStageK;
+            const int kx = ((SPLIT ? cu.split * sps : 0) + c_ks) * kStageK;
             // the first token block's activations first: their L2 latency hides behind the
             // dequant work below (further blocks, rarely populated at decode sizes, load in line)
             uint4 xv0[4];
@@ -318,19 +340,64 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
                     mma_16816<ACT>(su[cb], au0[2], au8[2], au0[3], au8[3], xv.z, xv.w);
                 }
             }
+            if constexpr (!SPLIT) {
 #pragma unroll
-            for (int cb = 0; cb < NB; ++cb) {
-                if (cb * 8 >= cu.ncols) break;
+                for (int cb = 0; cb < NB; ++cb) {
+                    if (cb * 8 >= cu.ncols) break;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc_g[cb][i] = __fadd_rn(acc_g[cb][i], sg[cb][i]);
-                    acc_u[cb][i] = __fadd_rn(acc_u[cb][i], su[cb][i]);
+                    for (int i = 0; i < 4; ++i) {
+                        acc_g[cb][i] = __fadd_rn(acc_g[cb][i], sg[cb][i]);
+                        acc_u[cb][i] = __fadd_rn(acc_u[cb][i], su[cb][i]);
+                    }
+                }
+            } else {
+                // split K: the stage's partial dots go to the unit's record, joined in stage order
+                // by whichever split finishes last
+                float4* rec = reinterpret_cast<float4*>(p.partial) +
+                              ((int64_t(cu.unit) * spu + cu.split * sps + c_ks) * 32 + lane) * (2 * NB);
+#pragma unroll
+                for (int cb = 0; cb < NB; ++cb) {
+                    if (cb * 8 >= cu.ncols) break;
+                    __stcg(rec + 2 * cb, make_float4(sg[cb][0], sg[cb][1], sg[cb][2], sg[cb][3]));
+                    __stcg(rec + 2 * cb + 1, make_float4(su[cb][0], su[cb][1], su[cb][2], su[cb][3]));
                 }
             }
         }
         if (++c_slot == kGuDepth) c_slot = 0;
-        if (++c_ks == spu) {
-            if (cu.ok) {
+        if (++c_ks == sps) {
+            bool finish = true;
+            if constexpr (SPLIT) {
+                // publish this split's stages; the last split to arrive sums all of them in stage
+                // order -- the same fp32 adds, in the same order, as one warp walking the unit
+                __threadfence();
+                __syncwarp();
+                int prev = 0;
+                if (lane == 0) prev = atomicAdd(p.tickets + cu.unit, 1);
+                prev = __shfl_sync(0xffffffffu, prev, 0);
+                finish = prev == S - 1;
+                if (finish && cu.ok) {
+                    __threadfence();
+                    const float4* rec = reinterpret_cast<const float4*>(p.partial) +
+                                        (int64_t(cu.unit) * spu * 32 + lane) * (2 * NB);
+                    for (int st = 0; st < spu; ++st) {
+#pragma unroll
+                        for (int cb = 0; cb < NB; ++cb) {
+                            if (cb * 8 >= cu.ncols) break;
+                            const float4 a = __ldcg(rec + int64_t(st) * 32 * 2 * NB + 2 * cb);
+                            const float4 b = __ldcg(rec + int64_t(st) * 32 * 2 * NB + 2 * cb + 1);
+                            acc_g[cb][0] = __fadd_rn(acc_g[cb][0], a.x);
+                            acc_g[cb][1] = __fadd_rn(acc_g[cb][1], a.y);
+                            acc_g[cb][2] = __fadd_rn(acc_g[cb][2], a.z);
+                            acc_g[cb][3] = __fadd_rn(acc_g[cb][3], a.w);
+                            acc_u[cb][0] = __fadd_rn(acc_u[cb][0], b.x);
+                            acc_u[cb][1] = __fadd_rn(acc_u[cb][1], b.y);
+                            acc_u[cb][2] = __fadd_rn(acc_u[cb][2], b.z);
+                            acc_u[cb][3] = __fadd_rn(acc_u[cb][3], b.w);
+                        }
+                    }
+                }
+            }
+            if (finish && cu.ok) {
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
 #pragma unroll
@@ -554,13 +621,15 @@ int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaS
     // unit assignment is static, so each whole grid must be resident at once).
     static int gu_blocks_per_sm = 0, dn_blocks_per_sm = 0;
     if (gu_blocks_per_sm == 0) {
-        cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(gu_smem()));
+        cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(gu_smem()));
         cudaFuncSetAttribute(down_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(dn_smem()));
         int nblk = 0, ndn = 0;
         cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &nblk, gate_up_kernel<ACT, SC, ZERO, NB>, kGuWarps * 32, gu_smem());
+            &nblk, gate_up_kernel<ACT, SC, ZERO, NB, false>, kGuWarps * 32, gu_smem());
         if (oe == cudaSuccess)
             oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ndn, down_kernel<ACT, SC, ZERO, NB>, kWarps * 32,
                                                                dn_smem());
@@ -569,7 +638,9 @@ int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaS
         gu_blocks_per_sm = nblk;
         dn_blocks_per_sm = ndn;
     }
-    cudaError_t e = launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu);
+    cudaError_t e = gu.k_splits > 1
+        ? launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB, true>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu)
+        : launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB, false>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
     if (timed) cudaEventRecord(ev[2], s);
     e = launch_pdl(down_kernel<ACT, SC, ZERO, NB>, dn_blocks_per_sm * sm_count, kWarps, dn_smem(), s, dn);
@@ -607,6 +678,10 @@ struct DecodeLayout {
     PassEntry* passes;
     uint16_t *x_perm, *h_perm;
     float* ybuf_g;   // the down projection's contributions (absent when the caller takes them)
+    int k_splits;    // gate/up split K (1: none)
+    int64_t max_units;
+    float* partial;  // k_splits > 1: per-stage partial dots of every gate/up unit
+    int32_t* tickets;
     size_t bytes;
 };
 
@@ -620,6 +695,23 @@ int nb_for(const vy_moe_call* c) {
 }
 int call_nb(const vy_moe_call* c) { return c->col_blocks ? c->col_blocks : nb_for(c); }
 
+// Gate/up warps of one resident wave on a 148-SM B200 (2 CTAs of kGuWarps): the split rule's
+// budget.  A fixed figure, so workspace sizing and launch agree on any device.
+constexpr int64_t kSplitWarps = 2 * 148 * kGuWarps;
+
+// Gate/up split K: when even the largest possible number of (pass, tile) units leaves three
+// quarters of the warps idle (batches of a token or two), each unit's K range is shared by 4 or 8
+// warps, as many as keep the units within one wave and every split at least two stages long.
+// (Measured on B200, cfg1: T = 1 38.1 -> 32.3 us with 4; a 2-way split at T = 2 cost more in
+// partial stores and the ordered join than it gained.)
+int k_splits_for(const vy_moe_call* c, int64_t max_units) {
+    if (c->k_splits) return c->k_splits;
+    const int spu = c->geom->hidden / kStageK;
+    int s = 1;
+    while (s < 8 && max_units * 2 * s <= kSplitWarps && spu % (2 * s) == 0 && spu / (2 * s) >= 2) s *= 2;
+    return s >= 4 ? s : 1;
+}
+
 DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
     const int64_t n = c->n_tokens * c->top_k;
     const int E = c->n_experts;
@@ -632,13 +724,20 @@ DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
     L.unit_start = cv.take<int32_t>(E + 1);
     L.slot_order = cv.take<int32_t>(n);
     L.counters = cv.take<int32_t>(4);
-    {
-        const int64_t tpu = call_nb(c) * 8, max_live = n < E ? n : E;
-        L.passes = cv.take<PassEntry>(n / tpu + max_live + 1);
-    }
+    const int64_t tpu = call_nb(c) * 8, max_live = n < E ? n : E;
+    const int64_t max_passes = n / tpu + max_live + 1;
+    L.passes = cv.take<PassEntry>(max_passes);
     L.x_perm = cv.take<uint16_t>(c->n_tokens * H);
     L.h_perm = cv.take<uint16_t>(n * I);
     L.ybuf_g = c->contrib == nullptr ? cv.take<float>(n * H) : nullptr;
+    L.max_units = max_passes * (I / kTileRows);
+    L.k_splits = k_splits_for(c, L.max_units);
+    L.partial = nullptr;
+    L.tickets = nullptr;
+    if (L.k_splits > 1) {
+        L.partial = cv.take<float>(L.max_units * (H / kStageK) * 32 * 8 * call_nb(c));
+        L.tickets = cv.take<int32_t>(L.max_units);
+    }
     L.bytes = cv.used;
     return L;
 }
@@ -680,6 +779,11 @@ int validate_call(const vy_moe_call* c) {
     if (c->n_tokens * int64_t(g.hidden) >= (int64_t(1) << 31) || n * int64_t(g.inter) >= (int64_t(1) << 31) ||
         n * int64_t(g.hidden) >= (int64_t(1) << 31))
         return fail(VY_ERR_UNSUPPORTED, "call too large for 32-bit element offsets");
+    if (c->k_splits != 0 && c->k_splits != 1 && c->k_splits != 2 && c->k_splits != 4 && c->k_splits != 8)
+        return fail(VY_ERR_INVALID, "k_splits %d (0, 1, 2, 4 or 8)", c->k_splits);
+    if (c->k_splits > 1 && (g.hidden / 128) % c->k_splits)
+        return fail(VY_ERR_INVALID, "k_splits %d does not divide the %d 128-element stages of hidden %d",
+                    c->k_splits, g.hidden / 128, g.hidden);
     if (c->shared_last != 0 && c->shared_last != 1)
         return fail(VY_ERR_INVALID, "shared_last %d (0 or 1)", c->shared_last);
     if (c->shared_last && (c->contrib || c->top_k < 2))
@@ -761,6 +865,10 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     pa.x_perm = L.x_perm;
     pa.expert_table = c->expert_table;
     pa.passes = L.passes;
+    if (L.k_splits > 1) {              // the split-K tickets start from zero every call
+        pa.zero_ints = L.tickets;
+        pa.zero_count = static_cast<int>(L.max_units);
+    }
     cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
     const bool timed = ev != nullptr && c->n_stage_events >= 4;
     if (timed && cudaEventRecord(ev[0], s) != cudaSuccess)
@@ -788,6 +896,9 @@ extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
     gu.x_perm = L.x_perm;
     gu.h_perm = L.h_perm;
     gu.h_out = static_cast<uint16_t*>(c->h_out);
+    gu.k_splits = L.k_splits;
+    gu.partial = L.partial;
+    gu.tickets = L.tickets;
 
     DownParams dn{};
     dn.hidden = g.hidden;

@@ -55,7 +55,12 @@ extern "C" int vy_moe_decode_static(const vy_moe_call* call, void* stream) {
     int st;
     if (!device_info(&st)) return st;
     if (!call || !call->geom) return fail(VY_ERR_INVALID, "vy_moe_decode_static: null call or geometry");
-    const size_t need = vy_moe_workspace_size(call, 0);
+    vy_moe_call local = *call;
+    size_t need = vy_moe_workspace_size(&local, 0);
+    if (need > VY_DECODE_STATIC_SCRATCH_BYTES && local.k_splits == 0) {
+        local.k_splits = 1;   // the split-K partials are what does not fit: run unsplit
+        need = vy_moe_workspace_size(&local, 0);
+    }
     if (need > VY_DECODE_STATIC_SCRATCH_BYTES)
         return fail(VY_ERR_UNSUPPORTED,
                     "vy_moe_decode_static: this call needs %zu bytes of scratch, more than the %zu "
@@ -64,7 +69,6 @@ extern "C" int vy_moe_decode_static(const vy_moe_call* call, void* stream) {
                     need, static_cast<size_t>(VY_DECODE_STATIC_SCRATCH_BYTES));
     void* scratch = nullptr;
     if ((st = scratch_address(&scratch)) != VY_OK) return st;
-    vy_moe_call local = *call;
     local.workspace = scratch;
     local.workspace_bytes = VY_DECODE_STATIC_SCRATCH_BYTES;
     return vy_moe_decode(&local, stream);

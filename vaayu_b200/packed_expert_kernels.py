@@ -593,7 +593,7 @@ def _check_flags(c, path, dev) -> None:
 
 def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *, path=None,
                 contrib=None, h_out=None, w_index=None, workspace=None, expert_base=0, col_blocks=0,
-                check=False, shared_last=False, result=None):
+                check=False, shared_last=False, result=None, k_splits=0):
     """The layer over a resident `ExpertTable` with the routing already on the device.
 
     x [T, hidden] act dtype; expert_ids [T, K] int32/int64 (indices into `table`; an id outside
@@ -604,6 +604,8 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     on the cfg1, cfg3 and Mixtral shapes lies between 8 and 16).  expert_base: expert_ids are global ids and the table holds [expert_base,
     expert_base + n) (others drop their slot); expert_ids may be a row-strided view.  col_blocks:
     tokens per decode pass of an expert in blocks of 8 (1, 2, 4; 0 = from the call size).
+    k_splits: decode warps sharing one gate/up unit's K range (0 = the library's choice, 1 = none,
+    2 / 4 / 8); the result does not depend on it.
     shared_last: slot K - 1 of every token is the block's shared expert (a table entry routed with
     weight 1 or its sigmoid gate); the call then ends with the model's epilogue
     result = act(act(routed fp32 sum) + act(shared contribution)) into `result` [T, hidden] act
@@ -634,7 +636,7 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
         c = _make_call(table.geom_s, x, n_tok, top_k, table.n_experts, table.table.data_ptr(),
                        ids.data_ptr(), ids_code, routing_weights, routing_weights.stride(0),
                        routing_weights.stride(1), _lib.ptr(w_index), out, contrib, h_out)
-        c.expert_base, c.col_blocks = int(expert_base), int(col_blocks)
+        c.expert_base, c.col_blocks, c.k_splits = int(expert_base), int(col_blocks), int(k_splits)
         c.ids_row_stride = ids.stride(0)
         if shared_last:
             c.shared_last = 1
@@ -716,13 +718,13 @@ def moe_forward_with_shared(x, expert_ids, routing_weights, table: ExpertTable, 
 
 
 def moe_workspace_bytes(table: ExpertTable, n_tokens: int, top_k: int, path: int = PATH_DECODE,
-                        contrib: bool = False, col_blocks: int = 0) -> int:
+                        contrib: bool = False, col_blocks: int = 0, k_splits: int = 0) -> int:
     """Scratch bytes one `moe_forward` call of this size needs (to preallocate for graphs)."""
     c = _lib.MoeCall()
     c.geom = ctypes.pointer(table.geom_s)
     c.n_tokens, c.top_k, c.n_experts = n_tokens, top_k, table.n_experts
     c.contrib = 1 if contrib else None
-    c.col_blocks = int(col_blocks)
+    c.col_blocks, c.k_splits = int(col_blocks), int(k_splits)
     return int(_lib.lib().vy_moe_workspace_size(ctypes.byref(c), path))
 
 
