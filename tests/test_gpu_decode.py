@@ -400,3 +400,23 @@ def test_a_token_gets_the_same_bits_alone_and_in_a_batch():
     for t in (0, 5, 31):
         one = vb.moe_forward(x[t:t + 1], idx[t:t + 1], w[t:t + 1], table, path=vb.PATH_DECODE)
         assert torch.equal(one[0], batch[t]), f"token {t}"
+
+
+def test_new_call_fields_refuse_bad_values():
+    """k_splits must be 0, 1, 2, 4 or 8 and divide hidden / 128; shared_last needs the layer's
+    own combine and an act-dtype result."""
+    blobs, x, idx, w = _batched(1024, 512, 128, 8, 2, 4, seed=41)
+    table = pk.ExpertTable(blobs)
+    with pytest.raises(RuntimeError, match="k_splits"):
+        vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=3)
+    with pytest.raises(RuntimeError, match="k_splits"):
+        vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=16)
+    with pytest.raises(RuntimeError, match="contrib"):
+        vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, shared_last=True,
+                       contrib=torch.empty(8, 1024, device="cuda"))
+    with pytest.raises(RuntimeError, match="activation dtype"):
+        vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, shared_last=True,
+                       result=torch.empty(4, 1024, device="cuda"))
+    # hidden 1024 has 8 stages of 128: 8 splits of one stage each are accepted and exact
+    assert torch.equal(vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=8),
+                       vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=1))
