@@ -402,7 +402,9 @@ def run_ours(args, rank, world, local):
     for t in sorted({T, 1, 8}):
         batches[t] = [tuple(v.to(device) for v in make_tokens(l, wl, t, device)) for l in range(args.layers)]
     out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
-    ws = torch.empty(pk.moe_workspace_bytes(layers[0], T, K), dtype=torch.uint8, device=device)
+    # one workspace for every batch size run below (a few-token call may take split-K partials)
+    ws = torch.empty(max(pk.moe_workspace_bytes(layers[0], t, K) for t in (T, 1, 8)), dtype=torch.uint8,
+                     device=device)
     L = args.layers
 
     def step_for(t):

@@ -278,7 +278,10 @@ int vy_moe_error_flags(const vy_moe_call* call, int32_t path, int32_t* out, void
  */
 int vy_selftest_bounded_wait(int32_t arrivals, int64_t limit_ns, int32_t* flags, void* stream);
 
-/* Bytes of workspace vy_moe_decode (path 0) / vy_moe_prefill (path 1) need for `call`. */
+/* Bytes of workspace vy_moe_decode (path 0) / vy_moe_prefill (path 1) need for `call`.  For a
+ * decode call with k_splits = 0 this includes the split-K partials a few-token call may use; a
+ * workspace of at least the k_splits = 1 size is accepted too (the call then runs unsplit, with
+ * the same result), so one workspace sized for the largest batch serves every smaller one. */
 size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path);
 
 /*

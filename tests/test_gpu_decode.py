@@ -420,3 +420,14 @@ def test_new_call_fields_refuse_bad_values():
     # hidden 1024 has 8 stages of 128: 8 splits of one stage each are accepted and exact
     assert torch.equal(vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=8),
                        vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=1))
+
+
+def test_a_workspace_sized_for_a_large_batch_serves_a_one_token_call():
+    """The split-K partials of a one-token call may not fit a workspace sized for 32 tokens: the
+    call then runs unsplit, with the same bits."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 64, 8, 32, seed=43)
+    table = pk.ExpertTable(blobs)
+    ws32 = torch.empty(pk.moe_workspace_bytes(table, 32, 8), dtype=torch.uint8, device="cuda")
+    assert pk.moe_workspace_bytes(table, 1, 8) > ws32.numel()      # the split needs more here
+    got = vb.moe_forward(x[:1], idx[:1], w[:1], table, path=vb.PATH_DECODE, workspace=ws32)
+    assert torch.equal(got, vb.moe_forward(x[:1], idx[:1], w[:1], table, path=vb.PATH_DECODE))

@@ -828,13 +828,23 @@ extern "C" size_t vy_moe_workspace_size(const vy_moe_call* call, int32_t path) {
     return decode_layout(call, nullptr).bytes + 256;
 }
 
-extern "C" int vy_moe_decode(const vy_moe_call* c, void* stream) {
+extern "C" int vy_moe_decode(const vy_moe_call* call, void* stream) {
     int st;
     const DeviceInfo* dev = device_info(&st);
     if (!dev) return st;
-    if ((st = validate_call(c)) != VY_OK) return st;
-    if (c->n_tokens == 0) return ok();
+    if ((st = validate_call(call)) != VY_OK) return st;
+    if (call->n_tokens == 0) return ok();
+    const vy_moe_call* c = call;
     DecodeLayout L = decode_layout(c, nullptr);
+    vy_moe_call unsplit;
+    if (c->workspace && c->workspace_bytes < L.bytes + 256 && c->k_splits == 0 && L.k_splits > 1) {
+        // a workspace sized for a larger batch may miss the split-K partials of a few-token call:
+        // such a call runs unsplit (same result) instead of failing
+        unsplit = *c;
+        unsplit.k_splits = 1;
+        c = &unsplit;
+        L = decode_layout(c, nullptr);
+    }
     if (!c->workspace || c->workspace_bytes < L.bytes + 256)
         return fail(VY_ERR_WORKSPACE, "workspace %zu bytes, %zu needed", c->workspace_bytes, L.bytes + 256);
     char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 255) & ~uintptr_t(255));

@@ -183,6 +183,11 @@ def _make_call(geom_s, x, n_tokens, top_k, n_experts, table_ptr, ids_ptr, ids_co
 
 def _enqueue(c: _lib.MoeCall, path: int, device, workspace: "torch.Tensor | None" = None) -> None:
     need = _lib.lib().vy_moe_workspace_size(ctypes.byref(c), path)
+    if workspace is not None and workspace.numel() < need and path == PATH_DECODE and c.k_splits == 0:
+        # a workspace sized for a larger batch: a few-token call then runs without split K
+        c.k_splits = 1
+        need = _lib.lib().vy_moe_workspace_size(ctypes.byref(c), path)
+        c.k_splits = 0     # the library makes the same choice from the workspace it is given
     ws = workspace if workspace is not None else _WORKSPACE.get(device, need)
     if ws.numel() < need:
         raise RuntimeError(f"workspace of {ws.numel()} bytes, {need} needed")
