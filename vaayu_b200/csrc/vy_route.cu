@@ -224,6 +224,9 @@ __device__ void plan_small(const PlanArgs& p) {
 
 // Block 0: the plan.  Blocks >= 1: the activation permutation (x -> x_perm).
 __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
+    // launched with programmatic serialisation: the previous kernel on the stream (often the last
+    // call's combine) may still run; nothing here reads or writes before it has completed
+    grid_dependency_wait();
     if (blockIdx.x > 0) {
         // each thread permutes one 8-element group of one token's activations
         const int64_t groups_per_tok = p.hidden / 8;
@@ -501,7 +504,18 @@ int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream) {
         int64_t b = (groups + threads - 1) / threads;
         perm_blocks = static_cast<int>(b < 4 * sm_count ? b : 4 * sm_count);
     }
-    plan_kernel<<<1 + perm_blocks, threads, smem, stream>>>(p);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(1 + perm_blocks));
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, plan_kernel, p);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "routing plan launch: %s", cudaGetErrorString(e));
     return check_launch("routing plan");
 }
 
@@ -513,6 +527,7 @@ __global__ void __launch_bounds__(256) slot_combine_kernel(const float* __restri
                                                            float* out, int64_t out_stride) {
     constexpr int kBatch = 8;   // slots whose row ids, then contributions, are loaded together
     grid_dependency_wait();
+    grid_dependents_launch();   // the next call's plan may be scheduled; it waits for this grid
     for (int64_t t = blockIdx.y; t < n_tokens; t += gridDim.y)
     for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < hidden; c += gridDim.x * blockDim.x * 4) {
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -571,6 +586,7 @@ __global__ void __launch_bounds__(256) shared_combine_kernel(const float* __rest
                                                              uint16_t* result, int64_t result_stride) {
     constexpr int kBatch = 8;
     grid_dependency_wait();
+    grid_dependents_launch();
     for (int64_t t = blockIdx.y; t < n_tokens; t += gridDim.y)
     for (int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4; c < hidden; c += gridDim.x * blockDim.x * 4) {
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f), sh = make_float4(0.f, 0.f, 0.f, 0.f);
