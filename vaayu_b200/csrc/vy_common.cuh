@@ -8,6 +8,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <utility>
 
 #include "../../include/vaayu_b200.h"
 
@@ -187,6 +188,25 @@ __device__ __forceinline__ void grid_dependency_wait() {
 }
 __device__ __forceinline__ void grid_dependents_launch() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch chained to the previous kernel on the stream (programmatic stream serialisation): the
+// kernel must call grid_dependency_wait() before it touches memory.  Back-to-back launches then
+// overlap the next kernel's launch with the previous one's tail.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                           Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Row-index permutation inside each 8-element group that lines activations up with the

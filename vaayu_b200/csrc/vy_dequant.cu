@@ -279,6 +279,8 @@ template <int SC, int OUT>
 __global__ void __launch_bounds__(kThreads) fp8_dequant_fast_kernel(const uint4* __restrict__ w, uint32_t chunks,
                                                                     uint32_t cpr, const void* scale, uint32_t scols,
                                                                     uint32_t bo, uint32_t bi16, void* out) {
+    grid_dependency_wait();      // launched chained to the previous kernel on the stream
+    grid_dependents_launch();
     const uint32_t stride = gridDim.x * blockDim.x;
     for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < chunks; q += 2 * stride) {
         const uint32_t q2 = q + stride;
@@ -311,6 +313,8 @@ template <int OUT>
 __global__ void __launch_bounds__(kThreads) fp4_dequant_fast_kernel(const uint2* __restrict__ w, uint32_t chunks,
                                                                     uint32_t cpr, const uint8_t* __restrict__ scale,
                                                                     uint32_t groups, uint32_t gs16, void* out) {
+    grid_dependency_wait();      // launched chained to the previous kernel on the stream
+    grid_dependents_launch();
     const uint32_t stride = gridDim.x * blockDim.x;
     for (uint32_t q = blockIdx.x * blockDim.x + threadIdx.x; q < chunks; q += 2 * stride) {
         const uint32_t q2 = q + stride;
@@ -486,7 +490,9 @@ extern "C" int vy_fp8_dequant(const uint8_t* w, int64_t rows, int64_t cols, cons
         const uint4* w4 = reinterpret_cast<const uint4*>(w);
         const uint32_t sc32 = static_cast<uint32_t>(scols), bo32 = static_cast<uint32_t>(bo),
                        b16 = static_cast<uint32_t>(bi / 16);
-#define VY_FP8F(S, O) fp8_dequant_fast_kernel<S, O><<<fgrid, kThreads, 0, s>>>(w4, chunks, cpr, scale, sc32, bo32, b16, out)
+        cudaError_t e = cudaSuccess;
+#define VY_FP8F(S, O) e = launch_chained(fp8_dequant_fast_kernel<S, O>, dim3(fgrid), dim3(kThreads), 0, s, w4, chunks, cpr, \
+                                       scale, sc32, bo32, b16, out)
 #define VY_FP8F_OUT(S)                                                  \
     switch (out_dtype) {                                                \
         case VY_BF16: VY_FP8F(S, VY_BF16); break;                       \
@@ -502,6 +508,7 @@ extern "C" int vy_fp8_dequant(const uint8_t* w, int64_t rows, int64_t cols, cons
         }
 #undef VY_FP8F_OUT
 #undef VY_FP8F
+        if (e != cudaSuccess) return fail(VY_ERR_CUDA, "vy_fp8_dequant launch: %s", cudaGetErrorString(e));
         return check_launch("vy_fp8_dequant");
     }
 #define VY_FP8(S, O) fp8_dequant_kernel<S, O><<<grid, kThreads, 0, s>>>(w, rows, cols, scale, scols, bo, bi, out, vec)
@@ -542,11 +549,16 @@ extern "C" int vy_fp4_dequant(const uint8_t* w, int64_t rows, int64_t cols, cons
         const uint32_t groups = static_cast<uint32_t>(cols / group_size), g16 = static_cast<uint32_t>(group_size / 16);
         const int fgrid = grid_for((chunks + 1) / 2, dev->sm_count);
         const uint2* w2 = reinterpret_cast<const uint2*>(w);
+        cudaError_t e;
         switch (out_dtype) {
-            case VY_BF16: fp4_dequant_fast_kernel<VY_BF16><<<fgrid, kThreads, 0, s>>>(w2, chunks, cpr, scale, groups, g16, out); break;
-            case VY_F16: fp4_dequant_fast_kernel<VY_F16><<<fgrid, kThreads, 0, s>>>(w2, chunks, cpr, scale, groups, g16, out); break;
-            default: fp4_dequant_fast_kernel<VY_F32><<<fgrid, kThreads, 0, s>>>(w2, chunks, cpr, scale, groups, g16, out); break;
+            case VY_BF16: e = launch_chained(fp4_dequant_fast_kernel<VY_BF16>, dim3(fgrid), dim3(kThreads), 0, s, w2,
+                                             chunks, cpr, scale, groups, g16, out); break;
+            case VY_F16: e = launch_chained(fp4_dequant_fast_kernel<VY_F16>, dim3(fgrid), dim3(kThreads), 0, s, w2,
+                                            chunks, cpr, scale, groups, g16, out); break;
+            default: e = launch_chained(fp4_dequant_fast_kernel<VY_F32>, dim3(fgrid), dim3(kThreads), 0, s, w2,
+                                        chunks, cpr, scale, groups, g16, out); break;
         }
+        if (e != cudaSuccess) return fail(VY_ERR_CUDA, "vy_fp4_dequant launch: %s", cudaGetErrorString(e));
         return check_launch("vy_fp4_dequant");
     }
     switch (out_dtype) {

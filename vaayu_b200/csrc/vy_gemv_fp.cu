@@ -104,6 +104,8 @@ __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_ker
     constexpr int kStepK = 4 * kPerThread;             // K per step per row
     extern __shared__ uint4 gv_ring[];                 // [kWarps][kDepth][2][32]
     __shared__ float part[kWarps][16][NB * 8];
+    grid_dependency_wait();      // launched chained to the previous kernel on the stream
+    grid_dependents_launch();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
     uint4* my_ring = gv_ring + warp * (kDepth * 64);
@@ -238,26 +240,23 @@ __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_ker
 constexpr size_t kRingBytes = size_t(kWarps) * kDepth * 64 * sizeof(uint4);
 
 template <int KIND, int NB>
-void launch_one(unsigned grid, const GemvParams& p, cudaStream_t s) {
+cudaError_t launch_one(unsigned grid, const GemvParams& p, cudaStream_t s) {
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(fp_gemv_kernel<KIND, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kRingBytes));
         configured = true;
     }
-    fp_gemv_kernel<KIND, NB><<<grid, kWarps * 32, kRingBytes, s>>>(p);
+    return launch_chained(fp_gemv_kernel<KIND, NB>, dim3(grid), dim3(kWarps * 32), kRingBytes, s, p);
 }
 
 int launch_gemv(int kind, const GemvParams& p, cudaStream_t s) {
     const unsigned grid = static_cast<unsigned>((p.n + 15) / 16);
     const bool two = p.n_tokens > 8;
-    if (kind == 0) {
-        if (two) launch_one<0, 2>(grid, p, s);
-        else launch_one<0, 1>(grid, p, s);
-    } else {
-        if (two) launch_one<1, 2>(grid, p, s);
-        else launch_one<1, 1>(grid, p, s);
-    }
+    const cudaError_t e = kind == 0 ? (two ? launch_one<0, 2>(grid, p, s) : launch_one<0, 1>(grid, p, s))
+                                    : (two ? launch_one<1, 2>(grid, p, s) : launch_one<1, 1>(grid, p, s));
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "%s launch: %s", kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv",
+                                      cudaGetErrorString(e));
     return check_launch(kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv");
 }
 
