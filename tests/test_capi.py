@@ -51,6 +51,29 @@ def test_workspace_size_needs_no_gpu():
     assert _lib.lib().vy_moe_workspace_size(ctypes.byref(c), 0) > small > 0
 
 
+def test_the_split_k_choice_shows_in_the_workspace_size():
+    """A one-token decode call shares each gate/up unit's K range among warps (its workspace holds
+    the per-stage partials); k_splits = 1 turns that off; a 32-token call never splits."""
+    g = _lib.ExpertGeom()
+    g.hidden, g.inter, g.bits, g.group_size = 2048, 768, 4, 128
+    c = _lib.MoeCall()
+    c.geom = ctypes.pointer(g)
+    c.top_k, c.n_experts = 8, 128
+    size = lambda: _lib.lib().vy_moe_workspace_size(ctypes.byref(c), 0)
+    c.n_tokens, c.k_splits = 1, 0
+    auto1 = size()
+    c.k_splits = 1
+    plain1 = size()
+    assert auto1 > plain1 > 0
+    # the partials: (8 rows / 8 per pass + 8 live experts + 1) passes x 48 tiles of 16 rows
+    # x 16 stages of 128 K x 32 lanes x 8 floats
+    assert auto1 - plain1 >= 10 * 48 * 16 * 32 * 8 * 4
+    c.n_tokens, c.k_splits = 32, 0
+    auto32 = size()
+    c.k_splits = 1
+    assert size() == auto32
+
+
 @pytest.mark.skipif(not Path("/usr/bin/gcc").exists(), reason="gcc not available")
 def test_ctypes_structures_match_the_c_layout(tmp_path):
     src = tmp_path / "layout.c"
