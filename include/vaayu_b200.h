@@ -257,6 +257,46 @@ typedef struct vy_moe_call {
 int vy_sum_ordered(const float* parts, int32_t n_parts, int64_t n, float* out, void* stream);
 
 /*
+ * Expert-parallel dispatch plan: addresses each (token, slot) row j = t * top_k + k of this
+ * rank's batch to the rank holding its expert and packs the send buffers of fixed-capacity,
+ * equal-split all-to-alls (the exchange itself is the caller's: NCCL).  No counterpart in the
+ * reference (it is single-GPU).
+ *   ids [n_tokens, ids_row_stride]   GLOBAL expert ids (int32 / int64); an id outside
+ *                                    [0, n_ranks * experts_per_rank) is dropped
+ *   placement                        0: expert e on rank e / experts_per_rank as local expert
+ *                                    e % experts_per_rank; 1 (interleaved): rank e % n_ranks,
+ *                                    local e / n_ranks
+ *   weights                          routing weights, element (t, k) at t * w_tok_stride +
+ *                                    k * w_slot_stride (bf16 / fp16 / fp32)
+ *   x [n_tokens, x_row_stride]       activations (bf16 / fp16), hidden columns used
+ *   capacity                         slots per destination; n_tokens * top_k takes any routing
+ * Row j takes slot dest * capacity + pos, pos its rank among the rows bound for dest, in row
+ * order; a row past a full destination is dropped.  Outputs (device memory):
+ *   send_ids [n_ranks * capacity]    int32 local expert id; -1 for an empty slot
+ *   send_w   [n_ranks * capacity]    fp32 routing weight
+ *   send_x   [n_ranks * capacity, hidden] the token's activations (empty slots unwritten)
+ *   slot_of_row [n_tokens * top_k]   int64 slot, -1 for a dropped row
+ *   counts   [n_ranks]               int32 rows taken per destination
+ */
+int vy_ep_dispatch_plan(const void* ids, int32_t ids_dtype, int64_t ids_row_stride, int64_t n_tokens,
+                        int32_t top_k, int32_t n_ranks, int32_t experts_per_rank, int32_t placement,
+                        const void* weights, int32_t w_dtype, int64_t w_tok_stride, int64_t w_slot_stride,
+                        const void* x, int32_t x_dtype, int64_t x_row_stride, int64_t hidden,
+                        int64_t capacity, int32_t* send_ids, float* send_w, void* send_x,
+                        int64_t* slot_of_row, int32_t* counts, void* stream);
+
+/*
+ * Expert-parallel combine on the tokens' home rank: out[t] = sum over token t's slots, in
+ * ascending GLOBAL expert id then slot (fp32), of back[slot_of_row[t * top_k + k]] -- the
+ * contributions returned by the reverse all-to-all, read in place through the dispatch plan's
+ * slot map (-1: none).  The order `accumulate_expert_outputs` (vaayu/moe_patch.py:914-940)
+ * sums in, so the result equals one GPU's layer bit for bit.  n_tokens <= 65535.
+ */
+int vy_ep_combine(const float* back, const int64_t* slot_of_row, const void* expert_ids, int32_t ids_dtype,
+                  int64_t n_tokens, int32_t top_k, int64_t hidden, float* out, int64_t out_row_stride,
+                  void* stream);
+
+/*
  * Error flags of the last vy_moe_decode (path 0) / vy_moe_prefill (path 1) call made with this
  * call structure and workspace, copied (enqueued on `stream`) to `out` (device or host int32):
  *   VY_FLAG_BAD_EXPERT  a routed expert's streams were unusable (null or misaligned pointer);

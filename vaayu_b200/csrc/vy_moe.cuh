@@ -58,9 +58,11 @@ int launch_slot_combine(const float* contrib, const int32_t* slot_order, int64_t
 // A layer call's final combine: launch_slot_combine, or with c->shared_last the shared-expert
 // epilogue into c->result (and the routed sum into c->out when given).
 int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32_t* slot_order, cudaStream_t s);
+// out[t] = sum over token t's slots, ascending expert id then slot, of contribution row
+// t * top_k + k -- or rows[t * top_k + k] when `rows` is given (-1: no contribution).
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
-                   cudaStream_t stream);
+                   cudaStream_t stream, const int64_t* rows = nullptr);
 
 // Shared validation of a vy_moe_call (decode and prefill entry points).
 int validate_call(const vy_moe_call* c);

@@ -437,7 +437,7 @@ __global__ void topk_softmax_kernel(const void* logits, int64_t row_stride, int6
 // out[t] = sum of contrib rows of token t in slot_order (ascending expert id, then slot).
 __global__ void combine_kernel(const float* __restrict__ contrib, const void* ids, bool ids64,
                                int64_t n_tokens, int top_k, int64_t hidden, float* out,
-                               int64_t out_stride) {
+                               int64_t out_stride, const int64_t* __restrict__ rows) {
     const int64_t t = blockIdx.y;
     int idx[kMaxTopK];
     int key[kMaxTopK];
@@ -459,8 +459,12 @@ __global__ void combine_kernel(const float* __restrict__ contrib, const void* id
     for (int64_t c = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; c < hidden;
          c += int64_t(gridDim.x) * blockDim.x) {
         float acc = 0.f;
-        for (int k = 0; k < top_k; ++k)
-            if (key[k] != INT32_MAX) acc += contrib[(t * top_k + idx[k]) * hidden + c];
+        for (int k = 0; k < top_k; ++k) {
+            if (key[k] == INT32_MAX) continue;
+            // the slot's contribution row: its own position, or where `rows` says it landed
+            const int64_t r = rows ? rows[t * top_k + idx[k]] : t * top_k + idx[k];
+            if (r >= 0) acc += contrib[r * hidden + c];
+        }
         out[t * out_stride + c] = acc;
     }
 }
@@ -661,13 +665,13 @@ int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32
 
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, const int64_t* rows) {
     if (n_tokens == 0) return VY_OK;
     int bx = static_cast<int>((hidden + 255) / 256);
     if (bx > 8) bx = 8;
     (void)sm_count;
     dim3 grid(bx, static_cast<unsigned>(n_tokens));
-    combine_kernel<<<grid, 256, 0, stream>>>(contrib, ids, ids64, n_tokens, top_k, hidden, out, out_stride);
+    combine_kernel<<<grid, 256, 0, stream>>>(contrib, ids, ids64, n_tokens, top_k, hidden, out, out_stride, rows);
     return check_launch("combine");
 }
 

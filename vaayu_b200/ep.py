@@ -127,6 +127,8 @@ class ExpertParallelLayer:
                      recv_w=torch.empty(P * cap, dtype=torch.float32, device=dev),
                      contrib=torch.empty(P * cap, H, dtype=torch.float32, device=dev),
                      back=torch.empty(P * cap, H, dtype=torch.float32, device=dev),
+                     slot=torch.empty(T * K, dtype=torch.int64, device=dev),
+                     counts=torch.empty(P, dtype=torch.int32, device=dev),
                      tok=torch.arange(T * K, device=dev) // K,
                      ranks=torch.arange(P, device=dev).view(1, P))
             self._bufs[key] = b
@@ -140,7 +142,43 @@ class ExpertParallelLayer:
         T, K = ids.shape
         P = self.world
         b = self._dispatch_buffers(T, K, x, weights)
-        cap = b["cap"]
+        if x.is_cuda:
+            self._plan_on_device(x, ids, weights, b)
+        else:
+            self._plan_on_host(x, ids, weights, b)
+        self._a2a(b["recv_id"], b["send_id"], None, None)
+        self._a2a(b["recv_w"], b["send_w"], None, None)
+        self._a2a(b["recv_x"], b["send_x"], None, None)
+        recv_w = b["recv_w"].view(-1, 1)
+        if weights.dtype != torch.float32:
+            # the exchange carries fp32; the routing weight keeps its own dtype for the rounding rule
+            recv_w = recv_w.to(weights.dtype)
+        return b["recv_x"], b["recv_id"].view(-1, 1), recv_w, (b["slot"], b)
+
+    def _plan_on_device(self, x, ids, weights, b):
+        """The send buffers and slot map from the library's dispatch-plan kernels (one planning
+        CTA, one packing grid), on the current stream."""
+        from . import _lib
+        T, K = ids.shape
+        weights = weights.reshape(T, K)
+        if ids.stride(1) != 1:
+            ids = ids.contiguous()
+        if x.stride(1) != 1:
+            x = x.contiguous()
+        ids_code, w_code, x_code = (_lib.DTYPE_CODE[t.dtype] for t in (ids, weights, x))
+        with torch.cuda.device(x.device):
+            _lib.check(_lib.lib().vy_ep_dispatch_plan(
+                ids.data_ptr(), ids_code, ids.stride(0), T, K, self.world, self.per_rank,
+                1 if self.interleaved else 0, weights.data_ptr(), w_code, weights.stride(0), weights.stride(1),
+                x.data_ptr(), x_code, x.stride(0), x.shape[1], b["cap"], b["send_id"].data_ptr(),
+                b["send_w"].data_ptr(), b["send_x"].data_ptr(), b["slot"].data_ptr(), b["counts"].data_ptr(),
+                _lib.stream_of(x.device)), "vy_ep_dispatch_plan")
+
+    def _plan_on_host(self, x, ids, weights, b):
+        """The same send buffers and slot map from torch operations, for CPU tensors (the
+        process-group logic's tests); every id must name one of the layer's experts."""
+        T, K = ids.shape
+        P, cap = self.world, b["cap"]
         flat = ids.reshape(-1).to(torch.int64)
         if self.interleaved:       # expert e lives on rank e % P as local expert e // P
             dest = torch.remainder(flat, P)
@@ -152,18 +190,11 @@ class ExpertParallelLayer:
         hit = (dest.view(-1, 1) == b["ranks"]).to(torch.int32)
         pos = hit.cumsum(0).gather(1, dest.view(-1, 1)).view(-1) - 1
         slot = dest * cap + pos
+        b["slot"].copy_(slot)
         b["send_id"].fill_(-1)
         b["send_id"].index_copy_(0, slot, local.to(torch.int32))
         b["send_w"].index_copy_(0, slot, weights.reshape(-1).to(torch.float32))
         b["send_x"].index_copy_(0, slot, x.index_select(0, b["tok"]))
-        self._a2a(b["recv_id"], b["send_id"], None, None)
-        self._a2a(b["recv_w"], b["send_w"], None, None)
-        self._a2a(b["recv_x"], b["send_x"], None, None)
-        recv_w = b["recv_w"].view(-1, 1)
-        if weights.dtype != torch.float32:
-            # the exchange carries fp32; the routing weight keeps its own dtype for the rounding rule
-            recv_w = recv_w.to(weights.dtype)
-        return b["recv_x"], b["recv_id"].view(-1, 1), recv_w, (slot, b)
 
     def compute(self, recv_x, recv_ids, recv_w, plan=None):
         """Contributions [P * cap, H] fp32 of the received rows (slots with id -1 stay unwritten:
@@ -182,10 +213,14 @@ class ExpertParallelLayer:
         return contrib
 
     def gather_back(self, contrib, plan):
-        """This rank's rows' contributions back from their experts' ranks, in (token, slot) order."""
+        """This rank's rows' contributions back from their experts' ranks, in (token, slot) order
+        (zeros for a row the dispatch dropped)."""
         slot, b = plan
         self._a2a(b["back"], contrib, None, None)
-        return b["back"].index_select(0, slot)
+        rows = b["back"].index_select(0, slot.clamp(min=0))
+        if slot.is_cuda:
+            rows.masked_fill_((slot < 0).view(-1, 1), 0.0)
+        return rows
 
     # ── replicate mode ───────────────────────────────────────────────────────────────────
     def _buffers(self, T, K, x, weights):
@@ -271,6 +306,21 @@ class ExpertParallelLayer:
             return self.replicate_forward(x, ids, weights, out)
         recv_x, recv_ids, recv_w, plan = self.dispatch(x, ids, weights)
         contrib = self.compute(recv_x, recv_ids, recv_w, plan)
+        if self._combine is None and contrib.is_cuda:
+            # the returned contributions summed in place through the slot map, ascending global
+            # expert id then slot (no gathered copy)
+            slot, b = plan
+            self._a2a(b["back"], contrib, None, None)
+            T, K = ids.shape
+            if out is None:
+                out = torch.empty(T, self.hidden, dtype=torch.float32, device=contrib.device)
+            from . import _lib
+            ids_c = ids.contiguous()
+            with torch.cuda.device(contrib.device):
+                _lib.check(_lib.lib().vy_ep_combine(
+                    b["back"].data_ptr(), slot.data_ptr(), ids_c.data_ptr(), _lib.DTYPE_CODE[ids_c.dtype], T, K,
+                    self.hidden, out.data_ptr(), out.stride(0), _lib.stream_of(contrib.device)), "vy_ep_combine")
+            return out
         rows = self.gather_back(contrib, plan)
         if self._combine is not None:
             res = self._combine(rows, ids)
