@@ -192,3 +192,35 @@ def test_a_rank_that_never_joins_makes_the_others_raise_not_hang(tmp_path):
     raised, seconds = np.load(tmp_path / "dropped.npy")
     assert raised == 1.0, "the exchange with a missing rank must raise"
     assert seconds < 30
+
+
+# ── the dispatch plan itself (one process, no exchange) ───────────────────────────────────────
+
+@pytest.mark.parametrize("placement", ["contiguous", "interleaved"])
+def test_the_dispatch_plan_files_rows_stably_by_destination(placement):
+    """Every (token, slot) row lands in its expert's rank's slot range, ranked among that rank's
+    rows in row order; empty slots carry id -1.  (The library's device plan is held to this same
+    plan bit for bit in test_gpu_ep_plan.py.)"""
+    from vaayu_b200.ep import ExpertParallelLayer
+    n_exp, ranks, tokens, k, hid = 12, 3, 10, 4, 8
+    layer = ExpertParallelLayer(None, n_exp, compute=lambda *a: None, hidden=hid, mode="dispatch",
+                                placement=placement)
+    layer.world, layer.per_rank = ranks, n_exp // ranks
+    g = torch.Generator().manual_seed(5)
+    ids = torch.stack([torch.randperm(n_exp, generator=g)[:k] for _ in range(tokens)])
+    w = torch.rand(tokens, k, generator=g)
+    x = torch.randn(tokens, hid, generator=g).to(torch.bfloat16)
+    b = layer._dispatch_buffers(tokens, k, x, w)
+    layer._plan_on_host(x, ids, w, b)
+    cap = b["cap"]
+    nxt = [0] * ranks
+    for j, e in enumerate(ids.reshape(-1).tolist()):
+        d, local = (e % ranks, e // ranks) if placement == "interleaved" else (e // (n_exp // ranks), e % (n_exp // ranks))
+        slot = d * cap + nxt[d]
+        nxt[d] += 1
+        assert b["slot"][j] == slot
+        assert b["send_id"][slot] == local
+        assert b["send_w"][slot] == w.reshape(-1)[j]
+        assert torch.equal(b["send_x"][slot], x[j // k])
+    for d in range(ranks):
+        assert (b["send_id"][d * cap + nxt[d]:(d + 1) * cap] == -1).all()
