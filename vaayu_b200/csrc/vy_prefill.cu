@@ -1,27 +1,36 @@
 // vy_prefill.cu -- the prefill expert layer as tcgen05 grouped GEMMs (accumulators in TMEM).
 //
-//   plan (vy_route.cu)   rows grouped by expert; the pass table holds one entry per 256-row unit
+//   plan (vy_route.cu)   rows grouped by expert; the pass table holds one entry per 128-row unit
 //                        of a live expert (stream pointers, first sorted row, row count)
 //   gather_kernel        x rows in sorted order -> x_sorted, 8-element groups permuted the way the
 //                        dequantised pairs come out (code j pairs with code j + 4), so A and B
 //                        share one consistent K order
-//   gemm_kernel<0>       h = act(act(silu(act(x Wg^T))) * act(x Wu^T)), 256 rows x 128 columns
-//   gemm_kernel<1>       c = act(h Wd^T) * w (one fp32 rounding), 256 rows x 256 columns,
+//   gemm_kernel<0>       h = act(act(silu(act(x Wg^T))) * act(x Wu^T)), 128 rows x 128 columns
+//                        (128 gate + 128 up weight rows per CTA)
+//   gemm_kernel<1>       c = act(h Wd^T) * w (one fp32 rounding), 128 rows x 256 columns,
 //                        scattered to the row ids
 //   slot_combine_kernel  each token's contributions in ascending expert id, then slot
 //
-// A GEMM CTA: 16 dequant warps + 1 control warp.  Each dequant thread owns one K half of one
-// row of the 256-row weight tile (32 codes per stage): it copies those packed codes into a private
-// cp.async ring (the row's scale and zero words stream through registers, a word ahead),
-// dequantises them (the reference's exact rounding of every weight: sub.rn then mul.rn on
-// activation-dtype pairs) and stores the 16-byte chunks into the weight tile in the
-// 128-byte-swizzled K-major layout the tensor core reads; then each warp arrives once on the
-// stage's barrier.  The control thread loads the 256-row activation tile with one TMA box (same
-// swizzle, no multicast; three tiles in flight) and issues tcgen05.mma M=128 N=256 K=16 for each
-// of the two 128-row halves into its own 256 TMEM columns, so every dequantised weight tile feeds
-// 256 rows; tcgen05.commit frees the stages.  The dequant warps then read TMEM with tcgen05.ld for
-// the epilogue.  Every barrier wait is bounded: on a timeout the CTA records an error flag, drains
-// what it issued, frees TMEM and returns.
+// A GEMM CTA: 8 dequant warps, 16 fold warps, one control warp group (one thread of it works);
+// `setmaxnreg` gives the fold warps the registers the other roles do not need.
+//   dequant  one thread per row of the 256-row weight tile (64 codes per stage): it copies the
+//            row's packed codes into a private cp.async ring (the row's scale and zero words
+//            stream through registers, a word ahead), dequantises them with the reference's exact
+//            rounding of every weight (sub.rn then mul.rn on activation-dtype pairs) and stores
+//            16-byte chunks into the weight tile in the 128-byte-swizzled K-major layout the
+//            tensor core reads; each warp then arrives once on the stage's barrier.
+//   control  loads the 128-row activation tile with one TMA box (same swizzle, no multicast) and
+//            issues tcgen05.mma M=128 N=256 K=16.
+//   fold     K is cut into chunks of kChunk stages.  Each chunk accumulates from zero in one of
+//            two TMEM buffers (2 x 256 columns); the fold warps read it with tcgen05.ld and add it
+//            into fp32 sums held in their registers with round-to-nearest adds (paired fp32 adds),
+//            while the tensor core fills the other buffer.  The tensor core's own accumulate
+//            truncates against the accumulator's magnitude, so one chain over the whole K drifts
+//            (biased) from the fp32 sum; short chunks keep every output as close to the correctly
+//            rounded dot product as the decode path's.  The fold warps then run the epilogue from
+//            their registers.
+// Every barrier wait is bounded: on a timeout the CTA records an error flag, drains what it
+// issued, frees TMEM and returns.
 #include <cuda.h>
 
 #include <mutex>
@@ -32,17 +41,41 @@ namespace vy {
 namespace {
 
 constexpr int kBM = 128, kBK = 64;    // one MMA: 128 rows, K = 64 per stage
-constexpr int kUnit = 2 * kBM;        // rows per CTA: two 128-row halves share the weight tile
-constexpr int kBlk = 128;             // rows of one weight block
-constexpr int kBN = 2 * kBlk;         // a CTA's N: two weight blocks (gate + up, or 256 down rows)
-constexpr int kAStages = 4;           // activation-tile ring (TMA): three tiles in flight
-constexpr int kBStages = 2;           // weight-tile ring (dequant warps)
-constexpr int kPack = 4;              // packed-code staging depth, private to each dequant thread
-constexpr int kDqThreads = 4 * kBlk;  // two per weight-tile row: K halves of each stage
-constexpr int kThreads = kDqThreads + 32;
-constexpr uint32_t kTmemCols = 2 * kBN;       // one N = 256 accumulator per 128-row half
+constexpr int kUnit = kBM;            // activation rows per CTA
+constexpr int kBN = 256;              // a CTA's N: 128 gate + 128 up rows, or 256 down rows
+constexpr int kGuCols = kBN / 2;      // intermediate columns of one gate/up CTA
+#ifndef VY_PF_ASTAGES
+#define VY_PF_ASTAGES 6
+#endif
+#ifndef VY_PF_BSTAGES
+#define VY_PF_BSTAGES 3
+#endif
+#ifndef VY_PF_PACK
+#define VY_PF_PACK 4
+#endif
+#ifndef VY_PF_CHUNK
+#define VY_PF_CHUNK 2
+#endif
+constexpr int kAStages = VY_PF_ASTAGES;   // activation-tile ring (TMA)
+constexpr int kBStages = VY_PF_BSTAGES;   // weight-tile ring (dequant warps)
+constexpr int kPack = VY_PF_PACK;         // packed-code staging depth, private to each dequant thread
+constexpr int kChunk = VY_PF_CHUNK;       // stages one TMEM accumulation runs before it is folded
+constexpr int kDqWarps = 8;           // one dequant thread per weight-tile row
+constexpr int kDqThreads = kDqWarps * 32;
+constexpr int kFoldWarps = 16;        // 4 lane quarters x 4 column quarters
+constexpr int kCtlWarp = kDqWarps + kFoldWarps;   // first warp of the control warp group
+constexpr int kThreads = (kCtlWarp + 4) * 32;     // 28 warps: 7 warp groups
+// Registers per thread after `setmaxnreg` (warp-group granular).  The launch gives every thread
+// the same count; the kernel only runs when that launch budget covers this split (host check).
+constexpr int kDqRegs = 56, kFoldRegs = 88, kCtlRegs = 40;
+constexpr int kRegSplit = (kDqWarps * kDqRegs + kFoldWarps * kFoldRegs + 4 * kCtlRegs) * 32;
+static_assert(kDqWarps % 4 == 0 && kFoldWarps % 4 == 0 && kCtlWarp % 4 == 0, "roles are whole warp groups");
+static_assert(kDqThreads == kBN, "one dequant thread per weight-tile row");
+constexpr uint32_t kBufCols = kBN;            // one accumulator buffer: 128 lanes x N = 256
+constexpr uint32_t kTmemCols = 2 * kBufCols;  // double-buffered: 512 columns
+constexpr int kFoldVals = kBN / 4;            // fp32 sums one fold thread holds (its row, 64 columns)
 constexpr uint64_t kWaitNs = 2000000000ull;   // a barrier wait gives up after 2 s
-constexpr int kTileBytes = kUnit * kBK * 2;   // 32 KB: one 256 x 64 activation tile
+constexpr int kTileBytes = kUnit * kBK * 2;   // 16 KB: one 128 x 64 activation tile
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -69,6 +102,19 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// The same test, but a thread whose phase is not complete yet may be suspended (woken when it
+// completes) for up to `hint_ns` instead of returning at once: waiting warps then take no issue
+// slots from the working ones.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+constexpr uint32_t kSuspendNs = 100000;   // a waiting thread rechecks abort / timeout every 0.1 ms
 __device__ __forceinline__ uint64_t now_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -82,7 +128,7 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, vo
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = now_ns();
     for (;;) {
-        if (mbar_try(bar, parity)) return true;
+        if (mbar_try_sleep(bar, parity, kSuspendNs)) return true;
         if (*abort_flag) return false;
         if (now_ns() - t0 > limit_ns) {
             *abort_flag = 1;
@@ -102,7 +148,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int32_t* err) {
     const uint64_t t0 = now_ns();
     for (;;) {
-        if (mbar_try(bar, parity)) return true;
+        if (mbar_try_sleep(bar, parity, kSuspendNs)) return true;
         if (now_ns() - t0 > kWaitNs) {
             atomicOr(err, 8);
             return false;
@@ -175,13 +221,28 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Two fp32 round-to-nearest adds in one instruction (each half of the pair rounds on its own,
+// exactly as two separate adds do).
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t pack_f32x2(uint32_t lo, uint32_t hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+    return d;
+}
+__device__ __forceinline__ float2 unpack_f32x2(uint64_t v) {
+    uint32_t lo, hi;
+    asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+    return make_float2(__uint_as_float(lo), __uint_as_float(hi));
 }
 
 // K-major, 128-byte swizzle, 64 bf16 per row, rows 128 bytes apart, 8-row groups 1024 bytes
@@ -256,10 +317,11 @@ struct GemmParams {
 };
 
 struct __align__(1024) GemmSmem {
-    uint16_t a[kAStages][kUnit * kBK];         // activation tiles (TMA, swizzled): rows 0-255
-    uint16_t b[kBStages][kBN * kBK];           // weight tiles: rows 0-127 block 0, 128-255 block 1
-    uint4 pack[kPack][kDqThreads];             // packed codes, private per thread
-    uint64_t full_a[kAStages], empty_a[kAStages], full_b[kBStages], empty_b[kBStages], done;
+    uint16_t a[kAStages][kUnit * kBK];         // activation tiles (TMA, swizzled): rows 0-127
+    uint16_t b[kBStages][kBN * kBK];           // weight tiles: KIND 0 rows 0-127 gate, 128-255 up
+    uint4 pack[kPack][2][kDqThreads];          // packed codes (2 chunks of a row), private per thread
+    uint64_t full_a[kAStages], empty_a[kAStages], full_b[kBStages], empty_b[kBStages];
+    uint64_t chunk_full[2], chunk_free[2], done;
     uint32_t tmem_base;
     int abort_flag;
 };
@@ -282,9 +344,10 @@ __device__ __forceinline__ uint32_t scale_bits(uint2 v, int sub) {
     }
 }
 
-// KIND 0: gate and up blocks of the same 128 intermediate rows; the epilogue writes
+// KIND 0: 128 gate and the same 128 up rows of the intermediate; the epilogue writes
 //         h = act(act(silu(g)) * u).
-// KIND 1: two 128-row blocks of down; the epilogue writes contributions act(y) * w by row id.
+// KIND 1: 256 rows of down (128 when hidden ends on an odd 128-block); the epilogue writes
+//         contributions act(y) * w by row id.
 template <int ACT, int SC, bool ZERO, int KIND>
 __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, GemmParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -296,9 +359,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     const int n_tiles = n_live > 0 ? p.unit_start[n_live] : 0;
     if (static_cast<int>(blockIdx.x) >= n_tiles) return;     // uniform: before any barrier
     const PassEntry pe = p.passes[blockIdx.x];
-    const int nbase = blockIdx.y * (KIND == 0 ? kBlk : kBN);
+    const int nbase = blockIdx.y * (KIND == 0 ? kGuCols : kBN);
     const int nk = p.kdim / kBK;
-    const bool two = pe.ncols > kBM;                         // second 128-row half has rows
+    const int n_chunks = (nk + kChunk - 1) / kChunk;
 
     if (tid == 0) {
         for (int i = 0; i < kAStages; ++i) {
@@ -306,8 +369,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             mbar_init(&S.empty_a[i], 1);
         }
         for (int i = 0; i < kBStages; ++i) {
-            mbar_init(&S.full_b[i], kDqThreads / 32);   // one arrive per dequant warp
+            mbar_init(&S.full_b[i], kDqWarps);      // one arrive per dequant warp
             mbar_init(&S.empty_b[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&S.chunk_full[i], 1);
+            mbar_init(&S.chunk_free[i], kFoldWarps);   // one arrive per fold warp
         }
         mbar_init(&S.done, 1);
         S.abort_flag = 0;
@@ -325,17 +392,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                          (!ZERO || (pe.zp != 0 && (pe.zp & 7) == 0));
     if (!ok_ptrs && tid == 0) atomicOr(err, 1);
 
-    if (tid < kDqThreads) {
-        // ── dequant producer: tile row r = tid % 256, K half hh = tid / 256 of every stage
-        // (words 4 hh .. 4 hh + 3 of the stage's 8: 32 codes, inside one scale group) ────────
-        const int r = tid & (kBN - 1), hh = tid >> 8;
-        const int blk = r >> 7;
-        const int m = KIND == 0 ? blk : 0;
-        const int row = KIND == 0 ? nbase + (r & (kBlk - 1)) : nbase + r;
+    if (warp < kDqWarps) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kDqRegs));
+        // ── dequant producer: weight-tile row r = tid (KIND 0: rows 0-127 gate, 128-255 up of
+        // intermediate rows nbase ..), all 64 codes of every stage (8 words; the two 32-code
+        // halves may sit in different scale groups when the group is 32) ────────────────────
+        const int r = tid;
+        const int m = KIND == 0 ? (r >= kGuCols) : 0;
+        const int row = KIND == 0 ? nbase + (r & (kGuCols - 1)) : nbase + r;
         const bool go = ok_ptrs && row < p.ndim;
         const uint32_t groups = static_cast<uint32_t>(p.kdim) >> p.gs_shift;
-        const int32_t* src = reinterpret_cast<const int32_t*>(pe.pk) + p.w_off[m] +
-                             int64_t(row) * (p.kdim / 8) + hh * 4;
+        const int32_t* src = reinterpret_cast<const int32_t*>(pe.pk) + p.w_off[m] + int64_t(row) * (p.kdim / 8);
         const uint32_t sidx0 = static_cast<uint32_t>(p.s_off[m]) + static_cast<uint32_t>(row) * groups;
         const uint32_t zidx0 = static_cast<uint32_t>(p.z_off[m]) + static_cast<uint32_t>(row >> 3) * groups;
         constexpr int kScLog = SC == VY_F32 ? 1 : 2;      // scale elements per 8-byte word: 2 or 4
@@ -343,175 +410,199 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
         const int nib = 4 * (row & 7);
         WordStream<kScLog> scw;
         WordStream<1> zpw;
-        scw.start(reinterpret_cast<const void*>(pe.sc), sidx0 + (static_cast<uint32_t>(hh * 32) >> gs_shift),
-                  sidx0 + groups - 1, go);
-        if constexpr (ZERO)
-            zpw.start(reinterpret_cast<const void*>(pe.zp), zidx0 + (static_cast<uint32_t>(hh * 32) >> gs_shift),
-                      zidx0 + groups - 1, go);
-        // chunk c = 4 hh + i of tile row r sits at r * 128 + ((c ^ (r & 7)) << 4)
-        uint32_t off[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) off[i] = r * 128 + (((4 * hh + i) ^ (r & 7)) << 4);
-        unsigned char* b_base = reinterpret_cast<unsigned char*>(S.b[0]);
+        scw.start(reinterpret_cast<const void*>(pe.sc), sidx0, sidx0 + groups - 1, go);
+        if constexpr (ZERO) zpw.start(reinterpret_cast<const void*>(pe.zp), zidx0, zidx0 + groups - 1, go);
+        // chunk c of tile row r sits at r * 128 + ((c ^ (r & 7)) << 4)
+        const uint32_t sw = r & 7;
+        unsigned char* b_base = reinterpret_cast<unsigned char*>(S.b[0]) + r * 128;
         auto issue = [&](int s) {
-            if (s < nk && go) cp_async16(&S.pack[s % kPack][tid], src + s * 8);
+            if (s < nk && go) {
+                cp_async16(&S.pack[s % kPack][0][tid], src + s * 8);
+                cp_async16(&S.pack[s % kPack][1][tid], src + s * 8 + 4);
+            }
             cp_async_commit();
         };
 #pragma unroll
         for (int s = 0; s < kPack - 1; ++s) issue(s);
         for (int s = 0; s < nk; ++s) {
             issue(s + kPack - 1);
-            const uint32_t grp = static_cast<uint32_t>(s * kBK + hh * 32) >> gs_shift;
-            const uint2 sw = scw.at(sidx0 + grp, go);
-            uint2 zw = make_uint2(0u, 0u);
-            if constexpr (ZERO) zw = zpw.at(zidx0 + grp, go);
+            uint32_t sp[2], bp[2];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                const uint32_t grp = static_cast<uint32_t>(s * kBK + hh * 32) >> gs_shift;
+                const uint2 sw2 = scw.at(sidx0 + grp, go);
+                sp[hh] = __byte_perm(scale_bits<ACT, SC>(sw2, (sidx0 + grp) & ((1u << kScLog) - 1)), 0, 0x1010);
+                bp[hh] = int4_bias_pair<ACT>(8u);
+                if constexpr (ZERO) {
+                    const uint2 zw = zpw.at(zidx0 + grp, go);
+                    bp[hh] = int4_bias_pair<ACT>(((((zidx0 + grp) & 1) ? zw.y : zw.x) >> nib) & 15u);
+                }
+            }
             cp_async_wait<kPack - 1>();
-            const int slot = s & (kBStages - 1);
+            const int slot = s % kBStages;
             // warp-uniform decision: a lane that left the loop alone would strand the warp's arrive
             if (s >= kBStages &&
                 !__all_sync(0xffffffffu, mbar_wait(&S.empty_b[slot], ((s / kBStages) - 1) & 1, abort_flag, err)))
                 break;
             const int ps = s % kPack;
-            const uint4 wv = S.pack[ps][tid];
-            const uint32_t sp = __byte_perm(scale_bits<ACT, SC>(sw, (sidx0 + grp) & ((1u << kScLog) - 1)), 0, 0x1010);
-            uint32_t bp = int4_bias_pair<ACT>(8u);
-            if constexpr (ZERO) bp = int4_bias_pair<ACT>(((((zidx0 + grp) & 1) ? zw.y : zw.x) >> nib) & 15u);
-            const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+            const uint4 w0 = S.pack[ps][0][tid], w1 = S.pack[ps][1][tid];
+            const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
             unsigned char* dst = b_base + slot * (kBN * kBK * 2);
 #pragma unroll
-            for (int w = 0; w < 4; ++w) {
+            for (int w = 0; w < 8; ++w) {
+                const uint32_t bw = bp[w >> 2], spw = sp[w >> 2];
                 uint4 o;
-                o.x = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 0), bp), sp);
-                o.y = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 1), bp), sp);
-                o.z = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 2), bp), sp);
-                o.w = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 3), bp), sp);
-                *reinterpret_cast<uint4*>(dst + off[w]) = o;
+                o.x = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 0), bw), spw);
+                o.y = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 1), bw), spw);
+                o.z = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 2), bw), spw);
+                o.w = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(words[w], 3), bw), spw);
+                *reinterpret_cast<uint4*>(dst + ((w ^ sw) << 4)) = o;
             }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.full_b[slot]);
         }
         cp_async_wait<0>();
-    } else if (warp == kDqThreads / 32 && lane == 0) {
-        // ── control: activation tiles by TMA, tcgen05.mma (N = 256), commits ───────────────
-        constexpr uint32_t idesc = idesc_f16<ACT>();
-        int loaded = 0, landed = 0;   // activation tiles issued / seen complete
-        for (; loaded < kAStages - 1 && loaded < nk; ++loaded) {
-            mbar_expect_tx(&S.full_a[loaded], kTileBytes);
-            tma_load_2d(S.a[loaded], &tmap_a, loaded * kBK, pe.row0, &S.full_a[loaded]);
-        }
-        for (int s = 0; s < nk; ++s) {
-            const int sa = s % kAStages, sb = s % kBStages;
-            if (!mbar_wait(&S.full_a[sa], (s / kAStages) & 1, abort_flag, err)) break;
-            landed = s + 1;
-            if (!mbar_wait(&S.full_b[sb], (s / kBStages) & 1, abort_flag, err)) break;
-            tc_fence_after();
-            const uint64_t ad = sw128_desc(S.a[sa]), bd = sw128_desc(S.b[sb]);
-            // second half: activation rows 128-255 start 128 rows x 128 bytes further on
-            constexpr uint64_t kHalf = (kBM * 128) >> 4;
-#pragma unroll
-            for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
-                umma(tmem, ad + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
-            if (two) {
-#pragma unroll
-                for (int j = 0; j < kBK / 16; ++j)
-                    umma(tmem + kBN, ad + kHalf + 2 * j, bd + 2 * j, idesc, (s > 0 || j > 0) ? 1u : 0u);
+    } else if (warp >= kCtlWarp) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtlRegs));
+        if (warp == kCtlWarp && lane == 0) {
+            // ── control: activation tiles by TMA, tcgen05.mma (M = 128, N = 256), commits ────
+            constexpr uint32_t idesc = idesc_f16<ACT>();
+            // kAhead tiles in flight: the tile issued after MMA s refills the slot MMA s - 2 read,
+            // which has completed by then (waiting for MMA s - 1 instead would put the commit ->
+            // barrier -> wake-up latency into every stage)
+            constexpr int kAhead = kAStages - 2;
+            int loaded = 0, landed = 0;   // activation tiles issued / seen complete
+            for (; loaded < kAhead && loaded < nk; ++loaded) {
+                mbar_expect_tx(&S.full_a[loaded], kTileBytes);
+                tma_load_2d(S.a[loaded], &tmap_a, loaded * kBK, pe.row0, &S.full_a[loaded]);
             }
-            umma_commit(&S.empty_a[sa]);
-            umma_commit(&S.empty_b[sb]);
-            // the next activation tile goes into the slot MMA s-1 read: wait for it only now,
-            // with MMA s already queued behind it
-            const int t = s + kAStages - 1;
-            if (t < nk) {
-                const int ts = t % kAStages;
-                if (t >= kAStages && !mbar_wait(&S.empty_a[ts], ((t / kAStages) - 1) & 1, abort_flag, err)) break;
-                mbar_expect_tx(&S.full_a[ts], kTileBytes);
-                tma_load_2d(S.a[ts], &tmap_a, t * kBK, pe.row0, &S.full_a[ts]);
-                loaded = t + 1;
+            for (int s = 0; s < nk; ++s) {
+                const int sa = s % kAStages, sb = s % kBStages;
+                const int c = s / kChunk, buf = c & 1, in_chunk = s - c * kChunk;
+                // a chunk's buffer is free once the fold warps have read the chunk two before it
+                if (in_chunk == 0 && c >= 2 &&
+                    !mbar_wait(&S.chunk_free[buf], ((c >> 1) - 1) & 1, abort_flag, err))
+                    break;
+                if (!mbar_wait(&S.full_a[sa], (s / kAStages) & 1, abort_flag, err)) break;
+                landed = s + 1;
+                if (!mbar_wait(&S.full_b[sb], (s / kBStages) & 1, abort_flag, err)) break;
+                tc_fence_after();
+                const uint64_t ad = sw128_desc(S.a[sa]), bd = sw128_desc(S.b[sb]);
+                const uint32_t d0 = tmem + buf * kBufCols;
+#pragma unroll
+                for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
+                    umma(d0, ad + 2 * j, bd + 2 * j, idesc, (in_chunk > 0 || j > 0) ? 1u : 0u);
+                umma_commit(&S.empty_a[sa]);
+                umma_commit(&S.empty_b[sb]);
+                if (in_chunk == kChunk - 1 || s == nk - 1) umma_commit(&S.chunk_full[buf]);
+                const int t = s + kAhead;
+                if (t < nk) {
+                    const int ts = t % kAStages;
+                    if (t >= kAStages && !mbar_wait(&S.empty_a[ts], ((t / kAStages) - 1) & 1, abort_flag, err))
+                        break;
+                    mbar_expect_tx(&S.full_a[ts], kTileBytes);
+                    tma_load_2d(S.a[ts], &tmap_a, t * kBK, pe.row0, &S.full_a[ts]);
+                    loaded = t + 1;
+                }
             }
+            umma_commit(&S.done);   // arrives once every MMA issued so far has completed
+            // aborted: the activation tiles still in flight must land before shared memory is released
+            for (int t = landed; t < loaded; ++t)
+                if (!mbar_drain(&S.full_a[t % kAStages], (t / kAStages) & 1, err)) break;
+            // every MMA must be complete before TMEM is freed, on the abort path too
+            mbar_drain(&S.done, 0, err);
         }
-        umma_commit(&S.done);   // arrives once every MMA issued so far has completed
-        // aborted: the activation tiles still in flight must land before shared memory is released
-        for (int t = landed; t < loaded; ++t)
-            if (!mbar_drain(&S.full_a[t % kAStages], (t / kAStages) & 1, err)) break;
-    }
-
-    // ── epilogue: TMEM -> registers -> global.  Warp w reads TMEM lanes 32 (w % 4) .. +31
-    // (its lane quarter) of M half (w / 4) % 2, i.e. tile row 128 ((w / 4) % 2) + 32 (w % 4) +
-    // lane, columns of half w / 8 ──────────────────────────────────────────────────────────────
-    if (tid < kDqThreads) {
-        // every MMA must be complete before TMEM is read or freed, on the abort path too
-        const bool finished = mbar_drain(&S.done, 0, err) && !*abort_flag && ok_ptrs;
         __syncwarp();
-        tc_fence_after();
-        const int q = warp & 3, half = (warp >> 2) & 1, ch = warp >> 3;   // lane quarter, M half, column half
-        const int m_row = half * kBM + q * 32 + lane;
-        const uint32_t lane_addr = tmem + (uint32_t(q * 32) << 16) + half * kBN;
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kFoldRegs));
+        // ── fold warps: warp f reads TMEM lanes 32 (f % 4) .. +31 (its lane quarter), column
+        // quarter f / 4: KIND 0 gate columns [32 cq, +32) and the same up columns, KIND 1 down
+        // columns [64 cq, +64) ──────────────────────────────────────────────────────────────
+        const int f = warp - kDqWarps;
+        const int q = f & 3, cq = f >> 2;
+        const int m_row = q * 32 + lane;
+        const uint32_t lane_addr = tmem + (uint32_t(q * 32) << 16);
+        const int ncol0 = nbase + (KIND == 0 ? 32 * cq : 64 * cq);   // first output column
+        const bool active = ncol0 < p.ndim;                        // warp-uniform
+        auto col_of = [&](int i) {                                 // piece i: 8 columns
+            return KIND == 0 ? ((i < 4) ? 32 * cq + 8 * i : kGuCols + 32 * cq + 8 * (i - 4)) : 64 * cq + 8 * i;
+        };
         const bool live = m_row < pe.ncols;
         const int pos = pe.row0 + m_row;
-        if (half == 0 || two) {                           // warp-uniform
-            if constexpr (KIND == 0) {
-#pragma unroll 1
-                for (int c = ch * (kBlk / 2); c < (ch + 1) * (kBlk / 2); c += 16) {
-                    uint32_t gr[16], ur[16];
-                    tmem_ld16(lane_addr + c, gr);
-                    tmem_ld16(lane_addr + kBlk + c, ur);
-                    if (finished && live) {
-                        uint32_t hb[16];
+        // KIND 1: the row's routing weight, fetched before the K loop (no epilogue latency)
+        int rowid = 0;
+        float wv = 0.f;
+        if (KIND == 1 && active && live && ok_ptrs) {
+            rowid = p.order[pos];
+            const int64_t t = rowid / p.top_k;
+            const int k = rowid - int(t) * p.top_k;
+            const int widx = p.w_index ? p.w_index[rowid] : k;
+            wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
+        }
+        uint64_t acc[kFoldVals / 2];                               // fp32 pairs (columns 2j, 2j + 1)
+        bool good = true;
+        for (int c = 0; c < n_chunks; ++c) {
+            const int buf = c & 1;
+            if (!mbar_wait(&S.chunk_full[buf], (c >> 1) & 1, abort_flag, err)) {
+                good = false;
+                break;
+            }
+            tc_fence_after();
+            if (active) {
+                const uint32_t base = lane_addr + buf * kBufCols;
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            const float gv = round_act<ACT>(__uint_as_float(gr[j]));
-                            const float uv = round_act<ACT>(__uint_as_float(ur[j]));
-                            const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
-                            hb[j] = act_bits<ACT>(__fmul_rn(av, uv));
-                        }
-                        // columns nbase+c .. +16 are two 8-element groups; store them permuted
-                        uint4 o0, o1;
-                        o0.x = hb[0] | (hb[4] << 16);
-                        o0.y = hb[1] | (hb[5] << 16);
-                        o0.z = hb[2] | (hb[6] << 16);
-                        o0.w = hb[3] | (hb[7] << 16);
-                        o1.x = hb[8] | (hb[12] << 16);
-                        o1.y = hb[9] | (hb[13] << 16);
-                        o1.z = hb[10] | (hb[14] << 16);
-                        o1.w = hb[11] | (hb[15] << 16);
-                        uint4* dst = reinterpret_cast<uint4*>(p.h_sorted + int64_t(pos) * p.ndim + nbase + c);
-                        dst[0] = o0;
-                        dst[1] = o1;
-                        if (p.h_out) {
-                            const int rowid = p.order[pos];
-                            for (int j = 0; j < 16; ++j)
-                                p.h_out[int64_t(rowid) * p.ndim + nbase + c + j] = static_cast<uint16_t>(hb[j]);
-                        }
+                for (int i = 0; i < kFoldVals / 8; ++i) {
+                    uint32_t v[8];
+                    tmem_ld8(base + col_of(i), v);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t pv = pack_f32x2(v[2 * j], v[2 * j + 1]);
+                        acc[4 * i + j] = c == 0 ? pv : add_f32x2(acc[4 * i + j], pv);
                     }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.chunk_free[buf]);
+        }
+        const bool finished = good && !*abort_flag && ok_ptrs;
+        if (active && finished && live) {
+            if constexpr (KIND == 0) {
+                // h for intermediate columns ncol0 .. +32: four 8-element groups, each stored
+                // permuted (and, on request, in natural order by row id) as soon as it is computed
+                uint4* dst = reinterpret_cast<uint4*>(p.h_sorted + int64_t(pos) * p.ndim + ncol0);
+                uint16_t* nat = p.h_out ? p.h_out + int64_t(p.order[pos]) * p.ndim + ncol0 : nullptr;
+#pragma unroll
+                for (int gq = 0; gq < 4; ++gq) {
+                    uint32_t hg[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const float2 gp = unpack_f32x2(acc[4 * gq + j / 2]), up = unpack_f32x2(acc[16 + 4 * gq + j / 2]);
+                        const float gv = round_act<ACT>((j & 1) ? gp.y : gp.x);
+                        const float uv = round_act<ACT>((j & 1) ? up.y : up.x);
+                        const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
+                        hg[j] = act_bits<ACT>(__fmul_rn(av, uv));
+                    }
+                    dst[gq] = make_uint4(hg[0] | (hg[4] << 16), hg[1] | (hg[5] << 16), hg[2] | (hg[6] << 16),
+                                         hg[3] | (hg[7] << 16));
+                    if (nat)
+                        *reinterpret_cast<uint4*>(nat + 8 * gq) = make_uint4(
+                            hg[0] | (hg[1] << 16), hg[2] | (hg[3] << 16), hg[4] | (hg[5] << 16), hg[6] | (hg[7] << 16));
                 }
             } else {
-                const int rowid = live ? p.order[pos] : 0;
-                float wv = 0.f;
-                if (finished && live) {
-                    const int64_t t = rowid / p.top_k;
-                    const int k = rowid - int(t) * p.top_k;
-                    const int widx = p.w_index ? p.w_index[rowid] : k;
-                    wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
-                }
-                const int ncol = min(kBN, p.ndim - nbase);   // 128 or 256: warp-uniform
-#pragma unroll 1
-                for (int c = ch * kBlk; c < min(ncol, (ch + 1) * kBlk); c += 16) {
-                    uint32_t yr[16];
-                    tmem_ld16(lane_addr + c, yr);
-                    if (finished && live) {
-                        float4 o[4];
-                        float* of = reinterpret_cast<float*>(o);
+                float4* dst = reinterpret_cast<float4*>(p.contrib + int64_t(rowid) * p.ndim + ncol0);
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            float cv = __fmul_rn(round_act<ACT>(__uint_as_float(yr[j])), wv);
-                            if (p.w_round) cv = round_act<ACT>(cv);
-                            of[j] = cv;
-                        }
-                        float4* dst = reinterpret_cast<float4*>(p.contrib + int64_t(rowid) * p.ndim + nbase + c);
+                for (int u = 0; u < kFoldVals / 4; ++u) {
+                    float o[4];
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) dst[u] = o[u];
+                    for (int j = 0; j < 4; ++j) {
+                        const float2 yp = unpack_f32x2(acc[2 * u + j / 2]);
+                        float cv = __fmul_rn(round_act<ACT>((j & 1) ? yp.y : yp.x), wv);
+                        if (p.w_round) cv = round_act<ACT>(cv);
+                        o[j] = cv;
                     }
+                    dst[u] = make_float4(o[0], o[1], o[2], o[3]);
                 }
             }
         }
@@ -612,8 +703,16 @@ int launch_gemm(const CUtensorMap& map, const GemmParams& gp, int max_tiles, cud
     const size_t smem = sizeof(GemmSmem) + 1024;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "prefill GEMM shared memory: %s", cudaGetErrorString(e));
+    // setmaxnreg.inc waits until the block's launch registers cover the split: never launch a
+    // build whose register count would leave the fold warps waiting
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "prefill GEMM attributes: %s", cudaGetErrorString(e));
+    if (static_cast<long long>(fa.numRegs) * kThreads < kRegSplit)
+        return fail(VY_ERR_UNSUPPORTED, "prefill GEMM built with %d registers a thread: %d x %d < the %d its "
+                    "register split needs", fa.numRegs, fa.numRegs, kThreads, kRegSplit);
     cudaLaunchConfig_t cfg = {};
-    const int nblk = KIND == 0 ? gp.ndim / kBlk : (gp.ndim + kBN - 1) / kBN;
+    const int nblk = KIND == 0 ? gp.ndim / kGuCols : (gp.ndim + kBN - 1) / kBN;
     cfg.gridDim = dim3(static_cast<unsigned>(max_tiles), static_cast<unsigned>(nblk));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
@@ -683,12 +782,14 @@ extern "C" int vy_moe_prefill(const vy_moe_call* c, void* stream) {
     if ((st = validate_call(c)) != VY_OK) return st;
     if (c->n_tokens == 0) return ok();
     const vy_expert_geom& g = *c->geom;
-    if (g.group_size < 32 || g.hidden % kBlk || g.inter % kBlk)
-        return fail(VY_ERR_UNSUPPORTED, "prefill tiles need hidden / intermediate multiples of %d", kBlk);
+    if (g.group_size < 32 || g.hidden % 128 || g.inter % kGuCols)
+        return fail(VY_ERR_UNSUPPORTED, "prefill tiles need hidden / intermediate multiples of %d", kGuCols);
     // a stage's scale / zero element is read as the aligned 8-byte word holding it
     for (int r = 0; r < 3; ++r)
         if (g.scale_off[r] % (g.scale_dtype == VY_F32 ? 2 : 4) || (g.has_zero && g.zero_off[r] % 2))
             return fail(VY_ERR_UNSUPPORTED, "prefill: role %d's scale / zero offset is not a multiple of 8 bytes", r);
+    if (c->h_out && !aligned16(c->h_out))
+        return fail(VY_ERR_ALIGNMENT, "prefill: h_out must be 16-byte aligned");
     PrefillLayout L = prefill_layout(c, nullptr);
     if (!c->workspace || c->workspace_bytes < L.bytes + 1024)
         return fail(VY_ERR_WORKSPACE, "workspace %zu bytes, %zu needed", c->workspace_bytes, L.bytes + 1024);
