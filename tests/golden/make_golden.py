@@ -174,10 +174,12 @@ def gen_decode(mp, pk, out):
     np.savez_compressed(out / "decode.npz", **cases)
 
 
-def gen_prefill(mp, pk, out):
-    """stock_experts_prefill with fp32-summed GEMMs (the kernels' reference) and with F.linear."""
+def gen_prefill(mp, pk, out, name="prefill", hid=128, inter=64, gs=32, tokens=12):
+    """stock_experts_prefill with fp32-summed GEMMs (the kernels' reference) and with F.linear.
+    `prefill` (intermediate 64) pins the oracle; `prefill_tiles` (hidden 256, intermediate 128,
+    40 tokens) is a geometry the CUDA kernels take, so the GPU suite reproduces it directly."""
     cases = {}
-    hid, inter, gs, n_exp, top_k, tokens = 128, 64, 32, 8, 3, 12
+    n_exp, top_k = 8, 3
     blobs = _experts(mp, hid, inter, n_exp, gs, 500)
     g = torch.Generator().manual_seed(501)
     eidx = torch.stack([torch.randperm(n_exp, generator=g)[:top_k] for _ in range(tokens)])
@@ -206,7 +208,7 @@ def gen_prefill(mp, pk, out):
     cases["plan_counts"] = arr(counts)
     cases["slot_order"] = arr(torch.argsort(eidx, dim=1, stable=True)
                               + (torch.arange(tokens) * top_k)[:, None])
-    np.savez_compressed(out / "prefill.npz", **cases)
+    np.savez_compressed(out / f"{name}.npz", **cases)
 
 
 def gen_cfg0(mp, pk, out):
@@ -271,20 +273,25 @@ def gen_asym(ct, out):
 
 
 def main():
-    if len(sys.argv) != 2:
-        raise SystemExit("usage: python tests/golden/make_golden.py <path to the reference project>")
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path to the reference project> [fixture ...]")
     root = Path(sys.argv[1])
     mp, pk, ds = _import_reference(root)
     import compressed_tensors.compressors.pack_quantized.helpers as ct
     torch.set_num_threads(8)
-    gen_unpack(mp, ct, HERE)
-    gen_dequant_role(mp, ct, HERE)
-    gen_blob(mp, HERE)
-    gen_decode(mp, pk, HERE)
-    gen_prefill(mp, pk, HERE)
-    gen_cfg0(mp, pk, HERE)
-    gen_fp8(ds, HERE)
-    gen_asym(ct, HERE)
+    gens = {
+        "unpack": lambda: gen_unpack(mp, ct, HERE),
+        "dequant_role": lambda: gen_dequant_role(mp, ct, HERE),
+        "blob": lambda: gen_blob(mp, HERE),
+        "decode": lambda: gen_decode(mp, pk, HERE),
+        "prefill": lambda: gen_prefill(mp, pk, HERE),
+        "prefill_tiles": lambda: gen_prefill(mp, pk, HERE, "prefill_tiles", 256, 128, 32, 40),
+        "cfg0": lambda: gen_cfg0(mp, pk, HERE),
+        "fp8": lambda: gen_fp8(ds, HERE),
+        "asym": lambda: gen_asym(ct, HERE),
+    }
+    for name in sys.argv[2:] or list(gens):
+        gens[name]()
     print("golden fixtures written to", HERE)
 
 

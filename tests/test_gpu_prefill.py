@@ -241,16 +241,15 @@ FORMS = [pytest.param(dict(), id="bf16-fp16scale-g128"),
 
 @pytest.mark.parametrize("kw", FORMS)
 def test_resident_table_prefill_matches_the_oracle(kw):
-    """300 tokens x 1024 outputs.  The tensor cores accumulate each output over the whole K in
-    one fp32 chain (as the reference's own GPU kernels do), so among ~600k rounding points of h a
-    few hundred land on the other side of a bf16 boundary than the oracle's double-accumulated
-    dot; the max-abs bar at this size is therefore taken against the fp64 truth: no worse than
-    the oracle's own error (rel-L2 within 5%, max-abs within 10%)."""
+    """300 tokens x 1024 outputs at the north-star bar (max |err| <= 2e-2 x RMS): every 256-element
+    K chunk accumulates from zero in TMEM and joins the fp32 sum with a round-to-nearest add, so
+    h lands on the oracle's side of a bf16 boundary as often as the decode GEMVs' does.  Also no
+    worse than the oracle against the fp64 truth."""
     blobs, x, idx, w = _table_case(**kw)
     got = vb.moe_forward(x, idx, w, pk.ExpertTable(blobs), path=pk._prefill_path()).cpu().numpy()
     ref = T.oracle_layer(blobs, x, idx, w)
     assert T.rel_l2(got, ref) <= 1e-3
-    assert T.max_abs_over_rms(got, ref) <= 4e-2
+    assert T.max_abs_over_rms(got, ref) <= 2e-2
     truth = T.fp64_layer(blobs, x, idx, w)
     assert T.rel_l2(got, truth) <= 1.05 * T.rel_l2(ref, truth) + 1e-12
     assert T.max_abs_over_rms(got, truth) <= 1.1 * T.max_abs_over_rms(ref, truth)

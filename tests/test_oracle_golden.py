@@ -212,3 +212,15 @@ def test_cfg0_layer_matches_the_reference_path():
                       threads=4)
     assert T.rel_l2(out, g["out"]) <= 2e-3
     assert T.max_abs_over_rms(out, g["out"]) <= 2e-2
+
+
+@pytest.mark.parametrize("tag,wcode", [("fp32", 2), ("bf16", 0)])
+def test_prefill_tiles_layer_matches_stock_experts_prefill(tag, wcode):
+    """The 40-token prefill fixture at a geometry the CUDA tiles take (hidden 256, inter 128)."""
+    g = T.golden("prefill_tiles")
+    hid, inter, bits, gs, n_exp, top_k, tokens = (int(v) for v in g["meta"])
+    out = O.moe_layer(T.geom(hid, inter, bits, gs), _experts_from(g, n_exp), g["x"], 0,
+                      g["eidx"], g[f"w_{tag}"], wcode, 1)
+    ref = g[f"out_{tag}"]
+    assert T.rel_l2(out, ref) <= 2e-3
+    assert T.max_abs_over_rms(out, ref) <= 2e-2

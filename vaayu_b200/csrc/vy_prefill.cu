@@ -19,8 +19,9 @@
 //            rounding of every weight (sub.rn then mul.rn on activation-dtype pairs) and stores
 //            16-byte chunks into the weight tile in the 128-byte-swizzled K-major layout the
 //            tensor core reads; each warp then arrives once on the stage's barrier.
-//   control  loads the 128-row activation tile with one TMA box (same swizzle, no multicast) and
-//            issues tcgen05.mma M=128 N=256 K=16.
+//   control  one thread issues tcgen05.mma M=128 N=256 K=16 (and nothing else: the tensor core
+//            queues only a few MMAs, so other work in that thread lets it drain); a second thread
+//            loads the 128-row activation tiles with one TMA box each (same swizzle, no multicast).
 //   fold     K is cut into chunks of kChunk stages.  Each chunk accumulates from zero in one of
 //            two TMEM buffers (2 x 256 columns); the fold warps read it with tcgen05.ld and add it
 //            into fp32 sums held in their registers with round-to-nearest adds (paired fp32 adds),
@@ -54,7 +55,7 @@ constexpr int kGuCols = kBN / 2;      // intermediate columns of one gate/up CTA
 #define VY_PF_PACK 4
 #endif
 #ifndef VY_PF_CHUNK
-#define VY_PF_CHUNK 2
+#define VY_PF_CHUNK 4
 #endif
 constexpr int kAStages = VY_PF_ASTAGES;   // activation-tile ring (TMA)
 constexpr int kBStages = VY_PF_BSTAGES;   // weight-tile ring (dequant warps)
@@ -320,7 +321,8 @@ struct __align__(1024) GemmSmem {
     uint16_t a[kAStages][kUnit * kBK];         // activation tiles (TMA, swizzled): rows 0-127
     uint16_t b[kBStages][kBN * kBK];           // weight tiles: KIND 0 rows 0-127 gate, 128-255 up
     uint4 pack[kPack][2][kDqThreads];          // packed codes (2 chunks of a row), private per thread
-    uint64_t full_a[kAStages], empty_a[kAStages], full_b[kBStages], empty_b[kBStages];
+    uint64_t full_a[kAStages], full_b[kBStages];
+    uint64_t mma_done[kAStages];               // stage s's MMAs complete: barrier s % kAStages
     uint64_t chunk_full[2], chunk_free[2], done;
     uint32_t tmem_base;
     int abort_flag;
@@ -366,12 +368,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     if (tid == 0) {
         for (int i = 0; i < kAStages; ++i) {
             mbar_init(&S.full_a[i], 1);
-            mbar_init(&S.empty_a[i], 1);
+            mbar_init(&S.mma_done[i], 1);
         }
-        for (int i = 0; i < kBStages; ++i) {
-            mbar_init(&S.full_b[i], kDqWarps);      // one arrive per dequant warp
-            mbar_init(&S.empty_b[i], 1);
-        }
+        for (int i = 0; i < kBStages; ++i) mbar_init(&S.full_b[i], kDqWarps);   // one arrive per dequant warp
         for (int i = 0; i < 2; ++i) {
             mbar_init(&S.chunk_full[i], 1);
             mbar_init(&S.chunk_free[i], kFoldWarps);   // one arrive per fold warp
@@ -440,9 +439,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             }
             cp_async_wait<kPack - 1>();
             const int slot = s % kBStages;
-            // warp-uniform decision: a lane that left the loop alone would strand the warp's arrive
-            if (s >= kBStages &&
-                !__all_sync(0xffffffffu, mbar_wait(&S.empty_b[slot], ((s / kBStages) - 1) & 1, abort_flag, err)))
+            // the slot is free once stage s - kBStages's MMAs are done; warp-uniform decision: a lane
+            // that left the loop alone would strand the warp's arrive
+            const int u = s - kBStages;
+            if (u >= 0 &&
+                !__all_sync(0xffffffffu, mbar_wait(&S.mma_done[u % kAStages], (u / kAStages) & 1, abort_flag, err)))
                 break;
             const int ps = s % kPack;
             const uint4 w0 = S.pack[ps][0][tid], w1 = S.pack[ps][1][tid];
@@ -466,17 +467,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
     } else if (warp >= kCtlWarp) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kCtlRegs));
         if (warp == kCtlWarp && lane == 0) {
-            // ── control: activation tiles by TMA, tcgen05.mma (M = 128, N = 256), commits ────
+            // ── MMA issuer: nothing but the waits its MMAs need, the MMAs and one commit a stage
+            // (the tensor core queues only a few MMAs: any other work here would let it drain) ─
             constexpr uint32_t idesc = idesc_f16<ACT>();
-            // kAhead tiles in flight: the tile issued after MMA s refills the slot MMA s - 2 read,
-            // which has completed by then (waiting for MMA s - 1 instead would put the commit ->
-            // barrier -> wake-up latency into every stage)
-            constexpr int kAhead = kAStages - 2;
-            int loaded = 0, landed = 0;   // activation tiles issued / seen complete
-            for (; loaded < kAhead && loaded < nk; ++loaded) {
-                mbar_expect_tx(&S.full_a[loaded], kTileBytes);
-                tma_load_2d(S.a[loaded], &tmap_a, loaded * kBK, pe.row0, &S.full_a[loaded]);
-            }
             for (int s = 0; s < nk; ++s) {
                 const int sa = s % kAStages, sb = s % kBStages;
                 const int c = s / kChunk, buf = c & 1, in_chunk = s - c * kChunk;
@@ -485,7 +478,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
                     !mbar_wait(&S.chunk_free[buf], ((c >> 1) - 1) & 1, abort_flag, err))
                     break;
                 if (!mbar_wait(&S.full_a[sa], (s / kAStages) & 1, abort_flag, err)) break;
-                landed = s + 1;
                 if (!mbar_wait(&S.full_b[sb], (s / kBStages) & 1, abort_flag, err)) break;
                 tc_fence_after();
                 const uint64_t ad = sw128_desc(S.a[sa]), bd = sw128_desc(S.b[sb]);
@@ -493,25 +485,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j)   // K = 16 per instruction: +32 bytes per step
                     umma(d0, ad + 2 * j, bd + 2 * j, idesc, (in_chunk > 0 || j > 0) ? 1u : 0u);
-                umma_commit(&S.empty_a[sa]);
-                umma_commit(&S.empty_b[sb]);
+                umma_commit(&S.mma_done[sa]);        // frees the activation and weight slots
                 if (in_chunk == kChunk - 1 || s == nk - 1) umma_commit(&S.chunk_full[buf]);
-                const int t = s + kAhead;
-                if (t < nk) {
-                    const int ts = t % kAStages;
-                    if (t >= kAStages && !mbar_wait(&S.empty_a[ts], ((t / kAStages) - 1) & 1, abort_flag, err))
-                        break;
-                    mbar_expect_tx(&S.full_a[ts], kTileBytes);
-                    tma_load_2d(S.a[ts], &tmap_a, t * kBK, pe.row0, &S.full_a[ts]);
-                    loaded = t + 1;
-                }
             }
             umma_commit(&S.done);   // arrives once every MMA issued so far has completed
-            // aborted: the activation tiles still in flight must land before shared memory is released
-            for (int t = landed; t < loaded; ++t)
-                if (!mbar_drain(&S.full_a[t % kAStages], (t / kAStages) & 1, err)) break;
             // every MMA must be complete before TMEM is freed, on the abort path too
             mbar_drain(&S.done, 0, err);
+        } else if (warp == kCtlWarp + 1 && lane == 0) {
+            // ── activation producer: one TMA box per stage into the ring; a slot is refilled once
+            // the MMAs of the stage that last used it are done ────────────────────────────────
+            int loaded = 0;
+            for (int t = 0; t < nk; ++t) {
+                const int ts = t % kAStages, u = t - kAStages;
+                if (u >= 0 && !mbar_wait(&S.mma_done[ts], (u / kAStages) & 1, abort_flag, err)) break;
+                mbar_expect_tx(&S.full_a[ts], kTileBytes);
+                tma_load_2d(S.a[ts], &tmap_a, t * kBK, pe.row0, &S.full_a[ts]);
+                loaded = t + 1;
+            }
+            // every tile still in flight (only the last kAStages issued can be) lands before the
+            // shared memory is released, on the abort path too
+            for (int t = loaded > kAStages ? loaded - kAStages : 0; t < loaded; ++t)
+                if (!mbar_drain(&S.full_a[t % kAStages], (t / kAStages) & 1, err)) break;
         }
         __syncwarp();
     } else {
