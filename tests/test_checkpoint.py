@@ -93,3 +93,46 @@ def test_bf16_and_fp8_tensors_read_back_exactly(tmp_path):
             assert torch.equal(r.view(torch.uint8), v.view(torch.uint8))
     finally:
         f.close()
+
+
+def test_lowest_expert_and_the_install_probe_read_the_layer_file(tmp_path):
+    """The engine's per-layer file `<checkpoint_path>/<layer_name>.safetensors`: the install probe
+    reads its lowest-numbered expert with this package's reader (no engine loader) and builds the
+    same blob as the in-memory components."""
+    from types import SimpleNamespace
+
+    from vaayu_b200 import packed_expert_kernels as pk
+    tensors, mem = {}, {}
+    for e in (7, 2, 5):
+        raw, by_role = _raw(prefix=f"model.layers.4.mlp.experts.{e}", seed=30 + e)
+        tensors.update(raw)
+        mem[e] = vb.build_expert_blob(by_role)
+    ck.write_safetensors(str(tmp_path / "model.layers.4.mlp.safetensors"), tensors)
+    cp = ck.Checkpoint(str(tmp_path / "model.layers.4.mlp.safetensors"))
+    try:
+        assert cp.lowest_expert() == ("model.layers.4.mlp", 2)
+    finally:
+        cp.close()
+    engine = SimpleNamespace(checkpoint_path=str(tmp_path))
+    block = SimpleNamespace(layer_name="model.layers.4.mlp", layer_idx=4)
+    blob = pk._probe_blob(engine, block, "cpu")
+    assert blob["geom"] == mem[2]["geom"]
+    for k, t in mem[2]["flat"].items():
+        assert torch.equal(blob["flat"][k], t), k
+    # the host's own probe wins; a missing layer file reads as "no blob"
+    engine.packed_probe_blob = lambda b, d: mem[5]
+    assert pk._probe_blob(engine, block, "cpu") is mem[5]
+    assert pk._probe_blob(SimpleNamespace(checkpoint_path=str(tmp_path)),
+                          SimpleNamespace(layer_name="model.layers.9.mlp"), "cpu") is None
+
+
+def test_install_leaves_a_cpu_model_and_a_model_without_fused_blocks_alone():
+    from types import SimpleNamespace
+
+    from vaayu_b200 import packed_expert_kernels as pk
+    cpu_model = SimpleNamespace(running_device="cpu", running_dtype=torch.bfloat16, _moe_blocks=[])
+    assert pk.install_packed_expert_kernels(cpu_model) is False
+    assert not hasattr(cpu_model, "_packed_moe_kernel")
+    assert pk._is_silu(torch.nn.functional.silu, "cpu", torch.float32)
+    assert not pk._is_silu(torch.nn.functional.gelu, "cpu", torch.float32)
+    assert not pk._is_silu(None, "cpu", torch.float32)

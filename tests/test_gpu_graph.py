@@ -1,6 +1,6 @@
-"""GPU: one CUDA graph per MoE layer for one-token decode (the reference's S28 C5 path,
-tests/test_packed_expert_kernels.py:301-676): capture gives the eager bits, replay rewrites only
-the table, and every failure falls back to the eager result."""
+"""GPU: one CUDA graph per MoE layer for one-token decode (`packed_experts_decode_graphed`, the
+contract of vaayu/packed_expert_kernels.py:531-539): a recording gives the eager bits, a replay
+computes the call's own experts, and every failure leaves the layer on the eager result."""
 import collections
 import gc
 
@@ -16,8 +16,8 @@ QWEN = (2048, 512, 32, 10)
 
 @pytest.fixture
 def fresh(monkeypatch):
-    for name, val in (("_GRAPHS", {}), ("_GRAPH_REFUSED", {}), ("_GRAPH_WARNED", set()),
-                      ("GRAPH_STATS", collections.Counter())):
+    for name, val in (("_GRAPHS", {}), ("_GRAPH_OFF", {}), ("_GRAPH_NOTES", set()),
+                      ("_GRAPH_VERIFIED", set()), ("GRAPH_STATS", collections.Counter())):
         monkeypatch.setattr(pk, name, val)
 
 
@@ -55,7 +55,7 @@ def test_the_graph_gives_the_eager_bits(fresh, tail, shared):
     second = pk.packed_experts_decode_graphed(0, x, pairs, w, sh, None, tail)
     torch.cuda.synchronize()
     assert torch.equal(second, want)
-    assert (pk.GRAPH_STATS["captures"], pk.GRAPH_STATS["replays"]) == (1, 1)
+    assert (pk.GRAPH_STATS["recorded"], pk.GRAPH_STATS["replays"]) == (1, 1)
 
 
 def test_a_rewritten_table_computes_the_new_experts(fresh):
@@ -74,29 +74,29 @@ def test_a_new_input_tensor_recaptures(fresh):
     pk.packed_experts_decode_graphed(0, x, pairs, w, None, None, False)
     x2 = x * 2
     got = pk.packed_experts_decode_graphed(0, x2, pairs, w, None, None, False)
-    assert pk.GRAPH_STATS["captures"] == 2
+    assert pk.GRAPH_STATS["recorded"] == 2
     assert torch.equal(got, _eager(x2, pairs, w, None, False))
 
 
-def test_inputs_that_move_every_call_keep_working(fresh, capsys):
+def test_inputs_that_move_every_call_keep_working(fresh, caplog):
     x, pairs, w, _b = _case(*QWEN)
     xs = [x * (i + 1) for i in range(5)]
     outs = [pk.packed_experts_decode_graphed(0, xi, pairs, w, None, None, False).clone() for xi in xs]
     torch.cuda.synchronize()
-    assert 0 not in pk._GRAPH_REFUSED and "WARNING" not in capsys.readouterr().out
+    assert 0 not in pk._GRAPH_OFF and not [r for r in caplog.records if r.levelname == "WARNING"]
     assert all(torch.equal(o, _eager(xi, pairs, w, None, False)) for o, xi in zip(outs, xs))
-    assert pk.GRAPH_STATS["captures"] == 5 and pk.GRAPH_STATS["replaced_unreplayed"] == 4
+    assert pk.GRAPH_STATS["recorded"] == 5 and pk.GRAPH_STATS["recorded_unused"] == 4
 
 
-def test_a_replay_that_disagrees_refuses_the_layer(fresh, monkeypatch, capsys):
+def test_a_replay_that_disagrees_refuses_the_layer(fresh, monkeypatch, caplog):
     x, pairs, w, _b = _case(*QWEN)
     want = _eager(x, pairs, w, None, False)
     real = pk._launch
     monkeypatch.setattr(pk, "_launch", lambda x, p, w, out, h_out=None: (real(x, p, w, out), out.add_(1.0)))
     got = pk.packed_experts_decode_graphed(0, x, pairs, w, None, None, False)
     assert torch.equal(got, want + 1.0), "the eager result is returned, never the graph's"
-    assert "disagrees bitwise" in pk._GRAPH_REFUSED.get(0, "")
-    assert "WARNING" in capsys.readouterr().out
+    assert "bit for bit" in pk._GRAPH_OFF.get(0, "")
+    assert any(r.levelname == "WARNING" and "stays eager" in r.getMessage() for r in caplog.records)
     assert pk.packed_experts_decode_graphed(0, x, pairs, w, None, None, False) is None
 
 
@@ -104,13 +104,13 @@ def test_a_call_the_graph_cannot_take_is_left_to_the_caller(fresh):
     x, pairs, w, _b = _case(*QWEN)
     mixed = [({"dense": {}}, pairs[0][1])] + pairs[1:]
     assert pk.packed_experts_decode_graphed(0, x, mixed, w, None, None, False) is None
-    assert pk.GRAPH_STATS["captures"] == 0
+    assert pk.GRAPH_STATS["recorded"] == 0
 
 
 def test_the_capture_allocates_only_its_static_buffers(fresh):
     x, pairs, w, _b = _case(*QWEN)
     sh = _shared(QWEN[0])
-    for _ in range(len(pk._TABLES._slots)):
+    for _ in range(4):
         _eager(x, pairs, w, sh, True)
     pk.packed_experts_decode_graphed(99, x * 3, pairs, w, sh, None, True)
     gc.collect()
@@ -120,12 +120,14 @@ def test_the_capture_allocates_only_its_static_buffers(fresh):
     torch.cuda.synchronize()
     g = pk._GRAPHS[0]
     static = sum(-(-t.numel() * t.element_size() // 512) * 512
-                 for t in (g.tbl, g.ws, g.out, g.tmp, g.result))
-    assert torch.cuda.memory_allocated() - m0 == static
+                 for t in (g.table, g.scratch, g.sum, g.cast, g.with_shared))
+    held = torch.cuda.memory_allocated() - m0
+    # torch's caching allocator rounds a block of 10 MB or more up to a 2 MB multiple
+    assert static <= held < static + (2 << 20)
     for _ in range(50):
         pk.packed_experts_decode_graphed(0, x, pairs, w, sh, None, True)
     torch.cuda.synchronize()
-    assert torch.cuda.memory_allocated() - m0 == static
+    assert torch.cuda.memory_allocated() - m0 == held, "a replay allocates nothing"
     assert pk.GRAPH_STATS["replays"] == 50
     del g
     pk._GRAPHS.pop(0)
@@ -160,7 +162,7 @@ def test_a_capture_leaves_gc_as_found(fresh, monkeypatch, capture_fails):
         monkeypatch.setattr(pk, "_decode_from_table", boom)
     for enabled in (False, True):
         pk._GRAPHS.clear()
-        pk._GRAPH_REFUSED.clear()
+        pk._GRAPH_OFF.clear()
         (gc.enable if enabled else gc.disable)()
         try:
             out = pk.packed_experts_decode_graphed(0, x * (2 if enabled else 3), pairs, w, None, None, False)
@@ -168,13 +170,13 @@ def test_a_capture_leaves_gc_as_found(fresh, monkeypatch, capture_fails):
         finally:
             gc.enable()
         assert out is not None
-        assert (0 in pk._GRAPH_REFUSED) == capture_fails
+        assert (0 in pk._GRAPH_OFF) == capture_fails
 
 
-def test_an_input_the_graph_cannot_take_warns_once(fresh, capsys):
+def test_an_input_the_graph_cannot_take_warns_once(fresh, caplog):
     x, pairs, w, _b = _case(*QWEN)
     w_strided = torch.cat([w, w], dim=1)[:, ::2]
     for _ in range(3):
         assert pk.packed_experts_decode_graphed(0, x, pairs, w_strided, None, None, False) is None
-    out = capsys.readouterr().out
-    assert out.count("WARNING") == 1 and "not used" in out
+    warned = [r.getMessage() for r in caplog.records if r.levelname == "WARNING"]
+    assert len(warned) == 1 and "run eagerly" in warned[0]

@@ -119,6 +119,16 @@ class Checkpoint:
         pat = re.compile(re.escape(layer_prefix) + r"\.experts\.(\d+)\.")
         return sorted({int(m.group(1)) for k in self.index for m in [pat.match(k)] if m})
 
+    def lowest_expert(self):
+        """(layer prefix, expert id) of the lowest-numbered expert stored anywhere in these files
+        (keys "<prefix>.experts.<id>.<...>"), or None when they hold no expert tensors."""
+        pat = re.compile(r"^(.*)\.experts\.(\d+)\.")
+        found = [(int(m.group(2)), m.group(1)) for k in self.index for m in [pat.match(k)] if m]
+        if not found:
+            return None
+        e, prefix = min(found)
+        return prefix, e
+
     def read_expert(self, layer_prefix: str, expert: int) -> dict:
         """{key: tensor} of one expert: the sparse read (only its own bytes)."""
         return {k: self.index[k].tensor(k) for k in self.expert_keys(layer_prefix, expert)}

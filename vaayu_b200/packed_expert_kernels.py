@@ -17,10 +17,13 @@ What differs from the reference, on purpose:
   * No fallback.  A call the kernels cannot take (mixed geometries, a dense entry, unsupported
     geometry or dtype) raises NotImplementedError instead of running the stock per-expert loop:
     this build has no CPU / torch / Triton path.  `install_packed_expert_kernels` still answers
-    False with a WARNING for a model it cannot serve, leaving the engine's own path in place.
+    False (and logs why) for a model it cannot serve, leaving the engine's own path in place.
   * The verdict is a geometry gate only (`_unsupported`); the first-call comparison against the
     stock arithmetic lives in the test suite, not in the product.
   * Zero-point blobs are served (see vaayu_b200.moe_patch).
+  * A call's host-built table reaches the device through torch's pinned caching allocator with a
+    stream-ordered copy (`_stage`); the layer graph records device work only and is fed the same
+    way.  Reports go to the "vaayu_b200" logger.
 Arithmetic: every weight is act(act(u - z) * act(scale)); g, u, SiLU(g), h, y are rounded to
 the activation dtype where the stock loop rounds; y * w is one fp32 product (rounded to the
 activation dtype when the weight is in that dtype); each token's contributions are summed in
@@ -32,6 +35,8 @@ import collections
 import ctypes
 import functools
 import gc
+import logging
+import os
 import threading
 
 import torch
@@ -52,27 +57,24 @@ def _layout(geom) -> dict:
 
 
 def _unsupported(geom, act_dtype, scale_dtype, w_dtype):
-    """Why the kernels cannot run a call with this geometry and these dtypes, or None."""
+    """The first reason the layer kernels cannot serve this (geometry, dtypes), or None."""
     bits, gs, roles = geom
-    shapes = {r: (rows, cols) for r, rows, cols in roles}
-    if set(shapes) != set(_ROLES):
-        return f"expert roles {sorted(shapes)} are not gate/up/down"
-    inter, hid = shapes["gate"]
-    if shapes["up"] != (inter, hid) or shapes["down"] != (hid, inter):
-        return f"projection shapes {shapes} are not a gated MLP"
-    if bits != 4:
-        return f"{bits}-bit codes (the expert kernels take int4)"
-    if gs & (gs - 1) or gs < 32:
-        return f"group size {gs} is not a power of two >= 32"
-    if hid % 128 or inter % 128 or hid % gs or inter % gs:
-        return (f"hidden {hid} / intermediate {inter} are not multiples of 128 and of the "
-                f"group size {gs}")
-    if act_dtype not in (torch.bfloat16, torch.float16):
-        return f"activation dtype {act_dtype} (bf16 / fp16)"
-    for what, dt in (("scale", scale_dtype), ("routing-weight", w_dtype)):
-        if dt not in _DTYPE_CODE:
-            return f"{what} dtype {dt}"
-    return None
+    dims = {role: (rows, cols) for role, rows, cols in roles}
+    if sorted(dims) != sorted(_ROLES):
+        return f"the blob holds roles {sorted(dims)}; the layer kernels need exactly gate, up and down"
+    inter, hid = dims["gate"]
+    if dims["up"] != (inter, hid) or dims["down"] != (hid, inter):
+        return f"role shapes {dims} do not form a gated MLP (gate / up [I, H], down [H, I])"
+    checks = (
+        (bits == 4, f"{bits}-bit codes: the layer kernels read int4"),
+        (gs >= 32 and gs & (gs - 1) == 0, f"group size {gs}: a power of two of at least 32 is needed"),
+        (hid % 128 == 0 and inter % 128 == 0 and hid % gs == 0 and inter % gs == 0,
+         f"hidden {hid} / intermediate {inter} must be multiples of 128 and of the group size {gs}"),
+        (act_dtype in (torch.bfloat16, torch.float16), f"activation dtype {act_dtype}: bf16 or fp16"),
+        (scale_dtype in _DTYPE_CODE, f"scale dtype {scale_dtype}"),
+        (w_dtype in _DTYPE_CODE, f"routing-weight dtype {w_dtype}"),
+    )
+    return next((why for ok, why in checks if not ok), None)
 
 
 @functools.lru_cache(maxsize=None)
@@ -104,7 +106,7 @@ def _blob_key(blob):
     return blob["geom"], flat["scale"].dtype, "zero" in flat
 
 
-# ── per-stream scratch and the pinned table ring ─────────────────────────────────────────
+# ── per-stream scratch and host-built tables ─────────────────────────────────────────────
 
 class _Workspace:
     """Scratch for the kernels, one buffer per (device, stream), grown on demand (torch's
@@ -125,40 +127,20 @@ class _Workspace:
 
 
 _WORKSPACE = _Workspace()
-
-
-class _TableRing:
-    """Pinned staging for a call's table, reused round-robin.  A slot's host buffer is rewritten
-    only after the H2D copy that last read it completed (its event); each slot has its own device
-    buffer, so no queued kernel's table is overwritten (vaayu/packed_expert_kernels.py:263-292)."""
-
-    def __init__(self, n_slots: int = 4):
-        self._slots: list = [None] * n_slots
-        self._next = 0
-
-    def put(self, values: torch.Tensor, device) -> torch.Tensor:
-        i = self._next
-        self._next = (i + 1) % len(self._slots)
-        n = values.numel()
-        slot = self._slots[i]
-        if slot is None or slot[0].numel() < n or slot[1].device != device:
-            host = torch.empty(max(64, 1 << (n - 1).bit_length()), dtype=torch.int64, pin_memory=True)
-            slot = self._slots[i] = [host, torch.empty(host.shape, dtype=torch.int64, device=device),
-                                     torch.cuda.Event(), False]
-        host, dev, done, used = slot
-        if used:
-            done.synchronize()
-        host[:n] = values
-        dev[:n].copy_(host[:n], non_blocking=True)
-        done.record()
-        slot[3] = True
-        return dev
-
-
-_TABLES = _TableRing()
-_PF_TABLES = _TableRing()
 _VERDICTS: dict = {}
 _PF_VERDICTS: dict = {}
+
+
+def _stage(values: torch.Tensor, device, into: "torch.Tensor | None" = None) -> torch.Tensor:
+    """A host-built table on `device`: copied on the current stream from a pinned block of torch's
+    caching host allocator, which keeps the block from reuse until the copy has read it.  The
+    device side is a fresh caching-allocator tensor (reusable only by later work on this stream),
+    or `into` when given (a graph's static table)."""
+    pinned = values.pin_memory()
+    if into is None:
+        return pinned.to(device, non_blocking=True)
+    into[:values.numel()].copy_(pinned, non_blocking=True)
+    return into
 
 
 # ── the call itself ──────────────────────────────────────────────────────────────────────
@@ -203,8 +185,9 @@ def _check_x(x, what):
 
 
 def _pairs_table(pairs) -> torch.Tensor:
-    """Pinned-ring payload of a decode call: int64 [4n] = n x (packed, scale, zero) addresses,
-    then n int32 expert indices (0..n-1, the table order) and n int32 slots."""
+    """A one-token decode call's table payload: int64 [4n] = n x (packed, scale, zero) stream
+    addresses in the pairs' order, then n int32 table indices (0..n-1: the pairs' order is the
+    order the fp32 sum runs in) and n int32 routing slots."""
     n = len(pairs)
     vals = torch.empty(4 * n, dtype=torch.int64)
     vals[:3 * n] = torch.tensor([p for blob, _s in pairs for p in _blob_ptrs(blob)], dtype=torch.int64)
@@ -225,21 +208,20 @@ def _decode_from_table(x, n, geom_s, dev_tbl, rw, out, h_out=None, workspace=Non
 
 def _launch(x, pairs, routing_weights, out, h_out=None) -> None:
     """The decode kernels over `pairs`, into `out`.  No checks: `_checked` gates this."""
-    blob0 = pairs[0][0]
-    geom_s = _geom_struct(*_blob_key(blob0))
-    tbl = _TABLES.put(_pairs_table(pairs), x.device)
+    geom_s = _geom_struct(*_blob_key(pairs[0][0]))
+    tbl = _stage(_pairs_table(pairs), x.device)
     _decode_from_table(x, len(pairs), geom_s, tbl, routing_weights, out, h_out)
 
 
 def _checked(x, pairs, routing_weights, act_fn=None) -> None:
-    """The cached geometry verdict for this call's (geometry, dtypes) key; raises when the
-    kernels cannot take it."""
+    """Raises NotImplementedError when the kernels cannot take this call's (geometry, dtypes);
+    the answer is cached per key."""
     blob = pairs[0][0]
     key = (blob["geom"], x.dtype, routing_weights.dtype, blob["flat"]["scale"].dtype)
-    if key not in _VERDICTS:
-        _VERDICTS[key] = _unsupported(blob["geom"], x.dtype, blob["flat"]["scale"].dtype,
-                                      routing_weights.dtype)
-    why = _VERDICTS[key]
+    why = _VERDICTS.get(key, False)
+    if why is False:
+        why = _VERDICTS[key] = _unsupported(blob["geom"], x.dtype, blob["flat"]["scale"].dtype,
+                                            routing_weights.dtype)
     if why is not None:
         raise NotImplementedError(f"fused packed-expert decode kernel: {why}")
 
@@ -279,17 +261,24 @@ def packed_experts_decode(x, pairs, routing_weights, out, act_fn=None) -> None:
         _launch(x, pairs, routing_weights, out)
 
 
-# ── one CUDA graph per MoE layer (vaayu/packed_expert_kernels.py:483-654) ────────────────────
+# ── one CUDA graph per MoE layer for one-token decode ────────────────────────────────────
+#
+# A layer's graph records only device work -- the routing plan, the gate/up and down kernels, the
+# combine and, on request, the forward's epilogue -- over static device buffers.  A call copies its
+# pair table into the graph's static table with an ordinary stream-ordered copy (`_stage`) and
+# replays.  The graph is recorded again when an input address, the pair count, the format or the
+# epilogue changes.  The first graph recorded for a layer is held bitwise to an eager launch of the
+# same call; a mismatch, or a recording that raises, switches the graph path off for that layer
+# (its calls then return None: the caller launches eagerly).  Reasons are logged once each.
 
-_GRAPHS: dict = {}              # layer -> _LayerGraph
-_GRAPH_REFUSED: dict = {}       # layer -> why
-_GRAPH_WARNED: set = set()
-_GRAPH_STREAMS: dict = {}       # device -> capture stream
-GRAPH_STATS: collections.Counter = collections.Counter()
-
-
-class _LayerGraph:
-    __slots__ = ("key", "graph", "host", "tbl", "ws", "out", "tmp", "result", "done", "replays")
+log = logging.getLogger("vaayu_b200")
+GRAPH_STATS: collections.Counter = collections.Counter()   # recorded, replays, recorded_unused, off
+_GRAPHS: dict = {}              # layer -> _DecodeGraph
+_GRAPH_OFF: dict = {}           # layer -> why the graph path is off for it
+_GRAPH_VERIFIED: set = set()    # layers whose first recording matched the eager launch bitwise
+_GRAPH_NOTES: set = set()       # reasons already logged
+_CAPTURE_STREAMS: dict = {}     # device -> side stream the recordings run on
+_KERNELS_READY: set = set()     # devices where an eager call has set the kernels' attributes up
 
 
 def _tail(out, dtype, shared):
@@ -300,133 +289,150 @@ def _tail(out, dtype, shared):
     return result
 
 
-def _refuse_graph(layer, why) -> None:
-    _GRAPH_REFUSED[layer] = why
+def _graph_note(why: str) -> None:
+    if why not in _GRAPH_NOTES:
+        _GRAPH_NOTES.add(why)
+        log.warning("vaayu_b200 decode graph: %s", why)
+
+
+def _graph_off(layer, why: str) -> None:
+    _GRAPH_OFF[layer] = why
     _GRAPHS.pop(layer, None)
-    GRAPH_STATS["refused"] += 1
-    if why not in _GRAPH_WARNED:
-        _GRAPH_WARNED.add(why)
-        print(f"[Vaayu] WARNING: packed-expert decode graph refused for MoE layer {layer} "
-              f"({why}); it launches eagerly. Later layers refused for the same reason are "
-              f"not listed.")
+    GRAPH_STATS["off"] += 1
+    _graph_note(f"layer {layer} stays eager: {why}")
 
 
-def _warn_skip(why) -> None:
-    if why not in _GRAPH_WARNED:
-        _GRAPH_WARNED.add(why)
-        print(f"[Vaayu] WARNING: packed-expert decode graph not used ({why}); those calls "
-              f"launch the kernels eagerly. Shown once per reason.")
+class _DecodeGraph:
+    """One layer's recorded decode step and the static buffers it reads and writes."""
+
+    def __init__(self, key, x, n_pairs, shared, tail):
+        dev = x.device
+        self.key, self.n, self.tail, self.replays = key, n_pairs, tail, 0
+        self.table = torch.empty(4 * n_pairs, dtype=torch.int64, device=dev)
+        probe = _lib.MoeCall()
+        probe.geom = ctypes.pointer(key[-1])
+        probe.n_tokens, probe.top_k, probe.n_experts = 1, n_pairs, n_pairs
+        self.scratch = torch.empty(max(_lib.lib().vy_moe_workspace_size(ctypes.byref(probe), PATH_DECODE), 256),
+                                   dtype=torch.uint8, device=dev)
+        self.sum = torch.empty(x.shape, dtype=torch.float32, device=dev)
+        self.cast = torch.empty(x.shape, dtype=x.dtype, device=dev) if tail else None
+        self.with_shared = (torch.empty(x.shape, dtype=x.dtype, device=dev)
+                            if tail and shared is not None else None)
+        self.graph = torch.cuda.CUDAGraph()
+
+    @property
+    def result(self):
+        if not self.tail:
+            return self.sum
+        return self.with_shared if self.with_shared is not None else self.cast
+
+    def body(self, x, rw, shared):
+        """The recorded work: the layer into `sum`, then the epilogue."""
+        _decode_from_table(x, self.n, self.key[-1], self.table, rw, self.sum, workspace=self.scratch)
+        if self.tail:
+            self.cast.copy_(self.sum)
+            if self.with_shared is not None:
+                torch.add(self.cast, shared, out=self.with_shared)
+
+    def record(self, x, rw, shared):
+        dev = x.device
+        side = _CAPTURE_STREAMS.get(dev)
+        if side is None:
+            side = _CAPTURE_STREAMS[dev] = torch.cuda.Stream(device=dev)
+        here = torch.cuda.current_stream(dev)
+        side.wait_stream(here)
+        gc_on = gc.isenabled()
+        gc.disable()        # a collection during the recording could run another graph's teardown
+        try:
+            with torch.cuda.stream(side), torch.no_grad():
+                self.graph.capture_begin(pool=torch.cuda.graph_pool_handle(), capture_error_mode="thread_local")
+                try:
+                    self.body(x, rw, shared)
+                finally:
+                    self.graph.capture_end()
+        finally:
+            if gc_on:
+                gc.enable()
+        here.wait_stream(side)
 
 
 def packed_experts_decode_graphed(layer, x, pairs, routing_weights, shared, act_fn, tail):
-    """`packed_experts_decode` (and, `tail` True, the forward's epilogue) through one CUDA graph
-    per MoE layer -- or None: this call is not the graph's, run the eager path.
+    """`packed_experts_decode` (and, `tail` True, the forward's epilogue `_tail`) as one CUDA graph
+    per MoE layer, or None when this call is not the graph's (the caller then runs eagerly).
 
-    The caller passes only inputs whose addresses hold from call to call.  Returns a STATIC
-    tensor the layer's next call overwrites: the fp32 sum [1, hidden] (`tail` False) or
-    `_tail(sum, x.dtype, shared)` (`tail` True)."""
-    if layer in _GRAPH_REFUSED:
+    Inputs must keep their addresses from call to call (static tensors); a new address records a
+    new graph.  Returns a STATIC tensor that the layer's next call overwrites: the fp32 sum
+    [1, hidden] (`tail` False) or the epilogue's result (`tail` True)."""
+    if layer in _GRAPH_OFF or not pairs:
         return None
-    blob0 = pairs[0][0]
-    geom = blob0.get("geom")
-    if geom is None or "flat" not in blob0 or any(
-            blob.get("geom") != geom or "flat" not in blob for blob, _slot in pairs[1:]):
-        return None
-    if not (x.is_contiguous() and routing_weights.is_contiguous()):
-        _warn_skip("a non-contiguous expert input or routing-weight tensor")
-        return None
-    if tail and shared is not None and shared.dtype != x.dtype:
-        _warn_skip(f"the shared expert's output is {shared.dtype}, the activations {x.dtype}")
+    entries = [b for b, _s in pairs]
+    if any("flat" not in b or b.get("geom") is None for b in entries):
         return None
     try:
-        _one_geometry([b for b, _s in pairs], "packed_experts_decode_graphed")
+        _one_geometry(entries, "decode graph")
         _checked(x, pairs, routing_weights, act_fn)
     except NotImplementedError:
         return None
-    vals = _pairs_table(pairs)
-    key = (len(pairs), x.data_ptr(), routing_weights.data_ptr(), routing_weights.dtype,
-           0 if shared is None else shared.data_ptr(), tail, geom, x.dtype,
-           blob0["flat"]["scale"].dtype, "zero" in blob0["flat"])
+    if not (x.is_contiguous() and routing_weights.is_contiguous()):
+        _graph_note("calls with strided activations or routing weights run eagerly")
+        return None
+    if tail and shared is not None and shared.dtype != x.dtype:
+        _graph_note(f"a shared-expert output in {shared.dtype} with {x.dtype} activations runs eagerly")
+        return None
+    geom_s = _geom_struct(*_blob_key(entries[0]))
+    key = (len(pairs), x.data_ptr(), routing_weights.data_ptr(), routing_weights.dtype, x.dtype,
+           None if shared is None else shared.data_ptr(), bool(tail), _blob_key(entries[0]), geom_s)
+    payload = _pairs_table(pairs)
     g = _GRAPHS.get(layer)
     if g is not None and g.key == key:
-        g.done.synchronize()            # this layer's last replay has read the table
-        g.host.copy_(vals)
-        g.graph.replay()
-        g.done.record()
+        with torch.cuda.device(x.device):
+            _stage(payload, x.device, into=g.table)
+            g.graph.replay()
         g.replays += 1
         GRAPH_STATS["replays"] += 1
-        return g.result if tail else g.out
+        return g.result
     if g is not None:
-        del _GRAPHS[layer]
-        if g.replays == 0:
-            GRAPH_STATS["replaced_unreplayed"] += 1
+        GRAPH_STATS["recorded_unused"] += g.replays == 0
+        del _GRAPHS[layer]          # its buffers go before the next recording allocates
         del g
-    return _capture(layer, key, x, pairs, routing_weights, shared, tail, vals)
+    return _record(layer, key, x, pairs, routing_weights, shared, tail, payload)
 
 
-def _capture(layer, key, x, pairs, rw, shared, tail, vals):
+def _record(layer, key, x, pairs, rw, shared, tail, payload):
     dev = x.device
-    n = len(pairs)
-    geom_s = _geom_struct(*_blob_key(pairs[0][0]))
     with torch.cuda.device(dev):
-        ref_out = torch.empty(x.shape, dtype=torch.float32, device=dev)
-        _launch(x, pairs, rw, ref_out)
-        ref = _tail(ref_out, x.dtype, shared) if tail else ref_out
-        g = _LayerGraph()
-        graph = torch.cuda.CUDAGraph()
-        pool = torch.cuda.graph_pool_handle()
-        was = gc.isenabled()
-        gc.disable()
+        want = None
+        if layer not in _GRAPH_VERIFIED or dev not in _KERNELS_READY:
+            # the eager launch the first recording is held to (it also sets the kernels'
+            # attributes up outside any capture)
+            eager = torch.empty(x.shape, dtype=torch.float32, device=dev)
+            _launch(x, pairs, rw, eager)
+            want = _tail(eager, x.dtype, shared) if tail else eager
+            _KERNELS_READY.add(dev)
         try:
-            g.key, g.replays = key, 0
-            g.host = torch.empty(len(vals), dtype=torch.int64, pin_memory=True)
-            g.host.copy_(vals)
-            g.tbl = torch.empty(len(vals), dtype=torch.int64, device=dev)
-            c_probe = _lib.MoeCall()
-            c_probe.geom = ctypes.pointer(geom_s)
-            c_probe.n_tokens, c_probe.top_k, c_probe.n_experts = 1, n, n
-            need = _lib.lib().vy_moe_workspace_size(ctypes.byref(c_probe), PATH_DECODE)
-            g.ws = torch.empty(max(need, 256), dtype=torch.uint8, device=dev)
-            g.out = torch.empty(x.shape, dtype=torch.float32, device=dev)
-            g.tmp = torch.empty(x.shape, dtype=x.dtype, device=dev) if tail else None
-            g.result = (torch.empty(x.shape, dtype=x.dtype, device=dev)
-                        if tail and shared is not None else g.tmp)
-            g.done = torch.cuda.Event()
-            side = _GRAPH_STREAMS.get(dev)
-            if side is None:
-                side = _GRAPH_STREAMS[dev] = torch.cuda.Stream(device=dev)
-            cur = torch.cuda.current_stream(dev)
-            side.wait_stream(cur)
-            with torch.cuda.stream(side), torch.no_grad():
-                graph.capture_begin(pool=pool, capture_error_mode="thread_local")
-                try:
-                    g.tbl.copy_(g.host, non_blocking=True)
-                    _decode_from_table(x, n, geom_s, g.tbl, rw, g.out, workspace=g.ws)
-                    if tail:
-                        g.tmp.copy_(g.out)
-                        if shared is not None:
-                            torch.add(g.tmp, shared, out=g.result)
-                finally:
-                    graph.capture_end()
-            cur.wait_stream(side)
-            g.graph = graph
-            graph.replay()
-            got = g.result if tail else g.out
-            same = torch.equal(got, ref)
-        except Exception as exc:
-            first = (str(exc).splitlines() or [""])[0][:200]
-            _refuse_graph(layer, f"capture failed: {type(exc).__name__}: {first}")
-            return ref
-        finally:
-            if was:
-                gc.enable()
-        if not same:
-            _refuse_graph(layer, "its replay disagrees bitwise with the eager launch")
-            return ref
-        g.done.record()
-        _GRAPHS[layer] = g
-        GRAPH_STATS["captures"] += 1
-        return got
+            g = _DecodeGraph(key, x, len(pairs), shared, tail)
+            g.record(x, rw, shared)
+            _stage(payload, dev, into=g.table)
+            g.graph.replay()
+            got = g.result
+            if layer not in _GRAPH_VERIFIED:
+                if not torch.equal(got, want):
+                    _graph_off(layer, "its first replay does not match the eager launch bit for bit")
+                    return want
+                _GRAPH_VERIFIED.add(layer)
+        except Exception as exc:     # the recording failed: this layer keeps the eager path
+            first = str(exc).splitlines()[0][:160] if str(exc) else ""
+            _graph_off(layer, f"recording raised {type(exc).__name__}: {first}")
+            return want if want is not None else _eager_result(x, pairs, rw, shared, tail)
+    _GRAPHS[layer] = g
+    GRAPH_STATS["recorded"] += 1
+    return got
+
+
+def _eager_result(x, pairs, rw, shared, tail):
+    out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    _launch(x, pairs, rw, out)
+    return _tail(out, x.dtype, shared) if tail else out
 
 
 # ── prefill ──────────────────────────────────────────────────────────────────────────────
@@ -475,7 +481,7 @@ def _prefill_launch(x, eidx_cpu, routing_weights, blobs, out, plan=None, path=PA
     n_tok, top_k = eidx_cpu.shape
     vals, u, entries = _prefill_payload(eidx_cpu, blobs)
     geom_s = _geom_struct(*_blob_key(entries[0]))
-    tbl = _PF_TABLES.put(vals, dev)
+    tbl = _stage(vals, dev)
     ids = tbl[3 * u:].view(torch.int32)
     if x.stride(-1) != 1:
         x = x.contiguous()
@@ -749,113 +755,130 @@ def combine(contrib, expert_ids, out=None):
     return out
 
 
-# ── install (vaayu/packed_expert_kernels.py:864-1012) ────────────────────────────────────────
+# ── install into a Vaayu engine ──────────────────────────────────────────────────────────
+#
+# The engine calls `install_packed_expert_kernels(self)` once at load; it routes the blocks
+# whose forward is the fused sparse one.  Decision, in order: a CUDA model on the current device,
+# the library present, SiLU experts, one real expert of the first fused block readable as a blob
+# whose geometry and dtypes the kernels take (decode, for every fused block); then prefill for
+# each block whose own first expert has the same format and whose expert set fits a quarter of
+# the device's free memory at install time (a prefill call holds every routed expert at once).
+
+_FUSED_FORWARD = "_make_fused_sparse_forward"    # the engine's name for the fused MoE forward
+
 
 def _is_silu(act_fn, device, dtype) -> bool:
-    """Behavioural: does the experts' activation compute SiLU? (the kernels hardcode it)"""
+    """Does the experts' activation compute SiLU on this dtype? (the kernels hardcode it)"""
     if act_fn is None:
         return False
-    t = torch.linspace(-8.0, 8.0, 257, device=device).to(dtype)
+    probe = torch.linspace(-12.0, 12.0, 301, device=device).to(dtype)
     try:
-        return torch.equal(act_fn(t), torch.nn.functional.silu(t))
+        return torch.equal(act_fn(probe), torch.nn.functional.silu(probe))
     except Exception:
         return False
 
 
-def _one_real_blob(vaayu_ref, block, device, quiet=False):
-    """The blob of `block`'s lowest-numbered expert.  Inside Vaayu the engine's own loader
-    reads it off the checkpoint; any other host supplies `vaayu_ref.packed_probe_blob(block,
-    device)`."""
-    probe = getattr(vaayu_ref, "packed_probe_blob", None)
-    why = "its projections are packed at different bit widths or group sizes"
+def _layer_file_blob(checkpoint_path, layer_name, device):
+    """The blob of the lowest-numbered expert stored in `<checkpoint_path>/<layer_name>.safetensors`,
+    read with this package's checkpoint reader (that expert's tensors only), or None."""
+    from .checkpoint import Checkpoint
+    path = os.path.join(str(checkpoint_path), f"{layer_name}.safetensors")
+    if not os.path.isfile(path):
+        return None
+    ck = Checkpoint(path)
     try:
-        if callable(probe):
-            blob = probe(block, device)
-        else:
-            from vaayu.moe_patch import (_group_packed_tensors_by_weight, _packed_roles_complete,
-                                         _upload_packed_expert)
-            from vaayu.persist.safetensor_model_persister import load_expert_sparse
-            from pathlib import Path
-            from .moe_patch import build_expert_blob
-            metas = vaayu_ref._expert_offset_index.index.get(block.layer_name, {})
-            if not metas:
-                return None
-            raw = load_expert_sparse(str(Path(vaayu_ref.checkpoint_path) / f"{block.layer_name}.safetensors"),
-                                     metas[min(metas)])
-            packed = _group_packed_tensors_by_weight(raw)
-            if not packed["gate"] or not _packed_roles_complete(packed):
-                return None
-            blob = build_expert_blob(_upload_packed_expert(packed, device))
-    except NotImplementedError as exc:
-        blob, why = None, str(exc)
-    if blob is None and not quiet:
-        print(f"[Vaayu] WARNING: fused packed-expert decode kernel not installed: {why}")
-    return blob
+        found = ck.lowest_expert()
+        return None if found is None else ck.expert_blob(found[0], found[1], device)
+    finally:
+        ck.close()
+
+
+def _probe_blob(vaayu_ref, block, device):
+    """One real expert of `block` as a blob: the host's own `packed_probe_blob(block, device)` when
+    it has one, else the block's layer file under `checkpoint_path`.  NotImplementedError from
+    `build_expert_blob` (act-order, mixed widths) propagates."""
+    probe = getattr(vaayu_ref, "packed_probe_blob", None)
+    if callable(probe):
+        return probe(block, device)
+    ckpt, name = getattr(vaayu_ref, "checkpoint_path", None), getattr(block, "layer_name", None)
+    if ckpt is None or name is None:
+        return None
+    return _layer_file_blob(ckpt, name, device)
+
+
+def _format_of(blob):
+    return blob["geom"], blob["flat"]["scale"].dtype, "zero" in blob["flat"]
+
+
+def _install_refusal(vaayu_ref, device, dtype, block):
+    """Why the kernels cannot serve this model at all, or None."""
+    current = torch.cuda.current_device()
+    if device.index is not None and device.index != current:
+        return (f"the model runs on {device}, not the current CUDA device cuda:{current} "
+                "(the kernels launch on the current device)")
+    act_fn = getattr(getattr(block.moe_module, block.experts_attr, None), "act_fn", None)
+    if not _is_silu(act_fn, device, dtype):
+        return "the experts' activation is not SiLU"
+    return None
 
 
 def install_packed_expert_kernels(vaayu_ref) -> bool:
-    """Route the fused pack-quantized MoE blocks through the kernels -- one-token decode of every
-    such block, and the prefill calls of each block whose geometry matches -- if the kernels can
-    take this model's geometry on this device.  Sets `vaayu_ref._packed_moe_kernel` (the
-    geometry) and `vaayu_ref._packed_moe_prefill_kernel` (frozenset of eligible `layer_idx`).
-    Returns whether the decode kernel was installed; a refusal is reported with a WARNING and
-    leaves the engine's own path in place."""
-    device = str(vaayu_ref.running_device)
-    if torch.device(device).type != "cuda" or not _lib.LIB_PATH.exists():
+    """Serve the engine's fused pack-quantized MoE blocks with these kernels: one-token decode of
+    every such block, and prefill of each block whose experts share the first block's format.
+    Sets `vaayu_ref._packed_moe_kernel` (the geometry served) and, when any block qualifies,
+    `vaayu_ref._packed_moe_prefill_kernel` (frozenset of their `layer_idx`).  Returns whether the
+    decode kernels were installed; when they are not, the reason is logged and the engine keeps
+    its own path."""
+    device = torch.device(str(vaayu_ref.running_device))
+    if device.type != "cuda" or not _lib.LIB_PATH.exists():
         return False
     blocks = [b for b in (getattr(vaayu_ref, "_moe_blocks", None) or [])
-              if getattr(b, "forward_name", None) == "_make_fused_sparse_forward"]
+              if getattr(b, "forward_name", None) == _FUSED_FORWARD]
     if not blocks:
         return False
-    dev_index = torch.device(device).index
-    if dev_index is not None and dev_index != torch.cuda.current_device():
-        print(f"[Vaayu] WARNING: fused packed-expert decode kernel not installed: model "
-              f"device {device} is not the current CUDA device "
-              f"({torch.cuda.current_device()}); decode keeps the stock per-expert path")
-        return False
-    block, dtype = blocks[0], vaayu_ref.running_dtype
-    act_fn = getattr(getattr(block.moe_module, block.experts_attr, None), "act_fn", None)
-    if not _is_silu(act_fn, device, dtype):
-        print("[Vaayu] fused packed-expert decode kernel not used: the experts' activation "
-              "is not SiLU")
-        return False
-    blob = _one_real_blob(vaayu_ref, block, device)
-    if blob is None:
-        return False
-    scale_dtype = blob["flat"]["scale"].dtype
-    bad = [why for why in (_unsupported(blob["geom"], dtype, scale_dtype, w)
-                           for w in (torch.float32, dtype)) if why]
-    if bad:
-        print(f"[Vaayu] WARNING: fused packed-expert decode kernel refused ({bad[0]}); these "
-              f"experts stay on the stock per-expert path")
+    dtype, first = vaayu_ref.running_dtype, blocks[0]
+    why, blob = _install_refusal(vaayu_ref, device, dtype, first), None
+    if why is None:
+        try:
+            blob = _probe_blob(vaayu_ref, first, device)
+        except NotImplementedError as exc:
+            why = str(exc)
+        if blob is None and why is None:
+            why = f"no pack-quantized expert of layer {first.layer_idx} could be read as a blob"
+    if why is None:
+        why = next((w for w in (_unsupported(blob["geom"], dtype, blob["flat"]["scale"].dtype, rw_dtype)
+                                for rw_dtype in (torch.float32, dtype)) if w), None)
+    if why is not None:
+        log.warning("vaayu_b200: fused expert kernels not installed: %s; the engine keeps its own path", why)
         return False
     vaayu_ref._packed_moe_kernel = blob["geom"]
     bits, gs, _roles = blob["geom"]
-    print(f"[Vaayu] fused packed-expert decode kernel on {len(blocks)} MoE layers "
-          f"({bits}-bit, group {gs})")
-    checked = (blob["geom"], scale_dtype, "zero" in blob["flat"])
-    eligible, skipped = [], {}
+    log.info("vaayu_b200: fused int%d expert decode (group %d) on %d MoE layers", bits, gs, len(blocks))
+
+    fmt, blob_bytes = _format_of(blob), sum(t.numel() * t.element_size() for t in blob["flat"].values())
+    budget = torch.cuda.mem_get_info(device)[0] // 4
+    eligible, left_out = [], collections.defaultdict(list)
     for b in blocks:
-        one = blob if b is block else _one_real_blob(vaayu_ref, b, device, quiet=True)
-        if one is None:
-            why = "experts not pack-quantized, or packed with no fused pass"
-        elif (one["geom"], one["flat"]["scale"].dtype, "zero" in one["flat"]) != checked:
-            why = "a different geometry or scale dtype than the checked layer"
-        else:
-            eligible.append(b.layer_idx)
-            continue
-        skipped.setdefault(why, []).append(b.layer_idx)
-    if not eligible:
-        print(f"[Vaayu] WARNING: fused packed-expert prefill kernel not installed: "
-              f"{'; '.join(skipped)}; prefill keeps the per-expert path")
-        return True
-    vaayu_ref._packed_moe_prefill_kernel = frozenset(eligible)
-    print(f"[Vaayu] fused packed-expert prefill kernel on {len(eligible)} MoE layers "
-          f"({bits}-bit, group {gs})")
-    if skipped:
-        left_out = sorted(i for idxs in skipped.values() for i in idxs)
-        print(f"[Vaayu] WARNING: fused packed-expert prefill kernel not used on "
-              f"{len(left_out)} of {len(blocks)} MoE layers (layer indices "
-              f"{', '.join(map(str, left_out))}): {'; '.join(skipped)}; prefill keeps the "
-              f"per-expert path there")
+        try:
+            one = blob if b is first else _probe_blob(vaayu_ref, b, device)
+            reason = "no pack-quantized expert could be read as a blob"
+        except NotImplementedError as exc:
+            one, reason = None, str(exc)
+        if one is not None:
+            n_exp = int(getattr(getattr(b.moe_module, b.experts_attr, None), "num_experts", 0) or 0)
+            if _format_of(one) != fmt:
+                reason = "its experts differ in geometry or format from layer %d's" % first.layer_idx
+            elif n_exp and n_exp * blob_bytes > budget:
+                reason = (f"its {n_exp} experts ({n_exp * blob_bytes / 2**30:.2f} GiB) exceed a quarter "
+                          f"of the free device memory at install ({budget / 2**30:.2f} GiB)")
+            else:
+                eligible.append(b.layer_idx)
+                continue
+        left_out[reason].append(b.layer_idx)
+    if eligible:
+        vaayu_ref._packed_moe_prefill_kernel = frozenset(eligible)
+        log.info("vaayu_b200: fused int%d expert prefill on %d of %d MoE layers", bits, len(eligible), len(blocks))
+    for reason, idxs in left_out.items():
+        log.warning("vaayu_b200: prefill of layers %s stays on the engine's path: %s",
+                    ", ".join(map(str, idxs)), reason)
     return True
