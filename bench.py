@@ -46,6 +46,9 @@ CFG3 = dict(name="cfg3: DeepSeek-V3-shaped int4 MoE layer (256 routed experts, t
             group=128, shared=1, zeros=True)   # zero points U{0..15} per (row, group), as configuration 3 asks
 PREFILL = dict(name="cfg2: Mixtral-8x7B-shaped int4 MoE layer, prefill", hidden=4096, inter=14336,
                experts=8, top_k=2, tokens=2048, group=128, skew=0.9)
+CFG3_PREFILL = dict(name="cfg3: DeepSeek-V3-shaped int4 MoE layer (256 routed experts, top-8, 1 shared), "
+                         "expert-parallel prefill", hidden=7168, inter=2048, experts=256, top_k=8, tokens=4096,
+                    group=128, shared=1, zeros=True)
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_HBM = 6650.0
 FALLBACK_BF16 = 1590.0
@@ -380,6 +383,342 @@ def time_steps(fn, steps, device):
     return start.elapsed_time(end) / steps
 
 
+def static_config(wl, world, layers, mode):
+    """The workload description shared by both arms' JSON lines (no run-time measurements)."""
+    T, E = wl["tokens"], wl["experts"]
+    cfg = {"workload": wl["name"], "hidden": wl["hidden"], "expert_intermediate": wl["inter"],
+           "experts": E, "top_k": wl["top_k"], "group_size": wl["group"], "layers_rotated": layers,
+           "zero_points": bool(wl.get("zeros")), "shared_experts": wl.get("shared", 0)}
+    if mode == "decode":
+        cfg["tokens_per_gpu"] = T
+        cfg["l2"] = f"inputs larger than L2: steps rotate over {layers} layers, each step reads its routed experts' weights"
+        cfg["parallelism"] = ("ep1" if world == 1 else
+                              f"ep{world}: {E // world} experts per GPU; replicate mode (one NCCL all-gather of "
+                              f"the tokens, one all-to-all of per-token partial sums, rank-ordered combine)")
+    else:
+        cfg["tokens_total"] = T
+        cfg["tokens_per_gpu"] = T // world
+        if wl.get("skew"):
+            cfg["router_skew"] = f"logits + linspace(0, {wl['skew']}, {E})"
+        cfg["l2"] = f"inputs larger than L2: steps rotate over {layers} layers of {E} experts"
+        cfg["parallelism"] = ("ep1" if world == 1 else
+                              f"ep{world}: {E // world} experts per GPU ({wl.get('placement', 'contiguous')}); "
+                              f"dispatch mode (bounded-capacity all-to-alls of rows and contributions, "
+                              f"ascending-global-expert combine)")
+    return cfg
+
+
+def staged_call(table, x, ids, w, device, path, workspace, stage_names, **kw):
+    """One moe_forward-equivalent call with the library's per-stage events: {stage: ms}."""
+    import ctypes
+
+    from vaayu_b200 import packed_expert_kernels as pk
+    n = 5 if path == 1 else 4
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+    for e in evs:
+        e.record()                      # torch creates the CUDA event on its first record
+    torch.cuda.synchronize(device)
+    handles = (ctypes.c_void_p * n)(*[e.cuda_event for e in evs])
+    T, K = ids.shape
+    out = kw.pop("out", None)
+    contrib = kw.pop("contrib", None)
+    c = pk._make_call(table.geom_s, x, T, K, table.n_experts, table.table.data_ptr(), ids.data_ptr(),
+                      6 if ids.dtype == torch.int64 else 5, w, w.stride(0), w.stride(1), None, out, contrib, None)
+    c.ids_row_stride = ids.stride(0)
+    for k, v in kw.items():
+        setattr(c, k, v)
+    c.stage_events, c.n_stage_events = ctypes.cast(handles, ctypes.c_void_p), n
+    pk._enqueue(c, path, device, workspace)
+    torch.cuda.synchronize(device)
+    marks = [0, 1, 2, 4, 3] if path == 1 else [0, 1, 2, 3]
+    return {name: evs[marks[i]].elapsed_time(evs[marks[i + 1]]) for i, name in enumerate(stage_names)}
+
+
+# ── expert-parallel arms (N GPUs of one node; also configuration 3 on one GPU) ─────────────────
+
+def _rank0_decode_roofline(layer, wl, world, device):
+    """Rank 0's gate/up kernel over its last gathered batch, timed alone with the library's stage
+    events: (achieved GB/s over the local routed experts' gate/up bytes + the gathered x, stages)."""
+    b = next(v for k, v in layer._bufs.items() if not (isinstance(k, tuple) and k and k[0] == "dispatch"))
+    T, K, H = wl["tokens"], wl["top_k"], wl["hidden"]
+    xb = b["xb"]
+    xa = b["recv"][:, :xb].view(torch.bfloat16)
+    ga = b["recv"][:, xb:xb + 4 * K].view(torch.int32)
+    wa = b["recv"][:, xb + 4 * K:xb + 4 * K + b["wb"]].view(torch.float32)
+    part = torch.empty(world * T, H, dtype=torch.float32, device=device)
+    st = staged_call(layer.table, xa, ga, wa, device, 0, b["ws"], ("plan", "gate_up", "down"), out=part,
+                     expert_base=layer.lo, col_blocks=b["nb"])
+    local = sorted({int(e) - layer.lo for e in ga.reshape(-1).tolist() if layer.lo <= int(e) < layer.lo + layer.per_rank})
+    gu_bytes = gate_up_bytes(layer.table, torch.tensor(local, dtype=torch.int64)) + world * T * H * 2
+    return gu_bytes / (st["gate_up"] / 1e3) / 1e9, st
+
+
+def _capture_steps(L, layer_step, rank, device):
+    """One CUDA graph per layer step (their collectives included); [] when capture fails here."""
+    graphs = []
+    try:
+        for l in range(L):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                layer_step(l)
+            graphs.append(g)
+        torch.cuda.synchronize(device)
+    except Exception as e:  # noqa: BLE001 - report and run eagerly
+        graphs = []
+        if rank == 0:
+            print(f"# EP graph capture unavailable, eager steps: {e}", flush=True)
+    return graphs
+
+
+def _device_record(batches, device):
+    """Each layer's inputs as views of one device record (the end-to-end step fills it with one
+    copy): (record bytes, the views function, the records, each record's views)."""
+    nbytes, views = record_layout(batches[0])
+    drecs = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in batches]
+    dviews = []
+    for rec, b in zip(drecs, batches):
+        vs = views(rec)
+        for v, src in zip(vs, b):
+            v.copy_(src)
+        dviews.append(vs)
+    return nbytes, views, drecs, dviews
+
+
+def run_ep_decode(args, rank, world, local, wl):
+    """`wl` (configuration 1 or 3) at `wl['tokens']` tokens per rank (weak scaling), the routed
+    experts sharded E/N per rank, steps rotating over `args.layers` layers, each layer step one CUDA
+    graph.  A workload with `shared` experts replicates them on every rank, applies them to the
+    rank's own tokens and adds their output in bf16 (the model epilogue: out.to(bf16) +
+    shared.to(bf16)); on one GPU the shared expert rides in the layer call."""
+    from vaayu_b200.ep import ExpertParallelLayer
+    from vaayu_b200.packed_expert_kernels import (PATH_DECODE, ExpertTable, _with_shared, moe_forward_with_shared,
+                                                  moe_workspace_bytes, shared_expert_forward)
+    device = torch.device("cuda", local)
+    E, T, K, H = wl["experts"], wl["tokens"], wl["top_k"], wl["hidden"]
+    per = E // world
+    L = args.layers
+    layers = [ExpertParallelLayer(make_layer(1000 * l, wl, device, (rank * per, (rank + 1) * per)), E,
+                                  col_blocks=getattr(args, "ep_col_blocks", None)) for l in range(L)]
+    batches = [tuple(v.to(device) for v in make_tokens(l * 97 + rank, wl, T, device)) for l in range(L)]
+    out = torch.empty(T, H, dtype=torch.float32, device=device)
+    shared = None
+    if wl.get("shared"):
+        shared = [ExpertTable(make_layer(5000 + l, dict(wl, experts=1), device)) for l in range(L)]
+        sh_out = torch.empty(T, H, dtype=torch.float32, device=device)
+        sh_ws = torch.empty(moe_workspace_bytes(shared[0], T, 1, path=PATH_DECODE), dtype=torch.uint8, device=device)
+        result = torch.empty(T, H, dtype=torch.bfloat16, device=device)
+        if world == 1:
+            fused_ws = torch.empty(moe_workspace_bytes(_with_shared(layers[0].table, shared[0]), T, K + 1,
+                                                       path=PATH_DECODE), dtype=torch.uint8, device=device)
+
+    def layer_step(l, x, w, idx):       # the device record's views: activations, weights, ids
+        if shared is not None and world == 1:
+            moe_forward_with_shared(x, idx, w, layers[l].table, shared[l], out=out, result=result,
+                                    path=PATH_DECODE, workspace=fused_ws)
+            return
+        layers[l].forward(x, idx, w, out)
+        if shared is not None:
+            shared_expert_forward(x, shared[l], out=sh_out, workspace=sh_ws)
+            torch.add(out.to(torch.bfloat16), sh_out.to(torch.bfloat16), out=result)
+
+    nbytes, views, drecs, dviews = _device_record(batches, device)
+    for l in range(L):
+        for _ in range(2):
+            layer_step(l, *dviews[l])
+    torch.cuda.synchronize(device)
+    barrier(world)
+    graphs = _capture_steps(L, lambda l: layer_step(l, *dviews[l]), rank, device)
+    barrier(world)
+
+    def step(i):
+        graphs[i % L].replay() if graphs else layer_step(i % L, *dviews[i % L])
+
+    for i in range(args.warmup):
+        step(i)
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        ms = time_steps(step, args.steps, device)
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+
+    pin = [pinned_record(b, nbytes, views) for b in batches]
+    out_h = torch.empty(T, H, dtype=torch.float32 if shared is None else torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        drecs[i % L].copy_(pin[i % L], non_blocking=True)
+        step(i)
+        out_h.copy_(out if shared is None else result, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    barrier(world)
+    e2e_ms = max_over_ranks(time_steps(e2e_step, args.steps, device), world)
+    barrier(world)
+    used_graphs = bool(graphs)
+    del graphs               # graphs holding NCCL calls go before the process group does
+    torch.cuda.synchronize(device)
+    peak, peak_kind = hbm_peak()
+    roof, cpu, st = None, None, None
+    if rank == 0:
+        if world > 1:
+            achieved, st = _rank0_decode_roofline(layers[0], wl, world, device)
+        else:               # the routed layer alone (the shared expert's slot left out)
+            x0, w0, i0 = dviews[0]
+            st = staged_call(layers[0].table, x0, i0, w0, device, 0, None, ("plan", "gate_up", "down"), out=out)
+            achieved = (gate_up_bytes(layers[0].table, i0) + T * H * 2) / (st["gate_up"] / 1e3) / 1e9
+        roof = {"kernel": "gate_up_kernel (rank 0, its gathered batch)", "bound": "hbm", "achieved": achieved,
+                "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                "traffic": None, "launch_ms": st["gate_up"]}
+        if not args.no_cpu:
+            full = ExpertTable(make_layer(0, wl, device)) if world > 1 else layers[0].table
+            cpu = cpu_baseline(full, make_tokens(0, wl, T, device), wl)
+            del full
+    uniq = statistics.mean(len(set(b[2].reshape(-1).tolist())) for b in batches)
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": T * world / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1))",
+            "config": static_config(wl, world, L, "decode"),
+            "run": {"routed_experts_per_rank_batch": uniq, "cuda_graphs": used_graphs, "stage_ms": st},
+            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": out_h.numel() * out_h.element_size(),
+                    "ms_per_step": e2e_ms},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            # plan, gate/up, down and the rank-ordered sum (one GPU: the layer's combine), plus the
+            # separate shared-expert call's four on several GPUs
+            "gpu_launches": (4 + (4 if shared is not None and world > 1 else 0)) * args.steps,
+            "clocks": clocks.summary(),
+        }))
+
+
+def run_ep_prefill(args, rank, world, local, wl):
+    """A prefill workload at any N (strong scaling): `wl['tokens']` tokens in total, rank r holding
+    tokens [r T/N, (r + 1) T/N) and its share of the experts (`wl['placement']`); dispatch mode --
+    the rows to their experts' ranks by bounded-capacity all-to-alls (no host round trip after the
+    first call), the local tcgen05 prefill GEMMs, contributions back by the reverse all-to-all, the
+    ascending-global-expert combine on each token's home rank.  A `shared` expert runs on each rank's
+    own tokens (prefill kernels) and joins in bf16.  Each layer step is one CUDA graph."""
+    from vaayu_b200 import synthetic
+    from vaayu_b200.ep import ExpertParallelLayer
+    from vaayu_b200.packed_expert_kernels import PATH_PREFILL, ExpertTable, moe_forward, moe_workspace_bytes
+    device = torch.device("cuda", local)
+    E, T, K, H, I = wl["experts"], wl["tokens"], wl["top_k"], wl["hidden"], wl["inter"]
+    if E % world or T % world:
+        raise ValueError(f"{wl['name']} splits {E} experts and {T} tokens evenly: not over {world} GPUs")
+    per, tl = E // world, T // world
+    L = 2
+    placement = wl.get("placement", "contiguous")
+    keep = range(rank, E, world) if placement == "interleaved" else range(rank * per, (rank + 1) * per)
+    layers = [ExpertParallelLayer(make_layer(2000 + l, wl, device, keep=keep), E, mode="dispatch",
+                                  placement=placement, path=PATH_PREFILL) for l in range(L)]
+    batches = []
+    for l in range(L):
+        g = torch.Generator(device=device).manual_seed(20_000 + l)
+        x, w, idx = synthetic.make_tokens(T, H, E, K, g, skew=wl.get("skew", 0.0))
+        sl = slice(rank * tl, (rank + 1) * tl)
+        batches.append((x[sl].contiguous(), w[sl].contiguous(), idx[sl].contiguous()))
+    out = torch.empty(tl, H, dtype=torch.float32, device=device)
+    shared = None
+    if wl.get("shared"):
+        shared = [ExpertTable(make_layer(5000 + l, dict(wl, experts=1), device)) for l in range(L)]
+        sh_ids = torch.zeros(tl, 1, dtype=torch.int32, device=device)
+        sh_w = torch.ones(tl, 1, dtype=torch.float32, device=device)
+        sh_out = torch.empty(tl, H, dtype=torch.float32, device=device)
+        sh_ws = torch.empty(moe_workspace_bytes(shared[0], tl, 1, path=PATH_PREFILL), dtype=torch.uint8, device=device)
+        result = torch.empty(tl, H, dtype=torch.bfloat16, device=device)
+    nbytes, views, drecs, dviews = _device_record(batches, device)
+
+    def layer_step(l):
+        xv, wv, iv = dviews[l]
+        layers[l].forward(xv, iv, wv, out)
+        if shared is not None:
+            moe_forward(xv, sh_ids, sh_w, shared[l], out=sh_out, path=PATH_PREFILL, workspace=sh_ws)
+            torch.add(out.to(torch.bfloat16), sh_out.to(torch.bfloat16), out=result)
+
+    for l in range(L):
+        for _ in range(2):
+            layer_step(l)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    graphs = _capture_steps(L, layer_step, rank, device)
+    barrier(world)
+
+    def step(i):
+        graphs[i % L].replay() if graphs else layer_step(i % L)
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    steps = max(5, min(args.steps, 20))
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        ms = time_steps(step, steps, device)
+    barrier(world)
+    ms = max_over_ranks(ms, world)
+
+    pin = [pinned_record(b, nbytes, views) for b in batches]
+    out_h = torch.empty(tl, H, dtype=torch.float32 if shared is None else torch.bfloat16).pin_memory()
+
+    def e2e_step(i):
+        drecs[i % L].copy_(pin[i % L], non_blocking=True)
+        step(i)
+        out_h.copy_(out if shared is None else result, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    barrier(world)
+    e2e_ms = max_over_ranks(time_steps(e2e_step, steps, device), world)
+    barrier(world)
+    used_graphs = bool(graphs)
+    del graphs               # graphs holding NCCL calls go before the process group does
+    torch.cuda.synchronize(device)
+    overflow = any(ly.overflowed() for ly in layers)
+    flops = 2.0 * T * (K + wl.get("shared", 0)) * 3 * H * I
+    burst, sustained, src = bf16_peak()
+    roof, cpu, st = None, None, None
+    if rank == 0:
+        # rank 0's own gate/up GEMM over the rows it received in the last step, timed alone
+        ly = layers[(steps - 1) % L]
+        cap = ly._caps.get((tl, K), tl * K)
+        b = next(v for k, v in ly._bufs.items() if isinstance(k, tuple) and k and k[0] == "dispatch" and v["cap"] == cap)
+        rx, rid, rw = b["recv_x"], b["recv_id"].view(-1, 1), b["recv_w"].view(-1, 1)
+        st = staged_call(ly.table, rx, rid, rw, device, PATH_PREFILL, None,
+                         ("plan_gather", "gate_up_gemm", "down_gemm", "combine"), contrib=b["contrib"])
+        rows = int((rid >= 0).sum().item())
+        gu_tf = 2.0 * rows * 2 * H * I / (st["gate_up_gemm"] / 1e3) / 1e12
+        roof = {"kernel": "gemm_kernel<gate/up> (rank 0, the rows it received)", "bound": "tensor",
+                "achieved": gu_tf, "peak": burst, "unit": "TFLOP/s", "frac": gu_tf / burst,
+                "peak_source": f"{src} (burst)", "frac_of_sustained": gu_tf / sustained if sustained else None,
+                "traffic": None, "launch_ms": st["gate_up_gemm"], "rows": rows}
+        if not args.no_cpu:
+            full = ExpertTable(make_layer(2000, wl, device))
+            cpu = cpu_prefill_baseline(full, batches[0], tokens=16)
+            del full
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": T / (ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1))",
+            "config": static_config(wl, world, L, "prefill"),
+            "run": {"cuda_graphs": used_graphs, "dispatch_capacity_per_destination": layers[0]._caps.get((tl, K)),
+                    "dispatch_overflowed": overflow, "layer_tflops_per_gpu": flops / (ms / 1e3) / 1e12 / world,
+                    "stage_ms_rank0": st},
+            "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
+                    "d2h_bytes_per_step": out_h.numel() * out_h.element_size(), "ms_per_step": e2e_ms},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            # plan, gather, gate/up GEMM, down GEMM (contributions), the dispatch plan and pack, the
+            # home-rank combine (+ the shared expert's five)
+            "gpu_launches": (7 + (5 if shared is not None else 0)) * steps,
+            "clocks": clocks.summary(),
+        }))
+
+
 def run_ours(args, rank, world, local):
     import vaayu_b200 as vb
     from vaayu_b200 import packed_expert_kernels as pk
@@ -387,11 +726,11 @@ def run_ours(args, rank, world, local):
     wl = dict(WORKLOAD)
     T, K = wl["tokens"], wl["top_k"]
     if args.workload == "cfg2":
-        from vaayu_b200 import ep
-        return ep.run_prefill_bench(args, rank, world, local, PREFILL)
+        return run_ep_prefill(args, rank, world, local, dict(PREFILL, placement="interleaved"))
+    if args.workload == "cfg3-prefill":
+        return run_ep_prefill(args, rank, world, local, CFG3_PREFILL)
     if world > 1 or args.workload == "cfg3":
-        from vaayu_b200 import ep
-        return ep.run_bench(args, rank, world, local, CFG3 if args.workload == "cfg3" else wl)
+        return run_ep_decode(args, rank, world, local, CFG3 if args.workload == "cfg3" else wl)
     if args.profile == "prefill":
         return prefill_bench(args, device)
     if args.profile == "gemv":
@@ -520,12 +859,8 @@ def run_ours(args, rank, world, local):
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
         "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1))",
-        "config": {"workload": wl["name"], "hidden": wl["hidden"], "expert_intermediate": wl["inter"],
-                   "experts": wl["experts"], "top_k": wl["top_k"], "tokens_per_gpu": T,
-                   "group_size": wl["group"], "layers_rotated": L,
-                   "l2": f"inputs larger than L2: each step reads ~{layer_bytes / 1e6:.0f} MB of "
-                         f"expert weights, steps rotate over {L} layers",
-                   "parallelism": "ep1", "unique_experts_per_step": uniq},
+        "config": static_config(wl, world, L, "decode"),
+        "run": {"unique_experts_per_step": uniq, "expert_weight_MB_per_step": layer_bytes / 1e6},
         "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "roofline": {"kernel": "gate_up_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
@@ -586,49 +921,61 @@ def cpu_prefill_baseline(table, batch, tokens=48):
 
 
 def run_reference(args, rank, world, local):
+    """The reference's CPU implementation of the path (the C oracle port of
+    `stock_experts_prefill(linear=_linear_fp32)`) on this host's cores, over the same layers and
+    batches the default arm rotates through (rank 0's batches), with the same `config`."""
     if rank != 0:
         return
     from oracle import oracle as O
     wl = dict(WORKLOAD)
+    T, L = wl["tokens"], args.layers
     device = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    calls = []
     if device.type == "cuda":
         from vaayu_b200 import packed_expert_kernels as pk
-        table = pk.ExpertTable(make_layer(0, wl, device))
-        batch = make_tokens(0, wl, wl["tokens"], device)
+        for l in range(L):
+            table = pk.ExpertTable(make_layer(1000 * l, wl, device))
+            batch = make_tokens(l * 97 if world > 1 else l, wl, T, device)
+            calls.append((table.geom, *_oracle_inputs(table, batch)))
+            del table
+        torch.cuda.empty_cache()
     else:
-        from vaayu_b200 import synthetic
         import vaayu_b200 as vb
+        from vaayu_b200 import synthetic
 
-        class _T:
+        class _Table:
             pass
-        g = torch.Generator().manual_seed(0)
-        table = _T()
-        table.blobs = [vb.build_expert_blob(synthetic.make_expert(wl["hidden"], wl["inter"], g))
-                       for _ in range(wl["experts"])]
-        table.geom = table.blobs[0]["geom"]
-        batch = synthetic.make_tokens(wl["tokens"], wl["hidden"], wl["experts"], wl["top_k"], g)
-    experts, x, idx, w = _oracle_inputs(table, batch)
+        for l in range(L):
+            g = torch.Generator().manual_seed(l)
+            table = _Table()
+            table.blobs = [vb.build_expert_blob(synthetic.make_expert(wl["hidden"], wl["inter"], g))
+                           for _ in range(wl["experts"])]
+            table.geom = table.blobs[0]["geom"]
+            batch = synthetic.make_tokens(T, wl["hidden"], wl["experts"], wl["top_k"], g)
+            calls.append((table.geom, *_oracle_inputs(table, batch)))
     threads = os.cpu_count() or 1
-    run = lambda: O.moe_layer(table.geom, experts, x, O.BF16, idx, w, O.F32, O.F16, threads=threads)
-    for _ in range(args.warmup):
-        run()
+
+    def run(i):
+        geom, experts, x, idx, w = calls[i % L]
+        O.moe_layer(geom, experts, x, O.BF16, idx, w, O.F32, O.F16, threads=threads)
+
+    for i in range(args.warmup):
+        run(i)
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        run()
+    for i in range(args.steps):
+        run(i)
     el = time.perf_counter() - t0
     ms = el * 1e3 / args.steps
-    v = wl["tokens"] / (ms / 1e3)
-    sample = f"{args.steps} layer calls of {wl['tokens']} tokens (the full benchmark workload)"
+    v = T / (ms / 1e3)
+    sample = (f"{args.steps} layer calls of {T} tokens rotating over the {L} layers the default arm times "
+              f"(rank 0's batches), all {threads} host threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations",
-        "data": "synthetic (seeded)",
-        "config": {"workload": wl["name"], "hidden": wl["hidden"], "expert_intermediate": wl["inter"],
-                   "experts": wl["experts"], "top_k": wl["top_k"], "tokens_per_gpu": wl["tokens"],
-                   "group_size": wl["group"]},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+        "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1))",
+        "config": static_config(wl, world, L, "decode"),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
 
@@ -646,11 +993,12 @@ def main():
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the configuration-2 prefill measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
-    ap.add_argument("--workload", default="cfg1", choices=("cfg1", "cfg2", "cfg3"),
+    ap.add_argument("--workload", default="cfg1", choices=("cfg1", "cfg2", "cfg3", "cfg3-prefill"),
                     help="cfg1 (default): the headline decode workload (expert-parallel for N > 1); "
                          "cfg2: the Mixtral-shaped 2048-token prefill, experts and tokens split over N "
                          "GPUs (strong scaling, dispatch mode); cfg3: DeepSeek-V3 shape, "
-                         "expert-parallel at any N")
+                         "expert-parallel decode at any N; cfg3-prefill: the same layer, 4096 tokens "
+                         "split over N GPUs (dispatch mode)")
     ap.add_argument("--ep-col-blocks", type=int, default=None, choices=(1, 2, 4),
                     help="tokens per expert pass (x8) in the expert-parallel step; default by load")
     args = ap.parse_args()

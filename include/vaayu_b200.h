@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define VY_ABI_VERSION 3
+#define VY_ABI_VERSION 4
 
 enum vy_status {
     VY_OK = 0,
@@ -277,24 +277,30 @@ int vy_sum_ordered(const float* parts, int32_t n_parts, int64_t n, float* out, v
  *   send_x   [n_ranks * capacity, hidden] the token's activations (empty slots unwritten)
  *   slot_of_row [n_tokens * top_k]   int64 slot, -1 for a dropped row
  *   counts   [n_ranks]               int32 rows taken per destination
+ *   wanted   [n_ranks]               optional (NULL: not written): int32 rows bound for each
+ *                                    destination before the capacity cut; a caller that sizes
+ *                                    `capacity` below n_tokens * top_k detects a dropped row as
+ *                                    wanted[d] > capacity (appended in ABI version 4)
  */
 int vy_ep_dispatch_plan(const void* ids, int32_t ids_dtype, int64_t ids_row_stride, int64_t n_tokens,
                         int32_t top_k, int32_t n_ranks, int32_t experts_per_rank, int32_t placement,
                         const void* weights, int32_t w_dtype, int64_t w_tok_stride, int64_t w_slot_stride,
                         const void* x, int32_t x_dtype, int64_t x_row_stride, int64_t hidden,
                         int64_t capacity, int32_t* send_ids, float* send_w, void* send_x,
-                        int64_t* slot_of_row, int32_t* counts, void* stream);
+                        int64_t* slot_of_row, int32_t* counts, int32_t* wanted, void* stream);
 
 /*
  * Expert-parallel combine on the tokens' home rank: out[t] = sum over token t's slots, in
  * ascending GLOBAL expert id then slot (fp32), of back[slot_of_row[t * top_k + k]] -- the
  * contributions returned by the reverse all-to-all, read in place through the dispatch plan's
  * slot map (-1: none).  The order `accumulate_expert_outputs` (vaayu/moe_patch.py:914-940)
- * sums in, so the result equals one GPU's layer bit for bit.  n_tokens <= 65535.
+ * sums in, so the result equals one GPU's layer bit for bit.  expert_ids [n_tokens,
+ * ids_row_stride] (0: top_k, contiguous) -- the same ids, with the same stride, as the dispatch
+ * plan was given (ids_row_stride appended in ABI version 4).  n_tokens <= 65535.
  */
 int vy_ep_combine(const float* back, const int64_t* slot_of_row, const void* expert_ids, int32_t ids_dtype,
-                  int64_t n_tokens, int32_t top_k, int64_t hidden, float* out, int64_t out_row_stride,
-                  void* stream);
+                  int64_t ids_row_stride, int64_t n_tokens, int32_t top_k, int64_t hidden, float* out,
+                  int64_t out_row_stride, void* stream);
 
 /*
  * Error flags of the last vy_moe_decode (path 0) / vy_moe_prefill (path 1) call made with this
@@ -304,7 +310,10 @@ int vy_ep_combine(const float* back, const int64_t* slot_of_row, const void* exp
  *   VY_FLAG_TIMEOUT     a device-side barrier wait ran out (bounded, never a hang); the work item
  *                       it belonged to was abandoned and its output is not valid
  *   VY_FLAG_DRAIN       draining in-flight copies after such a timeout ran out as well
- * 0 = clean.  The routing plan of every call clears them.  No counterpart in the reference.
+ * 0 = clean.  The routing plan of every call clears them.  For a vy_moe_decode_static call, pass
+ * the same call structure with workspace NULL and path 0: the flags are read from the library's
+ * scratch array (they are the last static call's, on the current device).  No counterpart in the
+ * reference.
  */
 #define VY_FLAG_BAD_EXPERT 1
 #define VY_FLAG_TIMEOUT 4

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_error_plumbing_without_a_gpu():
     lib = _lib.lib()
-    assert lib.vy_abi_version() == 3
+    assert lib.vy_abi_version() == 4
     assert isinstance(lib.vy_last_error(), bytes)
 
 

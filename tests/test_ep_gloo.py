@@ -224,3 +224,59 @@ def test_the_dispatch_plan_files_rows_stably_by_destination(placement):
         assert torch.equal(b["send_x"][slot], x[j // k])
     for d in range(ranks):
         assert (b["send_id"][d * cap + nxt[d]:(d + 1) * cap] == -1).all()
+
+
+# ── dispatch capacity: a recorded bound, overflow flagged ────────────────────────────────────
+
+def _capacity_worker(rank, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        from oracle import oracle as O
+        from tests import helpers as TH
+        from vaayu_b200.ep import ExpertParallelLayer
+        experts, _toks = _setup()
+        per = E // 2
+        local = experts[rank * per:(rank + 1) * per]
+
+        def compute(x_rows, local_ids, w_rows):
+            _o, y = O.moe_layer(_geom(), local, TH.to_np(x_rows), O.BF16, local_ids.numpy().astype(np.int64),
+                                w_rows.reshape(-1).numpy(), O.F32, O.F16, want_y=True)
+            return torch.from_numpy(y)
+
+        def combine(rows, ids_):
+            rows, ids_ = rows.numpy(), ids_.numpy()
+            out = np.zeros((ids_.shape[0], H), np.float32)
+            for t in range(ids_.shape[0]):
+                for k in np.argsort(ids_[t], kind="stable"):
+                    out[t] = (out[t] + rows[t * K + k]).astype(np.float32)
+            return torch.from_numpy(out)
+
+        layer = ExpertParallelLayer(None, E, compute=compute, combine_fn=combine, hidden=H, mode="dispatch",
+                                    capacity_margin=1.0)
+        tokens = 32
+        gr = torch.Generator().manual_seed(40 + rank)
+        x = torch.randn(tokens, H, generator=gr).to(torch.bfloat16)
+        ids = torch.stack([torch.randperm(E, generator=gr)[:K] for _ in range(tokens)])
+        w = torch.rand(tokens, K, generator=gr) + 0.05
+        w = w / w.sum(-1, keepdim=True)
+        ref = O.moe_layer(_geom(), experts, TH.to_np(x), O.BF16, ids.numpy(), w.numpy(), O.F32, O.F16)
+        first = layer.forward(x, ids, w)                          # records the bound
+        cap = layer._caps[(tokens, K)]
+        same = np.array_equal(first.numpy(), ref) and not layer.overflowed()
+        # every row of both ranks to rank 0's experts: more rows than the recorded bound
+        crowded = torch.stack([torch.tensor([0, 1, 2]) for _ in range(tokens)])
+        layer.forward(x, crowded, w)
+        over = layer.overflowed()
+        np.save(os.path.join(result_dir, f"cap{rank}.npy"), np.array([same, cap < tokens * K, over]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dispatch_capacity_is_a_recorded_bound_and_an_overflow_is_flagged(tmp_path):
+    mp.spawn(_capacity_worker, args=(_free_port(), str(tmp_path)), nprocs=2, join=True)
+    for r in range(2):
+        same, bounded, over = np.load(tmp_path / f"cap{r}.npy")
+        assert same, f"rank {r}: the bounded exchange must equal the one-process layer"
+        assert bounded, "the recorded capacity should be below T * K for this routing"
+        assert over, f"rank {r}: the crowded call overflows rank 0's slots"

@@ -61,12 +61,14 @@ def _plan(idx, w, x, ranks, per_rank, cap):
                send_w=torch.empty(ranks * cap, device="cuda"),
                send_x=torch.empty(ranks * cap, H, dtype=x.dtype, device="cuda"),
                slot=torch.empty(n, dtype=torch.int64, device="cuda"),
-               counts=torch.empty(ranks, dtype=torch.int32, device="cuda"))
+               counts=torch.empty(ranks, dtype=torch.int32, device="cuda"),
+               wanted=torch.empty(ranks, dtype=torch.int32, device="cuda"))
     _lib.check(_lib.lib().vy_ep_dispatch_plan(
         idx.data_ptr(), _lib.DTYPE_CODE[idx.dtype], idx.stride(0), idx.shape[0], idx.shape[1], ranks, per_rank, 0,
         w.data_ptr(), _lib.DTYPE_CODE[w.dtype], w.stride(0), w.stride(1), x.data_ptr(), _lib.DTYPE_CODE[x.dtype],
         x.stride(0), H, cap, out["send_id"].data_ptr(), out["send_w"].data_ptr(), out["send_x"].data_ptr(),
-        out["slot"].data_ptr(), out["counts"].data_ptr(), _lib.stream_of(x.device)), "vy_ep_dispatch_plan")
+        out["slot"].data_ptr(), out["counts"].data_ptr(), out["wanted"].data_ptr(), _lib.stream_of(x.device)),
+        "vy_ep_dispatch_plan")
     return out
 
 
@@ -83,6 +85,7 @@ def test_ids_outside_the_experts_and_rows_past_a_full_destination_are_dropped():
     assert slot[kept0[:5]].tolist() == [0, 1, 2, 3, 4]         # first come, in row order
     assert (slot[kept0[5:]] == -1).all()
     assert out["counts"].cpu().tolist()[0] == 5
+    assert out["wanted"].cpu().tolist()[0] == len(kept0) > 5      # the overflow stays visible
     assert (out["send_id"][:5] >= 0).all()
 
 
@@ -97,13 +100,21 @@ def test_the_combine_reads_the_returned_rows_through_the_slot_map():
     slot[5] = -1
     out = torch.empty(tokens, H, device="cuda")
     _lib.check(_lib.lib().vy_ep_combine(back.data_ptr(), slot.data_ptr(), idx.data_ptr(), _lib.DTYPE_CODE[idx.dtype],
-                                        tokens, k, H, out.data_ptr(), out.stride(0), _lib.stream_of(back.device)),
+                                        0, tokens, k, H, out.data_ptr(), out.stride(0), _lib.stream_of(back.device)),
                "vy_ep_combine")
     rows = back[slot.clamp(min=0)]
     rows[5] = 0.0
     idx_dropped = idx.clone()
     idx_dropped.view(-1)[5] = -1                               # a slot with id -1 adds nothing
     assert torch.equal(out, vb.combine(rows, idx_dropped))
+    # the same ids read through a row stride (every token's row padded to k + 3 ids)
+    wide = torch.full((tokens, k + 3), 999, dtype=idx.dtype, device="cuda")
+    wide[:, :k] = idx
+    out2 = torch.empty_like(out)
+    _lib.check(_lib.lib().vy_ep_combine(back.data_ptr(), slot.data_ptr(), wide.data_ptr(), _lib.DTYPE_CODE[idx.dtype],
+                                        wide.stride(0), tokens, k, H, out2.data_ptr(), out2.stride(0),
+                                        _lib.stream_of(back.device)), "vy_ep_combine")
+    assert torch.equal(out2, out)
 
 
 @pytest.mark.parametrize("path", [vb.PATH_DECODE, vb.PATH_PREFILL], ids=["decode", "prefill"])

@@ -63,8 +63,8 @@ SIGNATURES = {
     "vy_moe_combine": (ctypes.c_int, [P, P, I32T, I64T, I32T, I64T, P, I64T, P]),
     "vy_sum_ordered": (ctypes.c_int, [P, I32T, I64T, P, P]),
     "vy_ep_dispatch_plan": (ctypes.c_int, [P, I32T, I64T, I64T, I32T, I32T, I32T, I32T, P, I32T, I64T, I64T,
-                                           P, I32T, I64T, I64T, I64T, P, P, P, P, P, P]),
-    "vy_ep_combine": (ctypes.c_int, [P, P, P, I32T, I64T, I32T, I64T, P, I64T, P]),
+                                           P, I32T, I64T, I64T, I64T, P, P, P, P, P, P, P]),
+    "vy_ep_combine": (ctypes.c_int, [P, P, P, I32T, I64T, I64T, I32T, I64T, P, I64T, P]),
     "vy_moe_error_flags": (ctypes.c_int, [ctypes.POINTER(MoeCall), I32T, P, P]),
     "vy_selftest_bounded_wait": (ctypes.c_int, [I32T, I64T, P, P]),
 }

@@ -1,5 +1,7 @@
 // vy_capi.cu -- status plumbing and the per-device property cache of libvaayu_b200.
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "vy_common.cuh"
 
@@ -7,11 +9,32 @@ namespace vy {
 
 namespace {
 thread_local char g_last_error[512] = "";
-constexpr int kMaxDevices = 64;
 DeviceInfo g_info[kMaxDevices];
 bool g_have[kMaxDevices] = {};
 std::mutex g_info_mu;
+std::mutex g_once_mu;
+std::map<std::pair<int, const void*>, int> g_once;   // (device, key) set up
 }  // namespace
+
+int current_device() {
+    int dev = -1;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        fail(VY_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return dev;
+}
+
+int once_per_device(const void* key, int (*setup)(int device, void* ctx), void* ctx) {
+    const int dev = current_device();
+    if (dev < 0) return VY_ERR_CUDA;
+    std::lock_guard<std::mutex> lock(g_once_mu);
+    if (g_once.count({dev, key})) return VY_OK;
+    const int st = setup(dev, ctx);
+    if (st == VY_OK) g_once[{dev, key}] = st;
+    return st;
+}
 
 int fail(int code, const char* fmt, ...) {
     va_list ap;

@@ -33,6 +33,13 @@ struct DeviceInfo {
     size_t smem_optin;
 };
 const DeviceInfo* device_info(int* status);
+constexpr int kMaxDevices = 64;
+// The current device's index, or -1 (with the error recorded) when the runtime cannot tell.
+int current_device();
+// Kernel attributes (shared-memory opt-in) and occupancy figures belong to one device: runs
+// `setup` the first time (current device, key) succeeds, under a lock; later calls return VY_OK
+// at once.  A failed setup is tried again on the next call.  Thread-safe.
+int once_per_device(const void* key, int (*setup)(int device, void* ctx), void* ctx);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

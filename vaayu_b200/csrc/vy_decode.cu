@@ -618,26 +618,34 @@ template <int ACT, int SC, bool ZERO, int NB>
 int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaStream_t s,
                cudaEvent_t const* ev, bool timed) {
     // Resident CTAs per SM of the persistent grids, from the occupancy calculator (the warp ->
-    // unit assignment is static, so each whole grid must be resident at once).
-    static int gu_blocks_per_sm = 0, dn_blocks_per_sm = 0;
-    if (gu_blocks_per_sm == 0) {
-        cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(gu_smem()));
-        cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(gu_smem()));
-        cudaFuncSetAttribute(down_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(dn_smem()));
-        int nblk = 0, ndn = 0;
-        cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-            &nblk, gate_up_kernel<ACT, SC, ZERO, NB, false>, kGuWarps * 32, gu_smem());
-        if (oe == cudaSuccess)
-            oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ndn, down_kernel<ACT, SC, ZERO, NB>, kWarps * 32,
-                                                               dn_smem());
-        if (oe != cudaSuccess || nblk < 1 || ndn < 1)
-            return fail(VY_ERR_CUDA, "decode occupancy: %s", cudaGetErrorString(oe));
-        gu_blocks_per_sm = nblk;
-        dn_blocks_per_sm = ndn;
-    }
+    // unit assignment is static, so each whole grid must be resident at once).  The shared-memory
+    // opt-in and the occupancy figures belong to the device: set up once per device.
+    static int gu_per_sm[kMaxDevices], dn_per_sm[kMaxDevices];
+    const int st = once_per_device(
+        reinterpret_cast<const void*>(down_kernel<ACT, SC, ZERO, NB>),
+        [](int dev, void*) -> int {
+            cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gu_smem()));
+            cudaFuncSetAttribute(gate_up_kernel<ACT, SC, ZERO, NB, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gu_smem()));
+            cudaFuncSetAttribute(down_kernel<ACT, SC, ZERO, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(dn_smem()));
+            int nblk = 0, ndn = 0;
+            cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                &nblk, gate_up_kernel<ACT, SC, ZERO, NB, false>, kGuWarps * 32, gu_smem());
+            if (oe == cudaSuccess)
+                oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ndn, down_kernel<ACT, SC, ZERO, NB>,
+                                                                   kWarps * 32, dn_smem());
+            if (oe != cudaSuccess || nblk < 1 || ndn < 1)
+                return fail(VY_ERR_CUDA, "decode occupancy: %s", cudaGetErrorString(oe));
+            gu_per_sm[dev] = nblk;
+            dn_per_sm[dev] = ndn;
+            return VY_OK;
+        },
+        nullptr);
+    if (st != VY_OK) return st;
+    const int dev = current_device();
+    const int gu_blocks_per_sm = gu_per_sm[dev], dn_blocks_per_sm = dn_per_sm[dev];
     cudaError_t e = gu.k_splits > 1
         ? launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB, true>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu)
         : launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB, false>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu);
@@ -809,12 +817,17 @@ using namespace vy;
 extern "C" int vy_moe_error_flags(const vy_moe_call* c, int32_t path, int32_t* out, void* stream) {
     int st;
     if (!device_info(&st)) return st;
-    if (!c || !c->geom || !c->workspace || !out) return fail(VY_ERR_INVALID, "null call, workspace or output");
+    if (!c || !c->geom || !out) return fail(VY_ERR_INVALID, "null call or output");
+    if (!c->workspace && path != 0) return fail(VY_ERR_INVALID, "null workspace");
     const int32_t* flags;
     if (path == 1) {
         flags = prefill_flags(c);
     } else {
-        char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(c->workspace) + 255) & ~uintptr_t(255));
+        // no workspace: the call ran through vy_moe_decode_static, whose scratch is the library's array
+        void* ws = c->workspace;
+        int st2;
+        if (!ws && (st2 = decode_static_scratch(&ws)) != VY_OK) return st2;
+        char* base = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(ws) + 255) & ~uintptr_t(255));
         flags = decode_layout(c, base).counters + 2;
     }
     const cudaError_t e = cudaMemcpyAsync(out, flags, sizeof(int32_t), cudaMemcpyDefault, as_stream(stream));

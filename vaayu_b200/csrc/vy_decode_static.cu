@@ -21,7 +21,6 @@ namespace {
 
 static __device__ __align__(256) unsigned char g_decode_scratch[VY_DECODE_STATIC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
@@ -47,6 +46,9 @@ int scratch_address(void** out) {
 }
 
 }  // namespace
+
+int decode_static_scratch(void** out) { return scratch_address(out); }
+
 }  // namespace vy
 
 using namespace vy;

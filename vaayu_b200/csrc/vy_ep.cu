@@ -38,6 +38,7 @@ struct EpPlanArgs {
     float* send_w;
     int64_t* slot_of_row;
     int32_t* counts;
+    int32_t* wanted;           // optional: rows bound for each destination before the capacity cut
 };
 
 // Destination rank of row j = t * top_k + k (-1: an id outside the experts), and its local id.
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_plan_kernel(EpPlanArgs p) {
             total += c;
         }
         p.counts[d] = total < p.capacity ? total : static_cast<int>(p.capacity);
+        if (p.wanted) p.wanted[d] = total;
     }
     __syncthreads();
     // 3. each row's slot: its warp's next position for the destination + its rank among the
@@ -164,7 +166,8 @@ extern "C" int vy_ep_dispatch_plan(const void* ids, int32_t ids_dtype, int64_t i
                                    const void* weights, int32_t w_dtype, int64_t w_tok_stride,
                                    int64_t w_slot_stride, const void* x, int32_t x_dtype, int64_t x_row_stride,
                                    int64_t hidden, int64_t capacity, int32_t* send_ids, float* send_w,
-                                   void* send_x, int64_t* slot_of_row, int32_t* counts, void* stream) {
+                                   void* send_x, int64_t* slot_of_row, int32_t* counts, int32_t* wanted,
+                                   void* stream) {
     int st;
     const DeviceInfo* dev = device_info(&st);
     if (!dev) return st;
@@ -207,6 +210,7 @@ extern "C" int vy_ep_dispatch_plan(const void* ids, int32_t ids_dtype, int64_t i
     p.send_w = send_w;
     p.slot_of_row = slot_of_row;
     p.counts = counts;
+    p.wanted = wanted;
     ep_plan_kernel<<<1, kEpThreads, 0, s>>>(p);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "dispatch plan launch: %s", cudaGetErrorString(e));
@@ -233,8 +237,8 @@ extern "C" int vy_ep_dispatch_plan(const void* ids, int32_t ids_dtype, int64_t i
 }
 
 extern "C" int vy_ep_combine(const float* back, const int64_t* slot_of_row, const void* expert_ids,
-                             int32_t ids_dtype, int64_t n_tokens, int32_t top_k, int64_t hidden, float* out,
-                             int64_t out_row_stride, void* stream) {
+                             int32_t ids_dtype, int64_t ids_row_stride, int64_t n_tokens, int32_t top_k,
+                             int64_t hidden, float* out, int64_t out_row_stride, void* stream) {
     int st;
     const DeviceInfo* dev = device_info(&st);
     if (!dev) return st;
@@ -244,8 +248,10 @@ extern "C" int vy_ep_combine(const float* back, const int64_t* slot_of_row, cons
     if (top_k > kMaxTopK) return fail(VY_ERR_UNSUPPORTED, "top_k %d > %d", top_k, kMaxTopK);
     if (ids_dtype != VY_I32 && ids_dtype != VY_I64) return fail(VY_ERR_UNSUPPORTED, "id dtype %d", ids_dtype);
     if (out_row_stride < hidden) return fail(VY_ERR_INVALID, "out row stride %lld", (long long)out_row_stride);
+    if (ids_row_stride != 0 && ids_row_stride < top_k)
+        return fail(VY_ERR_INVALID, "ids row stride %lld < top_k %d", (long long)ids_row_stride, top_k);
     if (n_tokens == 0 || hidden == 0) return ok();
     if (!back || !slot_of_row || !expert_ids || !out) return fail(VY_ERR_INVALID, "null pointer");
     return launch_combine(back, expert_ids, ids_dtype == VY_I64, n_tokens, top_k, hidden, out, out_row_stride,
-                          dev->sm_count, as_stream(stream), slot_of_row);
+                          dev->sm_count, as_stream(stream), slot_of_row, ids_row_stride);
 }

@@ -241,12 +241,14 @@ constexpr size_t kRingBytes = size_t(kWarps) * kDepth * 64 * sizeof(uint4);
 
 template <int KIND, int NB>
 cudaError_t launch_one(unsigned grid, const GemvParams& p, cudaStream_t s) {
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(fp_gemv_kernel<KIND, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kRingBytes));
-        configured = true;
-    }
+    const int st = once_per_device(
+        reinterpret_cast<const void*>(fp_gemv_kernel<KIND, NB>),
+        [](int, void*) -> int {
+            return cudaFuncSetAttribute(fp_gemv_kernel<KIND, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        static_cast<int>(kRingBytes)) == cudaSuccess ? VY_OK : VY_ERR_CUDA;
+        },
+        nullptr);
+    if (st != VY_OK) return cudaErrorInvalidValue;
     return launch_chained(fp_gemv_kernel<KIND, NB>, dim3(grid), dim3(kWarps * 32), kRingBytes, s, p);
 }
 

@@ -59,15 +59,18 @@ int launch_slot_combine(const float* contrib, const int32_t* slot_order, int64_t
 // epilogue into c->result (and the routed sum into c->out when given).
 int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32_t* slot_order, cudaStream_t s);
 // out[t] = sum over token t's slots, ascending expert id then slot, of contribution row
-// t * top_k + k -- or rows[t * top_k + k] when `rows` is given (-1: no contribution).
+// t * top_k + k -- or rows[t * top_k + k] when `rows` is given (-1: no contribution).  Token t's
+// ids start at ids[t * ids_stride] (0: top_k, contiguous).
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
-                   cudaStream_t stream, const int64_t* rows = nullptr);
+                   cudaStream_t stream, const int64_t* rows = nullptr, int64_t ids_stride = 0);
 
 // Shared validation of a vy_moe_call (decode and prefill entry points).
 int validate_call(const vy_moe_call* c);
 size_t prefill_workspace_bytes(const vy_moe_call* c);
 int32_t* prefill_flags(const vy_moe_call* c);   // the call's error flags in its (prefill) workspace
+// The device address of the scratch array vy_moe_decode_static uses, on the current device.
+int decode_static_scratch(void** out);
 
 // Workspace carve-up shared by the decode and prefill entry points.
 struct Carve {

@@ -436,13 +436,13 @@ __global__ void topk_softmax_kernel(const void* logits, int64_t row_stride, int6
 
 // out[t] = sum of contrib rows of token t in slot_order (ascending expert id, then slot).
 __global__ void combine_kernel(const float* __restrict__ contrib, const void* ids, bool ids64,
-                               int64_t n_tokens, int top_k, int64_t hidden, float* out,
+                               int64_t ids_stride, int64_t n_tokens, int top_k, int64_t hidden, float* out,
                                int64_t out_stride, const int64_t* __restrict__ rows) {
     const int64_t t = blockIdx.y;
     int idx[kMaxTopK];
     int key[kMaxTopK];
     for (int k = 0; k < top_k; ++k) {
-        int e = load_id(ids, ids64, t * top_k + k);
+        int e = load_id(ids, ids64, t * ids_stride + k);
         key[k] = e < 0 ? INT32_MAX : e;
         idx[k] = k;
     }
@@ -488,12 +488,15 @@ int plan_validate(int64_t n_tokens, int top_k, int n_experts) {
 
 int launch_plan(const PlanArgs& p, int sm_count, cudaStream_t stream) {
     size_t smem = plan_smem_bytes(p.n_experts);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(plan_smem_bytes(kMaxExperts)));
-        configured = true;
-    }
+    const int st = once_per_device(
+        reinterpret_cast<const void*>(plan_kernel),
+        [](int, void*) -> int {
+            const cudaError_t e = cudaFuncSetAttribute(plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(plan_smem_bytes(kMaxExperts)));
+            return e == cudaSuccess ? VY_OK : fail(VY_ERR_CUDA, "routing plan shared memory: %s", cudaGetErrorString(e));
+        },
+        nullptr);
+    if (st != VY_OK) return st;
     // a decode-sized plan sorts with as many threads as the next power of two of its rows (the
     // fewer warps, the cheaper every block barrier); the counting sort takes the full block
     const int64_t n = p.n_tokens * p.top_k;
@@ -665,13 +668,14 @@ int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32
 
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
-                   cudaStream_t stream, const int64_t* rows) {
+                   cudaStream_t stream, const int64_t* rows, int64_t ids_stride) {
     if (n_tokens == 0) return VY_OK;
     int bx = static_cast<int>((hidden + 255) / 256);
     if (bx > 8) bx = 8;
     (void)sm_count;
     dim3 grid(bx, static_cast<unsigned>(n_tokens));
-    combine_kernel<<<grid, 256, 0, stream>>>(contrib, ids, ids64, n_tokens, top_k, hidden, out, out_stride, rows);
+    combine_kernel<<<grid, 256, 0, stream>>>(contrib, ids, ids64, ids_stride > 0 ? ids_stride : top_k, n_tokens,
+                                             top_k, hidden, out, out_stride, rows);
     return check_launch("combine");
 }
 

@@ -23,8 +23,12 @@ Layout: rank r holds the contiguous expert range [r * E/P, (r+1) * E/P) as a res
 "dispatch" (large batches, where replicating every token to every rank would move too much):
 
   1. every (token, slot) row is addressed to the rank owning its expert, into a fixed-capacity
-     slot range per destination (T * K slots, enough for any routing; empty slots carry expert
-     id -1), so the exchange needs no row counts on the host;
+     slot range per destination (empty slots carry expert id -1), so the exchange needs no row
+     counts on the host.  The capacity is a recorded bound, not T * K: the first call of a batch
+     shape counts the rows each destination wants (one host read, all ranks agreeing on the
+     largest), and later calls -- graph-capturable -- use that bound with a margin.  A call whose
+     routing would overflow it drops the excess rows and raises the layer's overflow flag
+     (`overflowed()`); `capacity=None` keeps T * K slots (nothing can be dropped);
   2. the rows' activations, local expert ids and routing weights cross with equal-split
      all-to-alls (NCCL over NVLink; peer data always lands in this GPU's own memory before a
      kernel reads it);
@@ -66,18 +70,27 @@ class ExpertParallelLayer:
                   "interleaved" (rank r holds experts r, r + P, r + 2P, ...: round-robin, which
                   spreads load that grows or shrinks with the expert index); local_blobs are the
                   rank's experts in ascending global id either way
+    capacity      dispatch mode's slots per destination: "auto" (default) sizes it once per batch
+                  shape from the rows the first call wants (x `capacity_margin`, agreed across
+                  ranks); an int fixes it; None uses T * K (never drops a row)
     """
 
     def __init__(self, local_blobs, n_experts: int, group=None, compute: Optional[Callable] = None,
                  combine_fn: Optional[Callable] = None, hidden: Optional[int] = None,
                  mode: str = "auto", replicate_max_tokens: int = 256,
                  layer_fn: Optional[Callable] = None, col_blocks: Optional[int] = None,
-                 path: Optional[int] = None, placement: str = "contiguous"):
+                 path: Optional[int] = None, placement: str = "contiguous", capacity="auto",
+                 capacity_margin: float = 1.5):
         if mode not in ("auto", "replicate", "dispatch"):
             raise ValueError(f"mode {mode!r}")
         if placement not in ("contiguous", "interleaved") or (placement == "interleaved" and mode != "dispatch"):
             raise ValueError(f"placement {placement!r} with mode {mode!r} (interleaved needs dispatch mode)")
         self.interleaved = placement == "interleaved"
+        if not (capacity is None or capacity == "auto" or (isinstance(capacity, int) and capacity > 0)):
+            raise ValueError(f"capacity {capacity!r} (\"auto\", a positive int or None)")
+        self.capacity, self.capacity_margin = capacity, capacity_margin
+        self._caps = {}           # (T, K) -> the recorded capacity per destination
+        self._over = None         # device int32: 1 once a dispatch dropped a row
         self.mode = mode
         self.path = path      # dispatch mode's local kernels: None = moe_forward's size rule
         self.replicate_max_tokens = replicate_max_tokens
@@ -110,14 +123,14 @@ class ExpertParallelLayer:
         dist.all_to_all_single(out, inp, output_split_sizes=out_splits,
                                input_split_sizes=in_splits, group=self.group)
 
-    def _dispatch_buffers(self, T, K, x, weights):
-        """Fixed-capacity exchange buffers: `cap` = T * K slots per destination, enough for any
-        routing (a token may even name one expert twice)."""
-        key = ("dispatch", T, K, x.dtype, weights.dtype, x.device)
+    def _dispatch_buffers(self, T, K, x, weights, cap=None):
+        """Exchange buffers for `cap` slots per destination (default: T * K, enough for any
+        routing -- a token may even name one expert twice)."""
+        cap = T * K if cap is None else cap
+        key = ("dispatch", T, K, cap, x.dtype, weights.dtype, x.device)
         b = self._bufs.get(key)
         if b is None:
             P, H, dev = self.world, x.shape[1], x.device
-            cap = T * K
             b = dict(cap=cap,
                      send_x=torch.empty(P * cap, H, dtype=x.dtype, device=dev),
                      send_id=torch.empty(P * cap, dtype=torch.int32, device=dev),
@@ -129,10 +142,42 @@ class ExpertParallelLayer:
                      back=torch.empty(P * cap, H, dtype=torch.float32, device=dev),
                      slot=torch.empty(T * K, dtype=torch.int64, device=dev),
                      counts=torch.empty(P, dtype=torch.int32, device=dev),
+                     wanted=torch.empty(P, dtype=torch.int32, device=dev),
                      tok=torch.arange(T * K, device=dev) // K,
                      ranks=torch.arange(P, device=dev).view(1, P))
             self._bufs[key] = b
         return b
+
+    def _capacity(self, T, K, x, ids, weights):
+        """Slots per destination for a (T, K) batch: T * K, the fixed int, or -- "auto" -- the
+        bound recorded on the first call of this shape: the rows the busiest destination wants on
+        any rank, times the margin, rounded up to 8 (one host read and one MAX all-reduce; not
+        inside a graph capture)."""
+        if self.capacity is None:
+            return T * K
+        if isinstance(self.capacity, int):
+            return min(self.capacity, T * K)
+        cap = self._caps.get((T, K))
+        if cap is None:
+            probe = self._dispatch_buffers(T, K, x, weights)
+            self._plan(x, ids, weights, probe)
+            most = probe["wanted"].max().reshape(1).to(torch.int64)
+            if self.world > 1:
+                dist.all_reduce(most, op=dist.ReduceOp.MAX, group=self.group)
+            cap = min(T * K, max(8, -(-int(self.capacity_margin * int(most.item())) // 8) * 8))
+            self._caps[(T, K)] = cap
+        return cap
+
+    def overflowed(self) -> bool:
+        """True once a dispatch call dropped a row because a destination was over its capacity
+        (reads a device flag: synchronises)."""
+        return bool(self._over is not None and int(self._over.item()))
+
+    def _plan(self, x, ids, weights, b):
+        if x.is_cuda:
+            self._plan_on_device(x, ids, weights, b)
+        else:
+            self._plan_on_host(x, ids, weights, b)
 
     def dispatch(self, x, ids, weights):
         """(recv_x, recv_local_ids, recv_w, plan) -- the rows this rank computes.  Row j of
@@ -140,12 +185,12 @@ class ExpertParallelLayer:
         the rows for the same destination, in row order); empty slots carry expert id -1, which
         the routing plan drops.  Equal-split exchanges: no host round trip, graph-capturable."""
         T, K = ids.shape
-        P = self.world
-        b = self._dispatch_buffers(T, K, x, weights)
-        if x.is_cuda:
-            self._plan_on_device(x, ids, weights, b)
-        else:
-            self._plan_on_host(x, ids, weights, b)
+        b = self._dispatch_buffers(T, K, x, weights, self._capacity(T, K, x, ids, weights))
+        self._plan(x, ids, weights, b)
+        if b["cap"] < T * K:       # record a dropped row (no host read: graph-capturable)
+            if self._over is None:
+                self._over = torch.zeros(1, dtype=torch.int32, device=x.device)
+            self._over.logical_or_((b["wanted"] > b["cap"]).any())
         self._a2a(b["recv_id"], b["send_id"], None, None)
         self._a2a(b["recv_w"], b["send_w"], None, None)
         self._a2a(b["recv_x"], b["send_x"], None, None)
@@ -172,10 +217,10 @@ class ExpertParallelLayer:
                 1 if self.interleaved else 0, weights.data_ptr(), w_code, weights.stride(0), weights.stride(1),
                 x.data_ptr(), x_code, x.stride(0), x.shape[1], b["cap"], b["send_id"].data_ptr(),
                 b["send_w"].data_ptr(), b["send_x"].data_ptr(), b["slot"].data_ptr(), b["counts"].data_ptr(),
-                _lib.stream_of(x.device)), "vy_ep_dispatch_plan")
+                b["wanted"].data_ptr(), _lib.stream_of(x.device)), "vy_ep_dispatch_plan")
 
     def _plan_on_host(self, x, ids, weights, b):
-        """The same send buffers and slot map from torch operations, for CPU tensors (the
+        """The same send buffers, slot map and counts from torch operations, for CPU tensors (the
         process-group logic's tests); every id must name one of the layer's experts."""
         T, K = ids.shape
         P, cap = self.world, b["cap"]
@@ -188,13 +233,17 @@ class ExpertParallelLayer:
             local = flat - dest * self.per_rank
         # rank among the rows bound for the same destination (a running count; no host check)
         hit = (dest.view(-1, 1) == b["ranks"]).to(torch.int32)
+        b["wanted"].copy_(hit.sum(0))
+        b["counts"].copy_(hit.sum(0).clamp(max=cap))
         pos = hit.cumsum(0).gather(1, dest.view(-1, 1)).view(-1) - 1
-        slot = dest * cap + pos
+        keep = pos < cap
+        slot = torch.where(keep, dest * cap + pos, torch.full_like(pos, -1))
         b["slot"].copy_(slot)
         b["send_id"].fill_(-1)
-        b["send_id"].index_copy_(0, slot, local.to(torch.int32))
-        b["send_w"].index_copy_(0, slot, weights.reshape(-1).to(torch.float32))
-        b["send_x"].index_copy_(0, slot, x.index_select(0, b["tok"]))
+        kept = keep.nonzero().view(-1)
+        b["send_id"].index_copy_(0, slot[kept], local[kept].to(torch.int32))
+        b["send_w"].index_copy_(0, slot[kept], weights.reshape(-1)[kept].to(torch.float32))
+        b["send_x"].index_copy_(0, slot[kept], x.index_select(0, b["tok"][kept]))
 
     def compute(self, recv_x, recv_ids, recv_w, plan=None):
         """Contributions [P * cap, H] fp32 of the received rows (slots with id -1 stay unwritten:
@@ -315,11 +364,12 @@ class ExpertParallelLayer:
             if out is None:
                 out = torch.empty(T, self.hidden, dtype=torch.float32, device=contrib.device)
             from . import _lib
-            ids_c = ids.contiguous()
+            ids_c = ids if ids.stride(1) == 1 else ids.contiguous()
             with torch.cuda.device(contrib.device):
                 _lib.check(_lib.lib().vy_ep_combine(
-                    b["back"].data_ptr(), slot.data_ptr(), ids_c.data_ptr(), _lib.DTYPE_CODE[ids_c.dtype], T, K,
-                    self.hidden, out.data_ptr(), out.stride(0), _lib.stream_of(contrib.device)), "vy_ep_combine")
+                    b["back"].data_ptr(), slot.data_ptr(), ids_c.data_ptr(), _lib.DTYPE_CODE[ids_c.dtype],
+                    ids_c.stride(0), T, K, self.hidden, out.data_ptr(), out.stride(0),
+                    _lib.stream_of(contrib.device)), "vy_ep_combine")
             return out
         rows = self.gather_back(contrib, plan)
         if self._combine is not None:
@@ -331,271 +381,3 @@ class ExpertParallelLayer:
         from .packed_expert_kernels import combine
         return combine(rows, ids, out)
 
-
-def run_bench(args, rank, world, local, wl):
-    """bench.py's N-GPU arm: `wl` (configuration 1 or 3) at `wl['tokens']` tokens per rank (weak
-    scaling), the routed experts sharded E/N per rank, steps rotating over `args.layers` layers.
-    A workload with `shared` experts replicates them on every rank, applies them to the rank's own
-    tokens and adds their output in bf16 (the model epilogue: out.to(bf16) + shared.to(bf16))."""
-    import json
-    import statistics
-
-    import bench
-    device = torch.device("cuda", local)
-    E, T, K = wl["experts"], wl["tokens"], wl["top_k"]
-    per = E // world
-    layers = [ExpertParallelLayer(bench.make_layer(1000 * l, wl, device, (rank * per, (rank + 1) * per)), E,
-                                  col_blocks=getattr(args, "ep_col_blocks", None))
-              for l in range(args.layers)]
-    batches = [tuple(v.to(device) for v in bench.make_tokens(l * 97 + rank, wl, T, device))
-               for l in range(args.layers)]
-    out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
-    L = args.layers
-    shared = None
-    if wl.get("shared"):
-        from .packed_expert_kernels import PATH_DECODE, ExpertTable, moe_workspace_bytes, shared_expert_forward
-        sw = dict(wl, experts=1)
-        shared = [ExpertTable(bench.make_layer(5000 + l, sw, device)) for l in range(L)]   # same on all ranks
-        sh_out = torch.empty(T, wl["hidden"], dtype=torch.float32, device=device)
-        sh_ws = torch.empty(moe_workspace_bytes(shared[0], T, 1, path=PATH_DECODE), dtype=torch.uint8, device=device)
-        result = torch.empty(T, wl["hidden"], dtype=torch.bfloat16, device=device)
-        if world == 1:
-            # one GPU holds every expert: the shared expert rides in the same layer call as every
-            # token's extra slot, the epilogue applied by the layer's combine
-            from .packed_expert_kernels import _with_shared, moe_forward_with_shared
-            fused_ws = torch.empty(moe_workspace_bytes(_with_shared(layers[0].table, shared[0]), T, K + 1,
-                                                       path=PATH_DECODE), dtype=torch.uint8, device=device)
-
-    def layer_step(l, x, idx, w):
-        if shared is not None and world == 1:
-            moe_forward_with_shared(x, idx, w, layers[l].table, shared[l], out=out, result=result,
-                                    path=PATH_DECODE, workspace=fused_ws)
-            return
-        layers[l].forward(x, idx, w, out)
-        if shared is not None:
-            shared_expert_forward(x, shared[l], out=sh_out, workspace=sh_ws)
-            torch.add(out.to(torch.bfloat16), sh_out.to(torch.bfloat16), out=result)
-
-    # each layer's step (pack, all-gather, kernels, all-to-all, combine) as one CUDA graph over
-    # static input buffers; eager calls when capture is not possible here
-    # (each layer's inputs are views of one device record, so the end-to-end step moves them with
-    # a single host-to-device copy)
-    nbytes, views = bench.record_layout(batches[0])
-    drecs = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(L)]
-    xs, ws_, ids_ = [], [], []
-    for l in range(L):
-        xv, wv, iv = views(drecs[l])
-        for v, src in zip((xv, wv, iv), batches[l]):
-            v.copy_(src)
-        xs.append(xv)
-        ws_.append(wv)
-        ids_.append(iv)
-    graphs = []
-    for l in range(L):
-        for _ in range(2):
-            layer_step(l, xs[l], ids_[l], ws_[l])
-    torch.cuda.synchronize(device)
-    bench.barrier(world)
-    try:
-        for l in range(L):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                layer_step(l, xs[l], ids_[l], ws_[l])
-            graphs.append(g)
-        torch.cuda.synchronize(device)
-    except Exception as e:  # noqa: BLE001 - report and run eagerly
-        graphs = []
-        if rank == 0:
-            print(f"# EP graph capture unavailable, eager steps: {e}", flush=True)
-    bench.barrier(world)
-
-    def step(i):
-        l = i % L
-        if graphs:
-            graphs[l].replay()
-        else:
-            layer_step(l, xs[l], ids_[l], ws_[l])
-
-    for i in range(args.warmup):
-        step(i)
-    bench.barrier(world)
-    with bench.ClockSampler(local) as clocks:
-        ms = bench.time_steps(step, args.steps, device)
-    bench.barrier(world)
-    ms = bench.max_over_ranks(ms, world)
-
-    pin = [bench.pinned_record(b, nbytes, views) for b in batches]
-    out_h = torch.empty(T, wl["hidden"], dtype=torch.float32 if shared is None else torch.bfloat16).pin_memory()
-
-    def e2e_step(i):
-        l = i % L
-        drecs[l].copy_(pin[l], non_blocking=True)
-        if graphs:
-            graphs[l].replay()
-        else:
-            layer_step(l, xs[l], ids_[l], ws_[l])
-        out_h.copy_(out if shared is None else result, non_blocking=True)
-
-    for i in range(args.warmup):
-        e2e_step(i)
-    bench.barrier(world)
-    e2e_ms = bench.max_over_ranks(bench.time_steps(e2e_step, args.steps, device), world)
-    bench.barrier(world)
-    h2d = nbytes                      # the record copied each step (its fields padded to 16 bytes)
-    used_graphs = bool(graphs)
-    del graphs               # graphs holding NCCL calls go before the process group does
-    torch.cuda.synchronize(device)
-    uniq = statistics.mean(len(set(b[2].reshape(-1).tolist())) for b in batches)
-    peak, peak_kind = bench.hbm_peak()
-    if rank == 0:
-        print(json.dumps({
-            "metric": bench.METRIC, "value": T * world / (ms / 1e3), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "int4 weights, bf16 activations, fp32 accumulate",
-            "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1))",
-            "config": {"workload": wl["name"], "hidden": wl["hidden"],
-                       "expert_intermediate": wl["inter"], "experts": E, "top_k": K,
-                       "tokens_per_gpu": T, "group_size": wl["group"], "layers_rotated": L,
-                       "l2": "inputs larger than L2 (each layer's expert weights exceed 126 MB per step)",
-                       "parallelism": f"ep{world}: {per} experts per GPU; replicate mode: one NCCL "
-                                      f"all-gather of the tokens, one all-to-all of per-token partial "
-                                      f"sums, rank-ordered combine",
-                       "routed_experts_per_rank_batch": uniq, "cuda_graphs": used_graphs,
-                       "shared_experts": wl.get("shared", 0),
-                       "col_blocks": layers[0]._bufs and next(iter(layers[0]._bufs.values()))["nb"]},
-            "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": out_h.numel() * out_h.element_size(),
-                    "ms_per_step": e2e_ms},
-            "roofline": {"kernel": "layer (expert parallel)", "bound": "hbm", "achieved": None,
-                         "peak": peak, "unit": "GB/s", "frac": None, "peak_source": peak_kind,
-                         "traffic": None},
-            "cpu_baseline": None,
-            # plan, gate/up, down and the rank-ordered sum (one GPU: the layer's combine), plus the
-            # separate shared-expert call's four on several GPUs
-            "gpu_launches": (4 + (4 if shared is not None and world > 1 else 0)) * args.steps,
-            "clocks": clocks.summary(),
-        }))
-
-
-def run_prefill_bench(args, rank, world, local, wl):
-    """bench.py's configuration-2 arm at any N (strong scaling): the one-GPU prefill bench's
-    2048-token batches (same seeds), rank r holding tokens [r T/N, (r + 1) T/N) and experts
-    r, r + N, r + 2N, ...; dispatch mode -- the rows to their experts' ranks by all-to-all (a fixed
-    capacity per destination, no host round trip), the local tcgen05 prefill GEMMs, contributions
-    back by the reverse all-to-all, the ascending-global-expert combine on each token's home rank.
-    Each layer step is one CUDA graph."""
-    import json
-
-    import bench
-    from . import synthetic
-    device = torch.device("cuda", local)
-    E, T, K, H, I = wl["experts"], wl["tokens"], wl["top_k"], wl["hidden"], wl["inter"]
-    if E % world or T % world:
-        raise ValueError(f"configuration 2 splits {E} experts and {T} tokens evenly: not over {world} GPUs")
-    per, tl = E // world, T // world
-    L = 2
-    # round-robin placement: the benchmark's router skew grows with the expert index, which
-    # contiguous ranges would hand to the last rank
-    layers = [ExpertParallelLayer(bench.make_layer(2000 + l, wl, device, keep=range(rank, E, world)), E,
-                                  mode="dispatch", placement="interleaved") for l in range(L)]
-    batches = []
-    for l in range(L):
-        g = torch.Generator(device=device).manual_seed(20_000 + l)
-        x, w, idx = synthetic.make_tokens(T, H, E, K, g, skew=wl["skew"])
-        sl = slice(rank * tl, (rank + 1) * tl)
-        batches.append((x[sl].contiguous(), w[sl].contiguous(), idx[sl].contiguous()))
-    out = torch.empty(tl, H, dtype=torch.float32, device=device)
-    # each layer's inputs are views of one device record (the end-to-end step fills it with one copy)
-    nbytes, views = bench.record_layout(batches[0])
-    drecs = [torch.empty(nbytes, dtype=torch.uint8, device=device) for _ in range(L)]
-    dviews = []
-    for l in range(L):
-        vs = views(drecs[l])
-        for v, src in zip(vs, batches[l]):
-            v.copy_(src)
-        dviews.append(vs)
-
-    def layer_step(l):
-        xv, wv, iv = dviews[l]
-        layers[l].forward(xv, iv, wv, out)
-
-    for l in range(L):
-        for _ in range(2):
-            layer_step(l)
-    torch.cuda.synchronize(device)
-    bench.barrier(world)
-    graphs = []
-    try:   # the dispatch is free of host round trips: one CUDA graph per layer step
-        for l in range(L):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                layer_step(l)
-            graphs.append(g)
-        torch.cuda.synchronize(device)
-    except Exception as e:  # noqa: BLE001 - report and run eagerly
-        graphs = []
-        if rank == 0:
-            print(f"# EP graph capture unavailable, eager steps: {e}", flush=True)
-    bench.barrier(world)
-
-    def step(i):
-        if graphs:
-            graphs[i % L].replay()
-        else:
-            layer_step(i % L)
-
-    for i in range(max(3, args.warmup)):
-        step(i)
-    steps = max(5, min(args.steps, 20))
-    bench.barrier(world)
-    with bench.ClockSampler(local) as clocks:
-        ms = bench.time_steps(step, steps, device)
-    bench.barrier(world)
-    ms = bench.max_over_ranks(ms, world)
-
-    pin = [bench.pinned_record(b, nbytes, views) for b in batches]
-    out_h = torch.empty(tl, H, dtype=torch.float32).pin_memory()
-
-    def e2e_step(i):
-        l = i % L
-        drecs[l].copy_(pin[l], non_blocking=True)
-        step(i)
-        out_h.copy_(out, non_blocking=True)
-
-    for i in range(3):
-        e2e_step(i)
-    bench.barrier(world)
-    e2e_ms = bench.max_over_ranks(bench.time_steps(e2e_step, steps, device), world)
-    bench.barrier(world)
-    used_graphs = bool(graphs)
-    del graphs               # graphs holding NCCL calls go before the process group does
-    torch.cuda.synchronize(device)
-    flops = 2.0 * T * K * 3 * H * I
-    burst, sustained, src = bench.bf16_peak()
-    achieved = flops / (ms / 1e3) / 1e12 / world           # per GPU
-    if rank == 0:
-        print(json.dumps({
-            "metric": bench.METRIC, "value": T / (ms / 1e3), "unit": "tokens/s",
-            "n_gpus": world, "steps": steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int4 weights, bf16 activations, fp32 accumulate",
-            "data": "synthetic (seeded; int4 codes U{0..15}, fp16 scales U(0.005,0.02), x~N(0,1), "
-                    f"router logits skewed by linspace(0, {wl['skew']}, {E}))",
-            "config": {"workload": wl["name"], "hidden": H, "expert_intermediate": I, "experts": E,
-                       "top_k": K, "tokens_total": T, "tokens_per_gpu": tl, "group_size": wl["group"],
-                       "layers_rotated": L, "l2": "inputs larger than L2 (each layer's expert weights: ~730 MB)",
-                       "parallelism": f"ep{world}: {per} experts per GPU (round-robin); dispatch mode: "
-                                      f"fixed-capacity all-to-alls of rows and contributions, "
-                                      f"ascending-global-expert combine",
-                       "cuda_graphs": used_graphs},
-            "e2e": {"value": T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": nbytes,
-                    "d2h_bytes_per_step": out_h.numel() * out_h.element_size(), "ms_per_step": e2e_ms},
-            "roofline": {"kernel": "layer (expert parallel, communication included)", "bound": "tensor",
-                         "achieved": achieved, "peak": burst, "unit": "TFLOP/s", "frac": achieved / burst,
-                         "peak_source": f"{src} (burst), per GPU", "traffic": None},
-            "cpu_baseline": None,
-            # plan, gather, gate/up GEMM, down GEMM (contributions) and the home-rank combine
-            "gpu_launches": 5 * steps,
-            "clocks": clocks.summary(),
-        }))

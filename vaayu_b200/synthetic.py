@@ -7,9 +7,9 @@ int4 zero points uniform in [0, 15], packed along rows as compressed-tensors pac
 (`pack_to_int32(zp, bits, packed_dim=0)`); activations ~N(0, 1) in bf16; router logits ~N(0, 1),
 softmax -> top-k -> renormalised (vaayu/moe_patch.py:160-161, 2331-2334).
 
-Generator call order follows the reference survey's baseline script: for every expert the roles
-gate [I, H], down [H, I], up [I, H] (codes then scales, then zero points when asked for); then the
-activations; then the router logits.  Works on any device the generator lives on.
+Generator call order: for every expert the roles gate [I, H], down [H, I], up [I, H] (codes then
+scales, then zero points when asked for); then the activations; then the router logits.  Works on
+any device the generator lives on.
 """
 from __future__ import annotations
 
