@@ -351,9 +351,10 @@ int vy_moe_prefill(const vy_moe_call* call, void* stream);
 
 /*
  * Bytes of the scratch array compiled into the library for vy_moe_decode_static.  Every GPU that
- * loads the library holds this much device memory until the process exits.
+ * loads the library holds this much device memory until the process exits.  Sized for the
+ * split-K partials of a two-token call at top-k 8 on a 2048 x 768 layer (about 15 MB).
  */
-#define VY_DECODE_STATIC_SCRATCH_BYTES (8u << 20)
+#define VY_DECODE_STATIC_SCRATCH_BYTES (16u << 20)
 
 /*
  * vy_moe_decode with no workspace from the caller and no allocation: the scratch is a fixed array

@@ -5,6 +5,7 @@ reference (vaayu/packed_expert_kernels.py, vaayu/moe_patch.py's packed-expert he
 DeepSeek-V4 block-scaled dequant), running on libvaayu_b200's CUDA kernels.  There is no CPU,
 torch or Triton fallback: calls on CPU tensors or geometry the kernels do not take raise.
 """
+from .arena import ExpertArena
 from .block_scaled import (dequantize_block_scaled, dequantize_fp4_block_scaled, fp4_gemv,
                            fp8_gemv)
 from .checkpoint import Checkpoint, group_packed_tensors_by_weight, packed_roles_complete
@@ -19,7 +20,7 @@ from .packed_expert_kernels import (PATH_DECODE, PATH_PREFILL, ExpertTable, comb
                                     packed_experts_decode_graphed, packed_experts_prefill)
 
 __all__ = [
-    "PATH_DECODE", "PATH_PREFILL", "Checkpoint", "ExpertTable", "accumulate_expert_outputs",
+    "PATH_DECODE", "PATH_PREFILL", "Checkpoint", "ExpertArena", "ExpertTable", "accumulate_expert_outputs",
     "build_expert_blob", "combine", "compute_expert_dispatch", "dequantize_block_scaled",
     "dequantize_expert_blob", "dequantize_expert_weights", "dequantize_fp4_block_scaled",
     "dequantize_packed_weight", "expert_weights_from_entry", "fp4_gemv", "fp8_gemv",

@@ -57,7 +57,8 @@ import torch.distributed as dist
 class ExpertParallelLayer:
     """One MoE layer's experts, sharded by contiguous ranges over the ranks of `group`.
 
-    local_blobs   the blobs of this rank's experts, in global id order
+    local_blobs   the blobs of this rank's experts, in global id order, or a ready table of them
+                  (an `ExpertTable`, or an `ExpertArena` holding every expert the rank is routed)
     n_experts     the layer's total expert count (divisible by the world size)
     mode          "replicate", "dispatch" or "auto" (replicate when every rank's batch is at most
                   `replicate_max_tokens` tokens)
@@ -110,7 +111,7 @@ class ExpertParallelLayer:
         self.table = None
         if compute is None and layer_fn is None:
             from .packed_expert_kernels import ExpertTable
-            self.table = ExpertTable(local_blobs)
+            self.table = local_blobs if hasattr(local_blobs, "geom_s") else ExpertTable(local_blobs)
             self.hidden = self.table.hidden
         else:
             self.hidden = hidden
