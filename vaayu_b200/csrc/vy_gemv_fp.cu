@@ -239,6 +239,213 @@ __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_ker
 
 constexpr size_t kRingBytes = size_t(kWarps) * kDepth * 64 * sizeof(uint4);
 
+// ── single-token NVFP4: f16 tensor-core operands ─────────────────────────────────────────
+//
+// One token (decode at batch 1) takes fp4_t1_kernel: the grid and the K split of fp_gemv_kernel,
+// with the arithmetic in f16.  cvt.rn.f16x2.e2m1x2 turns a byte (two codes) into an f16 pair, and
+// the product with the e4m3 group scale is exact in f16 (at most 6 significant bits, magnitudes
+// 2^-10 .. 2688), so the weights equal the bf16 dequantised ones.  Each warp stages its K range
+// of the activations in shared memory as x * 2^-s, s chosen so the range's largest |x| lands in
+// [2^14, 2^15): a bf16 value (8 significant bits) converts to f16 exactly down to 2^-28 of that
+// largest magnitude.  The warp's partial dots are multiplied back by 2^s (exact), so products
+// and sums equal those of the bf16 operands.  (A range whose largest |x| is below 2^-112 is staged
+// with s = -126 and loses low bits; an infinite or NaN activation is staged unscaled.)  This
+// replaces the byte-permute decode's ~2.6 integer instructions a code with half a conversion and
+// half an f16 multiply.
+
+#ifndef VY_GEMV_T1_WARPS
+#define VY_GEMV_T1_WARPS 16
+#endif
+constexpr int kT1Warps = VY_GEMV_T1_WARPS;
+constexpr int kT1StepK = 128;                     // K per step per row (16 B of codes a lane)
+constexpr size_t kT1RingBytes = size_t(kT1Warps) * kDepth * 64 * sizeof(uint4);
+
+// Two e2m1 codes (one byte, low nibble first) to an f16 pair, four bytes at a time.
+__device__ __forceinline__ void e2m1x8_f16(uint32_t c, uint32_t& d0, uint32_t& d1, uint32_t& d2, uint32_t& d3) {
+    asm("{ .reg .b8 b0, b1, b2, b3;\n"
+        "  mov.b32 {b0, b1, b2, b3}, %4;\n"
+        "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
+        "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+        "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
+        "  cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+        : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3) : "r"(c));
+}
+
+// An e4m3 code (low byte) as an f16 pair holding it twice (exact).
+__device__ __forceinline__ uint32_t e4m3_f16_dup(uint32_t b) {
+    uint32_t d;
+    const uint32_t two = (b & 0xFFu) * 0x101u;
+    asm("{ .reg .b16 h; cvt.u16.u32 h, %1; cvt.rn.f16x2.e4m3x2 %0, h; }" : "=r"(d) : "r"(two));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t f16x2_mul(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// The staging exponent s of a range whose largest |x| is m (see above).
+__device__ __forceinline__ int stage_shift(float m) {
+    if (!(m > 0.f) || !(m < __int_as_float(0x7F800000))) return 0;   // zero, infinite or NaN: unscaled
+    const int field = __float_as_int(m) >> 23;                        // biased exponent (m > 0)
+    const int s = field == 0 ? -126 : field - 127 - 14;
+    return s < -126 ? -126 : s;
+}
+__device__ __forceinline__ float pow2f(int s) {   // 2^s for s in [-126, 127]
+    return __int_as_float((s + 127) << 23);
+}
+
+__global__ void __launch_bounds__(kT1Warps * 32, 32 / kT1Warps) fp4_t1_kernel(GemvParams p) {
+    extern __shared__ uint4 t1_ring[];             // [kT1Warps][kDepth][2][32], then the staged x
+    __shared__ float part[kT1Warps][16];
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    uint4* my_ring = t1_ring + warp * (kDepth * 64);
+    const int64_t row0 = int64_t(blockIdx.x) * 16;
+    const int64_t steps = p.k / kT1StepK;
+    const int64_t s_lo = warp * steps / kT1Warps, s_hi = (warp + 1) * steps / kT1Warps;
+    const int64_t rA = row0 + g, rB = row0 + g + 8;
+    const bool okA = rA < p.n, okB = rB < p.n;
+    const uint8_t* wA = p.w + (okA ? rA : 0) * (p.k / 2);
+    const uint8_t* wB = p.w + (okB ? rB : 0) * (p.k / 2);
+    const uint8_t* sA = reinterpret_cast<const uint8_t*>(p.scale) + (okA ? rA : 0) * (p.k / p.gs);
+    const uint8_t* sB = reinterpret_cast<const uint8_t*>(p.scale) + (okB ? rB : 0) * (p.k / p.gs);
+    const uint32_t div = static_cast<uint32_t>(p.gs);
+    const int dsh = p.div_shift;
+    auto kdiv = [&](uint32_t kk) { return dsh >= 0 ? (kk >> dsh) : (kk / div); };
+
+    int64_t i_s = s_lo;
+    int i_slot = 0;
+    auto issue = [&]() {
+        if (i_s < s_hi) {
+            const int64_t off = (i_s * kT1StepK + tig * 32) / 2;
+            uint4* dst = my_ring + i_slot * 64 + lane;
+            if (okA) cp_async16(dst, wA + off);
+            if (okB) cp_async16(dst + 32, wB + off);
+        }
+        cp_async_commit();
+        ++i_s;
+        if (++i_slot == kDepth) i_slot = 0;
+    };
+#pragma unroll
+    for (int d = 0; d < kDepth - 1; ++d) issue();
+
+    // stage this warp's activations: x * 2^-sh as f16
+    const int64_t max_len = ((steps + kT1Warps - 1) / kT1Warps) * kT1StepK;
+    __half* xs = reinterpret_cast<__half*>(t1_ring + kT1Warps * kDepth * 64) + warp * max_len;
+    const int64_t len = (s_hi - s_lo) * kT1StepK;
+    const __nv_bfloat16* xt = p.x + s_lo * kT1StepK;
+    float m = 0.f;
+    for (int64_t k = 4 * lane; k < len; k += 128) {
+        const uint2 v = *reinterpret_cast<const uint2*>(xt + k);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(__uint_as_float(v.x << 16)), fabsf(__uint_as_float(v.x & 0xFFFF0000u))),
+                           fmaxf(fabsf(__uint_as_float(v.y << 16)), fabsf(__uint_as_float(v.y & 0xFFFF0000u)))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    const int sh = stage_shift(m);
+    const float down = pow2f(-sh);
+    for (int64_t k = 4 * lane; k < len; k += 128) {
+        const uint2 v = *reinterpret_cast<const uint2*>(xt + k);
+        const __half2 h0 = __floats2half2_rn(__uint_as_float(v.x << 16) * down, __uint_as_float(v.x & 0xFFFF0000u) * down);
+        const __half2 h1 = __floats2half2_rn(__uint_as_float(v.y << 16) * down, __uint_as_float(v.y & 0xFFFF0000u) * down);
+        *reinterpret_cast<uint2*>(xs + k) = make_uint2(*reinterpret_cast<const uint32_t*>(&h0),
+                                                       *reinterpret_cast<const uint32_t*>(&h1));
+    }
+    __syncwarp();
+
+    // the group scales of step i (rows A and B, groups of codes 0-15 and 16-31), loaded a step early
+    auto load_scales = [&](int64_t i, uint32_t& ga, uint32_t& gb) {
+        ga = gb = 0u;
+        if (i >= s_hi) return;
+        const uint32_t k0 = static_cast<uint32_t>(i * kT1StepK + tig * 32);
+        const uint32_t g0 = kdiv(k0), g1 = kdiv(k0 + 16);
+        if (okA) ga = __ldg(sA + g0) | (uint32_t(__ldg(sA + g1)) << 8);
+        if (okB) gb = __ldg(sB + g0) | (uint32_t(__ldg(sB + g1)) << 8);
+    };
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    int c_slot = 0;
+    uint32_t ga, gb;
+    load_scales(s_lo, ga, gb);
+    for (int64_t s = s_lo; s < s_hi; ++s) {
+        uint32_t na, nb;
+        load_scales(s + 1, na, nb);
+        issue();
+        cp_async_wait<kDepth - 1>();
+        const uint4* st = my_ring + c_slot * 64 + lane;
+        const uint4 va = okA ? st[0] : make_uint4(0u, 0u, 0u, 0u);
+        const uint4 vb = okB ? st[32] : make_uint4(0u, 0u, 0u, 0u);
+        if (++c_slot == kDepth) c_slot = 0;
+        const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
+        const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
+        const uint32_t ha[2] = {e4m3_f16_dup(ga), e4m3_f16_dup(ga >> 8)};   // f16 pairs
+        const uint32_t hb[2] = {e4m3_f16_dup(gb), e4m3_f16_dup(gb >> 8)};
+        const __half* xq = xs + (s - s_lo) * kT1StepK + tig * 32;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {      // word j: codes 8j .. 8j + 7 = mma steps 2j, 2j + 1
+            uint32_t ea[4], eb[4];
+            e2m1x8_f16(wa[j], ea[0], ea[1], ea[2], ea[3]);
+            e2m1x8_f16(wb[j], eb[0], eb[1], eb[2], eb[3]);
+            const uint32_t sa = ha[j >> 1], sb = hb[j >> 1];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint2 xv = make_uint2(0u, 0u);
+                if (g == 0) xv = *reinterpret_cast<const uint2*>(xq + 8 * j + 4 * h);
+                mma_16816<VY_F16>(acc, f16x2_mul(ea[2 * h], sa), f16x2_mul(eb[2 * h], sb),
+                                  f16x2_mul(ea[2 * h + 1], sa), f16x2_mul(eb[2 * h + 1], sb), xv.x, xv.y);
+            }
+        }
+        ga = na;
+        gb = nb;
+    }
+    cp_async_wait<0>();
+    // column 0 of the fragment is the token: acc[0] row g, acc[2] row g + 8 (lanes with tig 0)
+    if (tig == 0) {
+        const float up = pow2f(sh);
+        part[warp][g] = acc[0] * up;
+        part[warp][g + 8] = acc[2] * up;
+    }
+    __syncthreads();
+    if (threadIdx.x < 16) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < kT1Warps; ++w) a += part[w][threadIdx.x];
+        if (row0 + threadIdx.x < p.n) p.out[row0 + threadIdx.x] = __float2bfloat16_rn(a);
+    }
+}
+
+size_t t1_smem(int64_t k) {
+    const int64_t steps = k / kT1StepK;
+    return kT1RingBytes + size_t((steps + kT1Warps - 1) / kT1Warps) * kT1StepK * kT1Warps * 2;
+}
+
+// The largest dynamic shared memory fp4_t1_kernel may take on this device (its limit is raised to
+// that once per device; 0 when the setup failed).
+size_t t1_smem_limit() {
+    static size_t limit[kMaxDevices] = {};
+    const int st = once_per_device(
+        reinterpret_cast<const void*>(fp4_t1_kernel),
+        [](int dev, void*) -> int {
+            cudaFuncAttributes fa;
+            int optin = 0;
+            if (cudaFuncGetAttributes(&fa, fp4_t1_kernel) != cudaSuccess ||
+                cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+                return VY_ERR_CUDA;
+            const int room = optin - static_cast<int>(fa.sharedSizeBytes);
+            if (room <= 0 || cudaFuncSetAttribute(fp4_t1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  room) != cudaSuccess)
+                return VY_ERR_CUDA;
+            limit[dev] = static_cast<size_t>(room);
+            return VY_OK;
+        },
+        nullptr);
+    const int d = current_device();
+    return (st == VY_OK && d >= 0 && d < kMaxDevices) ? limit[d] : 0;
+}
+
 template <int KIND, int NB>
 cudaError_t launch_one(unsigned grid, const GemvParams& p, cudaStream_t s) {
     const int st = once_per_device(
@@ -252,11 +459,18 @@ cudaError_t launch_one(unsigned grid, const GemvParams& p, cudaStream_t s) {
     return launch_chained(fp_gemv_kernel<KIND, NB>, dim3(grid), dim3(kWarps * 32), kRingBytes, s, p);
 }
 
+// One-token NVFP4 calls with whole 16-code groups take fp4_t1_kernel while its staged activations
+// fit in shared memory; the rest fp_gemv_kernel.
 int launch_gemv(int kind, const GemvParams& p, cudaStream_t s) {
     const unsigned grid = static_cast<unsigned>((p.n + 15) / 16);
     const bool two = p.n_tokens > 8;
-    const cudaError_t e = kind == 0 ? (two ? launch_one<0, 2>(grid, p, s) : launch_one<0, 1>(grid, p, s))
-                                    : (two ? launch_one<1, 2>(grid, p, s) : launch_one<1, 1>(grid, p, s));
+    cudaError_t e;
+    const size_t t1 = kind == 1 && p.n_tokens == 1 && p.gs % 16 == 0 ? t1_smem(p.k) : 0;
+    if (t1 && t1 <= t1_smem_limit())
+        e = launch_chained(fp4_t1_kernel, dim3(grid), dim3(kT1Warps * 32), t1, s, p);
+    else
+        e = kind == 0 ? (two ? launch_one<0, 2>(grid, p, s) : launch_one<0, 1>(grid, p, s))
+                      : (two ? launch_one<1, 2>(grid, p, s) : launch_one<1, 1>(grid, p, s));
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "%s launch: %s", kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv",
                                       cudaGetErrorString(e));
     return check_launch(kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv");
