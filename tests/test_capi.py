@@ -52,8 +52,10 @@ def test_workspace_size_needs_no_gpu():
 
 
 def test_the_split_k_choice_shows_in_the_workspace_size():
-    """A one-token decode call shares each gate/up unit's K range among warps (its workspace holds
-    the per-stage partials); k_splits = 1 turns that off; a 32-token call never splits."""
+    """A decode call of at most 16 routed rows takes the few-row kernels: no split-K partials in
+    its workspace, whatever k_splits says.  A larger call with few units per warp (20 tokens,
+    top-1, 2 experts) shares each gate/up unit's K range among warps and its workspace holds the
+    per-stage partials; k_splits = 1 turns that off."""
     g = _lib.ExpertGeom()
     g.hidden, g.inter, g.bits, g.group_size = 2048, 768, 4, 128
     c = _lib.MoeCall()
@@ -62,13 +64,16 @@ def test_the_split_k_choice_shows_in_the_workspace_size():
     size = lambda: _lib.lib().vy_moe_workspace_size(ctypes.byref(c), 0)
     c.n_tokens, c.k_splits = 1, 0
     auto1 = size()
+    c.k_splits = 4
+    assert size() == auto1 > 0
+    c.top_k, c.n_experts, c.n_tokens, c.k_splits = 1, 2, 20, 0
+    auto20 = size()
     c.k_splits = 1
-    plain1 = size()
-    assert auto1 > plain1 > 0
-    # the partials: (8 rows / 8 per pass + 8 live experts + 1) passes x 48 tiles of 16 rows
+    plain20 = size()
+    # the partials: (20 rows / 8 per pass + 2 live experts + 1) passes x 48 tiles of 16 rows
     # x 16 stages of 128 K x 32 lanes x 8 floats
-    assert auto1 - plain1 >= 10 * 48 * 16 * 32 * 8 * 4
-    c.n_tokens, c.k_splits = 32, 0
+    assert auto20 - plain20 >= 5 * 48 * 16 * 32 * 8 * 4
+    c.top_k, c.n_experts, c.n_tokens, c.k_splits = 8, 128, 32, 0
     auto32 = size()
     c.k_splits = 1
     assert size() == auto32

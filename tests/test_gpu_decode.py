@@ -422,12 +422,53 @@ def test_new_call_fields_refuse_bad_values():
                        vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, k_splits=1))
 
 
-def test_a_workspace_sized_for_a_large_batch_serves_a_one_token_call():
-    """The split-K partials of a one-token call may not fit a workspace sized for 32 tokens: the
-    call then runs unsplit, with the same bits."""
-    blobs, x, idx, w = _batched(2048, 768, 128, 64, 8, 32, seed=43)
+def test_a_workspace_sized_for_a_large_batch_serves_a_split_call():
+    """The split-K partials of a call with few units per warp (20 tokens, top-1, 2 experts) may not
+    fit a workspace sized for 128 tokens: the call then runs unsplit, with the same bits."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 2, 1, 128, seed=43)
     table = pk.ExpertTable(blobs)
-    ws32 = torch.empty(pk.moe_workspace_bytes(table, 32, 8), dtype=torch.uint8, device="cuda")
-    assert pk.moe_workspace_bytes(table, 1, 8) > ws32.numel()      # the split needs more here
-    got = vb.moe_forward(x[:1], idx[:1], w[:1], table, path=vb.PATH_DECODE, workspace=ws32)
-    assert torch.equal(got, vb.moe_forward(x[:1], idx[:1], w[:1], table, path=vb.PATH_DECODE))
+    ws = torch.empty(pk.moe_workspace_bytes(table, 128, 1), dtype=torch.uint8, device="cuda")
+    assert pk.moe_workspace_bytes(table, 20, 1) > ws.numel()      # the split needs more here
+    got = vb.moe_forward(x[:20], idx[:20], w[:20], table, path=vb.PATH_DECODE, workspace=ws)
+    assert torch.equal(got, vb.moe_forward(x[:20], idx[:20], w[:20], table, path=vb.PATH_DECODE))
+
+
+@pytest.mark.parametrize("zeros,act", [(False, torch.bfloat16), (True, torch.bfloat16), (False, torch.float16)],
+                         ids=["symmetric-bf16", "zero-points-bf16", "symmetric-fp16"])
+def test_few_row_calls_match_the_planned_path_bit_for_bit(zeros, act):
+    """Two tokens at top-8 (16 routed rows) take the few-row kernels, three tokens the planned
+    path; a token's result does not depend on the other tokens of its batch, so the first two
+    tokens' h, contributions and combined rows agree bit for bit."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 32, 8, 3, seed=47, zeros=zeros, act=act)
+    table = pk.ExpertTable(blobs)
+    h3 = torch.empty(24, 768, dtype=act, device="cuda")
+    h2 = torch.empty(16, 768, dtype=act, device="cuda")
+    out3 = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, h_out=h3)
+    out2 = vb.moe_forward(x[:2], idx[:2], w[:2], table, path=vb.PATH_DECODE, h_out=h2)
+    assert torch.equal(out2, out3[:2])
+    assert torch.equal(h2, h3[:16])
+    c3 = torch.empty(24, 2048, device="cuda")
+    c2 = torch.empty(16, 2048, device="cuda")
+    vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, contrib=c3)
+    vb.moe_forward(x[:2], idx[:2], w[:2], table, path=vb.PATH_DECODE, contrib=c2)
+    assert torch.equal(c2, c3[:16])
+
+
+def test_few_row_calls_drop_foreign_and_missing_ids_like_the_planned_path():
+    """Global ids with expert_base (one expert-parallel rank's range) and -1 slots: rows outside
+    the table add nothing, in both paths."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 16, 8, 3, seed=53)
+    table = pk.ExpertTable(blobs)
+    gid = idx + 16                                   # this table holds experts [16, 32)
+    gid[0, 1] = -1
+    gid[1, 3] = 3                                    # another rank's expert
+    gid[2, 5] = 40
+    out3 = vb.moe_forward(x, gid, w, table, path=vb.PATH_DECODE, expert_base=16)
+    out2 = vb.moe_forward(x[:2], gid[:2], w[:2], table, path=vb.PATH_DECODE, expert_base=16)
+    assert torch.equal(out2, out3[:2])
+    keep = (gid[:2] >= 16) & (gid[:2] < 32)
+    ref = T.oracle_layer(blobs, x[:2], torch.where(keep, gid[:2] - 16, torch.zeros_like(gid[:2])),
+                         torch.where(keep, w[:2], torch.zeros_like(w[:2])))
+    assert T.rel_l2(out2.cpu().numpy(), ref) <= 1e-3
+
+

@@ -442,6 +442,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(D
     __shared__ UnitQueue<NB, kDnDepth> queue;
 
     grid_dependency_wait();
+    grid_dependents_launch();   // the combine may be scheduled now; it waits for this grid
 
     const int n_live = p.counters[0];
     if (n_live <= 0) return;
@@ -594,6 +595,353 @@ __global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(D
     cp_async_wait<0>();
 }
 
+// ── few-row calls: one CTA per (routed row, 16-row tile), no routing plan ────────────────
+//
+// A call of at most kRowMaxRows routed rows (a token or two at top-8) is latency-bound: the plan
+// kernel, the persistent grids' unit hand-off and the split-K join through global memory cost
+// more than moving its weights.  Here every CTA looks up its own row's expert, its warps share
+// the tile's K range (contiguous stage ranges, each streamed through a small cp.async ring), and
+// the stages' partial dots meet in shared memory, summed in stage order by one thread per output
+// row.  The per-stage MMA chains and that stage-order sum are the ones gate_up_kernel and
+// down_kernel perform, so the result is bit-identical to the planned path's.  A row routed to an
+// expert outside the table (or to one whose streams are unusable) contributes zero; the
+// layer's combine then sums each token's slots in ascending expert id, then slot.
+
+#ifndef VY_ROW_GU_WARPS
+#define VY_ROW_GU_WARPS 8
+#endif
+#ifndef VY_ROW_DN_WARPS
+#define VY_ROW_DN_WARPS 4
+#endif
+#ifndef VY_ROW_DEPTH
+#define VY_ROW_DEPTH 3
+#endif
+constexpr int kRowMaxRows = 16;
+constexpr int kRowGuWarps = VY_ROW_GU_WARPS;   // warps sharing a gate/up tile's K range
+constexpr int kRowDnWarps = VY_ROW_DN_WARPS;   // warps sharing a down tile's K range
+constexpr int kRowDepth = VY_ROW_DEPTH;        // ring stages per warp (kRowDepth - 1 in flight)
+constexpr int kRowMaxStages = 64;     // hidden / 128 and intermediate / 128 (stash bound)
+
+struct RowParams {
+    const void* ids;
+    bool ids64;
+    int64_t ids_stride;
+    int id_base, n_experts, top_k, n_rows;
+    const int64_t* table;
+    int hidden, inter, gs_shift;
+    int64_t w_off[3], s_off[3], z_off[3];   // gate, up, down
+    const void* x;
+    int64_t x_stride;
+    bool x_vec;
+    uint16_t* h_perm;
+    uint16_t* h_out;
+    const void* weights;
+    int w_dtype;
+    bool w_round;
+    int64_t w_tok_stride, w_slot_stride;
+    const int32_t* w_index;
+    float* contrib;       // [n_rows][hidden] weighted contributions, by row id
+    int32_t* flags;       // the call's error flags (one word)
+    float* out;           // the layer's combine into out [n_tokens, out_stride] (null: contributions only)
+    int64_t out_stride;
+    int32_t* tickets;     // [n_tokens][hidden / 16], zeroed by the gate/up kernel
+};
+
+__device__ __forceinline__ int row_id_load(const void* ids, bool ids64, int64_t j) {
+    if (ids64) {
+        const int64_t v = reinterpret_cast<const int64_t*>(ids)[j];
+        return (v < INT32_MIN || v > INT32_MAX) ? -1 : static_cast<int>(v);
+    }
+    return reinterpret_cast<const int32_t*>(ids)[j];
+}
+
+struct RowExpert {
+    const int32_t* pk;
+    const void* sc;
+    const int32_t* zp;
+    bool ok;              // routed to this table and its streams usable
+    bool bad;             // routed to this table but its streams unusable
+};
+
+__device__ __forceinline__ RowExpert row_expert(const RowParams& p, int r) {
+    const int64_t t = r / p.top_k;
+    int e = row_id_load(p.ids, p.ids64, t * p.ids_stride + (r - t * p.top_k));
+    e = (e < 0) ? -1 : e - p.id_base;
+    RowExpert x{nullptr, nullptr, nullptr, false, false};
+    if (e < 0 || e >= p.n_experts) return x;
+    x.pk = reinterpret_cast<const int32_t*>(p.table[3 * int64_t(e)]);
+    x.sc = reinterpret_cast<const void*>(p.table[3 * int64_t(e) + 1]);
+    x.zp = reinterpret_cast<const int32_t*>(p.table[3 * int64_t(e) + 2]);
+    x.ok = x.pk != nullptr && x.sc != nullptr && (reinterpret_cast<uintptr_t>(x.pk) & 15u) == 0;
+    x.bad = !x.ok;
+    return x;
+}
+
+// One warp's share of a tile's K range: stages [lo, hi) of `spu`, through a kRowDepth ring of
+// `chunks` 16-byte copies per lane and stage.  `src(stage, c)` is copy c's global address.
+template <int CHUNKS, typename Src>
+struct RowRing {
+    uint4* ring;          // this warp's [kRowDepth][CHUNKS][32]
+    int lo, hi, next;
+    __device__ __forceinline__ void issue(const Src& src, int lane) {
+        if (next < hi) {
+            uint4* dst = ring + ((next - lo) % kRowDepth) * (CHUNKS * 32) + lane;
+#pragma unroll
+            for (int c = 0; c < CHUNKS; ++c) cp_async16(dst + 32 * c, src(next, c));
+        }
+        cp_async_commit();
+        ++next;
+    }
+    __device__ __forceinline__ const uint4* slot(int stage, int lane) const {
+        return ring + ((stage - lo) % kRowDepth) * (CHUNKS * 32) + lane;
+    }
+};
+
+// After a down CTA has stored its 16 contributions of row r: the last of token t's top_k rows to
+// finish this 16-column tile sums them into `out`, in ascending expert id, then slot (ids below
+// zero skipped) -- the order of the layer's combine, whichever CTA arrives last.
+__device__ __forceinline__ void row_combine(const RowParams& p, int r, int tile) {
+    if (!p.out) return;
+    __shared__ int last;
+    const int64_t t = r / p.top_k;
+    if (threadIdx.x < kTileRows) __threadfence();      // this thread's contribution is visible
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int prev = atomicAdd(p.tickets + t * (p.hidden / kTileRows) + tile, 1);
+        last = prev == p.top_k - 1;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x >= kTileRows) return;
+    __threadfence();
+    int key[kMaxTopK], idx[kMaxTopK];
+    for (int k = 0; k < p.top_k; ++k) {
+        const int e = row_id_load(p.ids, p.ids64, t * p.ids_stride + k);
+        key[k] = e < 0 ? INT32_MAX : e;
+        idx[k] = k;
+    }
+    for (int a = 1; a < p.top_k; ++a) {
+        const int kv = key[a], iv = idx[a];
+        int b = a - 1;
+        while (b >= 0 && key[b] > kv) {
+            key[b + 1] = key[b];
+            idx[b + 1] = idx[b];
+            --b;
+        }
+        key[b + 1] = kv;
+        idx[b + 1] = iv;
+    }
+    const int64_t col = int64_t(tile) * kTileRows + threadIdx.x;
+    float acc = 0.f;
+    for (int k = 0; k < p.top_k; ++k)
+        if (key[k] != INT32_MAX) acc += __ldcg(p.contrib + (t * p.top_k + idx[k]) * p.hidden + col);
+    p.out[t * p.out_stride + col] = acc;
+}
+
+template <int ACT, int SC, bool ZERO>
+__global__ void __launch_bounds__(kRowGuWarps * 32) row_gate_up_kernel(RowParams p) {
+    extern __shared__ uint4 row_smem[];   // rings [kRowGuWarps][kRowDepth][4][32], then x (permuted)
+    __shared__ float stash[kRowMaxStages][kTileRows][2];
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const int tile = blockIdx.x, r = blockIdx.y;
+    if (tile == 0 && r == 0) {
+        // the call's error flags, written whole: a routed expert's streams unusable
+        if (threadIdx.x == 0) {
+            int32_t f = 0;
+            for (int q = 0; q < p.n_rows; ++q) f |= row_expert(p, q).bad ? 1 : 0;
+            *p.flags = f;
+        }
+        // the down kernel's combine tickets (it runs after this grid has completed)
+        if (p.out)
+            for (int i = threadIdx.x; i < (p.n_rows / p.top_k) * (p.hidden / kTileRows); i += blockDim.x)
+                p.tickets[i] = 0;
+    }
+    const RowExpert ex = row_expert(p, r);
+    if (!ex.ok) return;                   // no h row: the down kernel gives this row zeros
+    const int64_t t = r / p.top_k;
+    // this token's activations in the pair-permuted order (code j, code j + 4) of int4_pair
+    uint16_t* xs = reinterpret_cast<uint16_t*>(row_smem + kRowGuWarps * kRowDepth * 4 * 32);
+    const uint16_t* xt = reinterpret_cast<const uint16_t*>(p.x) + t * p.x_stride;
+    for (int c8 = threadIdx.x; c8 < p.hidden / 8; c8 += blockDim.x) {
+        uint16_t v[8];
+        if (p.x_vec) {
+            *reinterpret_cast<uint4*>(v) = *reinterpret_cast<const uint4*>(xt + c8 * 8);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = xt[c8 * 8 + j];
+        }
+        uint4 o;
+        o.x = v[0] | (uint32_t(v[4]) << 16);
+        o.y = v[1] | (uint32_t(v[5]) << 16);
+        o.z = v[2] | (uint32_t(v[6]) << 16);
+        o.w = v[3] | (uint32_t(v[7]) << 16);
+        *reinterpret_cast<uint4*>(xs + c8 * 8) = o;
+    }
+    const int spu = p.hidden / kStageK, wpr = p.hidden / 8, groups = p.hidden >> p.gs_shift;
+    const int row = tile * kTileRows + g;
+    const int32_t* srcg = ex.pk + p.w_off[0] + int64_t(row) * wpr + tig * 4;
+    const int32_t* srcu = ex.pk + p.w_off[1] + int64_t(row) * wpr + tig * 4;
+    auto src = [&](int stage, int c) -> const int32_t* {
+        const int32_t* b = (c < 2 ? srcg : srcu) + stage * 16;
+        return (c & 1) ? b + 8 * wpr : b;
+    };
+    RowRing<4, decltype(src)> rg{row_smem + warp * (kRowDepth * 4 * 32), warp * spu / kRowGuWarps,
+                                 (warp + 1) * spu / kRowGuWarps, warp * spu / kRowGuWarps};
+#pragma unroll
+    for (int d = 0; d < kRowDepth - 1; ++d) rg.issue(src, lane);
+    __syncthreads();                      // xs complete
+    int sidx[4], zidx[2];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+        sidx[2 * m] = static_cast<int>(p.s_off[m]) + row * groups;
+        sidx[2 * m + 1] = sidx[2 * m] + 8 * groups;
+        zidx[m] = static_cast<int>(p.z_off[m]) + (row >> 3) * groups;
+    }
+    const int kfirst = tig * 32;
+    for (int st = rg.lo; st < rg.hi; ++st) {
+        rg.issue(src, lane);
+        cp_async_wait<kRowDepth - 1>();
+        const int kx = st * kStageK;
+        uint4 xv[4];
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) xv[wi] = *reinterpret_cast<const uint4*>(xs + kx + kfirst + wi * 8);
+        const uint4* sl = rg.slot(st, lane);
+        const uint4 wg0 = sl[0], wg8 = sl[32], wu0 = sl[64], wu8 = sl[96];
+        const int grp = (kx + kfirst) >> p.gs_shift;
+        const uint32_t sg0 = scale_pair<ACT, SC>(ex.sc, sidx[0] + grp);
+        const uint32_t sg8 = scale_pair<ACT, SC>(ex.sc, sidx[1] + grp);
+        const uint32_t su0 = scale_pair<ACT, SC>(ex.sc, sidx[2] + grp);
+        const uint32_t su8 = scale_pair<ACT, SC>(ex.sc, sidx[3] + grp);
+        const uint32_t bg0 = bias_pair<ACT, ZERO>(ex.zp, zidx[0] + grp, g);
+        const uint32_t bg8 = bias_pair<ACT, ZERO>(ex.zp, zidx[0] + groups + grp, g);
+        const uint32_t bu0 = bias_pair<ACT, ZERO>(ex.zp, zidx[1] + grp, g);
+        const uint32_t bu8 = bias_pair<ACT, ZERO>(ex.zp, zidx[1] + groups + grp, g);
+        float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t wgw0[4] = {wg0.x, wg0.y, wg0.z, wg0.w}, wgw8[4] = {wg8.x, wg8.y, wg8.z, wg8.w};
+        const uint32_t wuw0[4] = {wu0.x, wu0.y, wu0.z, wu0.w}, wuw8[4] = {wu8.x, wu8.y, wu8.z, wu8.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            uint32_t ag0[4], ag8[4], au0[4], au8[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                ag0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wgw0[wi], j), bg0), sg0);
+                ag8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wgw8[wi], j), bg8), sg8);
+                au0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wuw0[wi], j), bu0), su0);
+                au8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wuw8[wi], j), bu8), su8);
+            }
+            mma_16816<ACT>(sg, ag0[0], ag8[0], ag0[1], ag8[1], xv[wi].x, xv[wi].y);
+            mma_16816<ACT>(sg, ag0[2], ag8[2], ag0[3], ag8[3], xv[wi].z, xv[wi].w);
+            mma_16816<ACT>(su, au0[0], au8[0], au0[1], au8[1], xv[wi].x, xv[wi].y);
+            mma_16816<ACT>(su, au0[2], au8[2], au0[3], au8[3], xv[wi].z, xv[wi].w);
+        }
+        if (tig == 0) {                   // column 0 of the fragment is the token
+            stash[st][g][0] = sg[0];
+            stash[st][g + 8][0] = sg[2];
+            stash[st][g][1] = su[0];
+            stash[st][g + 8][1] = su[2];
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (threadIdx.x < kTileRows) {
+        const int rr = threadIdx.x;
+        float ag = 0.f, au = 0.f;
+        for (int st = 0; st < spu; ++st) {
+            ag = __fadd_rn(ag, stash[st][rr][0]);
+            au = __fadd_rn(au, stash[st][rr][1]);
+        }
+        const int rrow = tile * kTileRows + rr;
+        const float gv = round_act<ACT>(ag);
+        const float uv = round_act<ACT>(au);
+        const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
+        const uint32_t hb = act_bits<ACT>(__fmul_rn(av, uv));
+        p.h_perm[int64_t(r) * p.inter + perm8(rrow)] = static_cast<uint16_t>(hb);
+        if (p.h_out) p.h_out[int64_t(r) * p.inter + rrow] = static_cast<uint16_t>(hb);
+    }
+}
+
+template <int ACT, int SC, bool ZERO>
+__global__ void __launch_bounds__(kRowDnWarps * 32) row_down_kernel(RowParams p) {
+    extern __shared__ uint4 row_smem[];   // rings [kRowDnWarps][kRowDepth][2][32]
+    __shared__ float stash[kRowMaxStages][kTileRows];
+    // Launched chained to the gate/up grid, which starts after the call's inputs are complete: the
+    // routing ids and the expert table may be read, and this row's down weights fetched, while
+    // that grid still runs; h and the combine tickets only after it has finished.
+    grid_dependents_launch();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const int tile = blockIdx.x, r = blockIdx.y;
+    const RowExpert ex = row_expert(p, r);
+    if (!ex.ok) {                         // not this table's row: it adds nothing to the combine
+        grid_dependency_wait();
+        if (threadIdx.x < kTileRows) p.contrib[int64_t(r) * p.hidden + tile * kTileRows + threadIdx.x] = 0.f;
+        row_combine(p, r, tile);
+        return;
+    }
+    const int spu = p.inter / kStageK, wpr = p.inter / 8, groups = p.inter >> p.gs_shift;
+    const int row = tile * kTileRows + g;
+    const int32_t* srcd = ex.pk + p.w_off[2] + int64_t(row) * wpr + tig * 4;
+    auto src = [&](int stage, int c) -> const int32_t* { return srcd + stage * 16 + (c ? 8 * wpr : 0); };
+    RowRing<2, decltype(src)> rg{row_smem + warp * (kRowDepth * 2 * 32), warp * spu / kRowDnWarps,
+                                 (warp + 1) * spu / kRowDnWarps, warp * spu / kRowDnWarps};
+#pragma unroll
+    for (int d = 0; d < kRowDepth - 1; ++d) rg.issue(src, lane);
+    grid_dependency_wait();
+    const int sidx0 = static_cast<int>(p.s_off[2]) + row * groups;
+    const int zidx = static_cast<int>(p.z_off[2]) + (row >> 3) * groups;
+    const int kfirst = tig * 32;
+    const uint16_t* hrow = p.h_perm + int64_t(r) * p.inter + kfirst;
+    for (int st = rg.lo; st < rg.hi; ++st) {
+        rg.issue(src, lane);
+        const int kh = st * kStageK;
+        uint4 hv[4];
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) hv[wi] = ld_nc_v4(hrow + kh + wi * 8);
+        cp_async_wait<kRowDepth - 1>();
+        const uint4* sl = rg.slot(st, lane);
+        const uint4 w0 = sl[0], w8 = sl[32];
+        const int grp = (kh + kfirst) >> p.gs_shift;
+        const uint32_t s0 = scale_pair<ACT, SC>(ex.sc, sidx0 + grp);
+        const uint32_t s8 = scale_pair<ACT, SC>(ex.sc, sidx0 + 8 * groups + grp);
+        const uint32_t b0 = bias_pair<ACT, ZERO>(ex.zp, zidx + grp, g);
+        const uint32_t b8 = bias_pair<ACT, ZERO>(ex.zp, zidx + groups + grp, g);
+        float sp[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t ww0[4] = {w0.x, w0.y, w0.z, w0.w}, ww8[4] = {w8.x, w8.y, w8.z, w8.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            uint32_t a0[4], a8[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(ww0[wi], j), b0), s0);
+                a8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(ww8[wi], j), b8), s8);
+            }
+            mma_16816<ACT>(sp, a0[0], a8[0], a0[1], a8[1], hv[wi].x, hv[wi].y);
+            mma_16816<ACT>(sp, a0[2], a8[2], a0[3], a8[3], hv[wi].z, hv[wi].w);
+        }
+        if (tig == 0) {
+            stash[st][g] = sp[0];
+            stash[st][g + 8] = sp[2];
+        }
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (threadIdx.x < kTileRows) {
+        const int rr = threadIdx.x;
+        float acc = 0.f;
+        for (int st = 0; st < spu; ++st) acc = __fadd_rn(acc, stash[st][rr]);
+        const int64_t t = r / p.top_k;
+        const int k = r - int(t) * p.top_k;
+        const int widx = p.w_index ? p.w_index[r] : k;
+        const float wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
+        float c = __fmul_rn(round_act<ACT>(acc), wv);
+        if (p.w_round) c = round_act<ACT>(c);
+        p.contrib[int64_t(r) * p.hidden + tile * kTileRows + rr] = c;
+    }
+    row_combine(p, r, tile);
+}
+
 // ── host side ─────────────────────────────────────────────────────────────────────────────
 
 size_t gu_smem() { return size_t(kGuWarps) * kGuDepth * 4 * 32 * sizeof(uint4); }
@@ -681,6 +1029,50 @@ int dispatch_sc(int sc, bool zero, int nb, const GateUpParams& gu, const DownPar
     }
 }
 
+size_t row_gu_smem(int hidden) { return size_t(kRowGuWarps) * kRowDepth * 4 * 32 * sizeof(uint4) + size_t(hidden) * 2; }
+size_t row_dn_smem() { return size_t(kRowDnWarps) * kRowDepth * 2 * 32 * sizeof(uint4); }
+
+template <int ACT, int SC, bool ZERO>
+int run_rows_typed(const RowParams& p, cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+    const int st = once_per_device(
+        reinterpret_cast<const void*>(row_gate_up_kernel<ACT, SC, ZERO>),
+        [](int, void*) -> int {
+            const cudaError_t e = cudaFuncSetAttribute(row_gate_up_kernel<ACT, SC, ZERO>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(row_gu_smem(kRowMaxStages * kStageK)));
+            return e == cudaSuccess ? VY_OK : fail(VY_ERR_CUDA, "few-row gate/up shared memory: %s",
+                                                   cudaGetErrorString(e));
+        },
+        nullptr);
+    if (st != VY_OK) return st;
+    cudaError_t e = launch_chained(row_gate_up_kernel<ACT, SC, ZERO>, dim3(p.inter / kTileRows, p.n_rows),
+                                   dim3(kRowGuWarps * 32), row_gu_smem(p.hidden), s, p);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "few-row gate/up launch: %s", cudaGetErrorString(e));
+    if (timed) cudaEventRecord(ev[2], s);
+    e = launch_chained(row_down_kernel<ACT, SC, ZERO>, dim3(p.hidden / kTileRows, p.n_rows), dim3(kRowDnWarps * 32),
+                       row_dn_smem(), s, p);
+    if (e != cudaSuccess) return fail(VY_ERR_CUDA, "few-row down launch: %s", cudaGetErrorString(e));
+    return VY_OK;
+}
+
+template <int ACT>
+int run_rows_act(int sc, bool zero, const RowParams& p, cudaStream_t s, cudaEvent_t const* ev, bool timed) {
+    switch (sc) {
+        case VY_BF16: return zero ? run_rows_typed<ACT, VY_BF16, true>(p, s, ev, timed)
+                                  : run_rows_typed<ACT, VY_BF16, false>(p, s, ev, timed);
+        case VY_F16: return zero ? run_rows_typed<ACT, VY_F16, true>(p, s, ev, timed)
+                                 : run_rows_typed<ACT, VY_F16, false>(p, s, ev, timed);
+        default: return zero ? run_rows_typed<ACT, VY_F32, true>(p, s, ev, timed)
+                             : run_rows_typed<ACT, VY_F32, false>(p, s, ev, timed);
+    }
+}
+
+// Whether a decode call takes the few-row kernels.
+bool rows_path(const vy_moe_call* c) {
+    return c->n_tokens * c->top_k <= kRowMaxRows && !c->shared_last &&
+           c->geom->hidden / kStageK <= kRowMaxStages && c->geom->inter / kStageK <= kRowMaxStages;
+}
+
 struct DecodeLayout {
     int32_t *order, *live_expert, *live_start, *unit_start, *slot_order, *counters;
     PassEntry* passes;
@@ -690,6 +1082,7 @@ struct DecodeLayout {
     int64_t max_units;
     float* partial;  // k_splits > 1: per-stage partial dots of every gate/up unit
     int32_t* tickets;
+    int32_t* row_tickets;   // few-row path: [n_tokens][hidden / 16] rows finished, for the combine
     size_t bytes;
 };
 
@@ -739,9 +1132,17 @@ DecodeLayout decode_layout(const vy_moe_call* c, void* base) {
     L.h_perm = cv.take<uint16_t>(n * I);
     L.ybuf_g = c->contrib == nullptr ? cv.take<float>(n * H) : nullptr;
     L.max_units = max_passes * (I / kTileRows);
-    L.k_splits = k_splits_for(c, L.max_units);
     L.partial = nullptr;
     L.tickets = nullptr;
+    L.row_tickets = nullptr;
+    if (rows_path(c)) {
+        // the few-row kernels: no split-K partials; one combine ticket per (token, 16-column tile)
+        L.k_splits = 1;
+        L.row_tickets = cv.take<int32_t>(c->n_tokens * (H / kTileRows));
+        L.bytes = cv.used;
+        return L;
+    }
+    L.k_splits = k_splits_for(c, L.max_units);
     if (L.k_splits > 1) {
         L.partial = cv.take<float>(L.max_units * (H / kStageK) * 32 * 8 * call_nb(c));
         L.tickets = cv.take<int32_t>(L.max_units);
@@ -865,6 +1266,54 @@ extern "C" int vy_moe_decode(const vy_moe_call* call, void* stream) {
     const vy_expert_geom& g = *c->geom;
     cudaStream_t s = as_stream(stream);
     const int nb = call_nb(c);
+    cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
+    const bool timed = ev != nullptr && c->n_stage_events >= 4;
+    if (timed && cudaEventRecord(ev[0], s) != cudaSuccess)
+        return fail(VY_ERR_INVALID, "stage_events[0] is not a usable cudaEvent_t");
+
+    if (rows_path(c)) {
+        RowParams rp{};
+        rp.ids = c->expert_ids;
+        rp.ids64 = c->ids_dtype == VY_I64;
+        rp.ids_stride = c->ids_row_stride ? c->ids_row_stride : c->top_k;
+        rp.id_base = c->expert_base;
+        rp.n_experts = c->n_experts;
+        rp.top_k = c->top_k;
+        rp.n_rows = static_cast<int>(c->n_tokens * c->top_k);
+        rp.table = c->expert_table;
+        rp.hidden = g.hidden;
+        rp.inter = g.inter;
+        int gs_shift = 0;
+        while ((1 << gs_shift) < g.group_size) ++gs_shift;
+        rp.gs_shift = gs_shift;
+        for (int m = 0; m < 3; ++m) {
+            rp.w_off[m] = g.word_off[m];
+            rp.s_off[m] = g.scale_off[m];
+            rp.z_off[m] = g.zero_off[m];
+        }
+        rp.x = c->x;
+        rp.x_stride = c->x_row_stride;
+        rp.x_vec = aligned16(c->x) && (c->x_row_stride % 8 == 0);
+        rp.h_perm = L.h_perm;
+        rp.h_out = static_cast<uint16_t*>(c->h_out);
+        rp.weights = c->weights;
+        rp.w_dtype = c->w_dtype;
+        rp.w_round = c->w_dtype == c->act_dtype;
+        rp.w_tok_stride = c->w_tok_stride;
+        rp.w_slot_stride = c->w_slot_stride;
+        rp.w_index = c->w_index;
+        rp.contrib = c->contrib ? c->contrib : L.ybuf_g;
+        rp.flags = L.counters + 2;
+        rp.out = c->contrib ? nullptr : c->out;      // the combine runs inside the down kernel
+        rp.out_stride = c->out_row_stride;
+        rp.tickets = L.row_tickets;
+        if (timed) cudaEventRecord(ev[1], s);
+        st = c->act_dtype == VY_BF16 ? run_rows_act<VY_BF16>(g.scale_dtype, g.has_zero != 0, rp, s, ev, timed)
+                                     : run_rows_act<VY_F16>(g.scale_dtype, g.has_zero != 0, rp, s, ev, timed);
+        if (st != VY_OK) return st;
+        if (timed) cudaEventRecord(ev[3], s);
+        return check_launch("vy_moe_decode");
+    }
 
     PlanArgs pa{};
     pa.ids = c->expert_ids;
@@ -892,10 +1341,6 @@ extern "C" int vy_moe_decode(const vy_moe_call* call, void* stream) {
         pa.zero_ints = L.tickets;
         pa.zero_count = static_cast<int>(L.max_units);
     }
-    cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(c->stage_events);
-    const bool timed = ev != nullptr && c->n_stage_events >= 4;
-    if (timed && cudaEventRecord(ev[0], s) != cudaSuccess)
-        return fail(VY_ERR_INVALID, "stage_events[0] is not a usable cudaEvent_t");
     if ((st = launch_plan(pa, dev->sm_count, s)) != VY_OK) return st;
     if (timed) cudaEventRecord(ev[1], s);
 

@@ -61,9 +61,11 @@ int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32
 // out[t] = sum over token t's slots, ascending expert id then slot, of contribution row
 // t * top_k + k -- or rows[t * top_k + k] when `rows` is given (-1: no contribution).  Token t's
 // ids start at ids[t * ids_stride] (0: top_k, contiguous).
+// `chained`: launched with programmatic stream serialisation (it waits for the previous kernel).
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
-                   cudaStream_t stream, const int64_t* rows = nullptr, int64_t ids_stride = 0);
+                   cudaStream_t stream, const int64_t* rows = nullptr, int64_t ids_stride = 0,
+                   bool chained = false);
 
 // Shared validation of a vy_moe_call (decode and prefill entry points).
 int validate_call(const vy_moe_call* c);

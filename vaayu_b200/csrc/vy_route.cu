@@ -227,6 +227,7 @@ __global__ void __launch_bounds__(kPlanThreads) plan_kernel(PlanArgs p) {
     // launched with programmatic serialisation: the previous kernel on the stream (often the last
     // call's combine) may still run; nothing here reads or writes before it has completed
     grid_dependency_wait();
+    grid_dependents_launch();   // the gate/up grid may be scheduled now; it waits for this grid
     if (blockIdx.x > 0) {
         // each thread permutes one 8-element group of one token's activations
         const int64_t groups_per_tok = p.hidden / 8;
@@ -438,6 +439,7 @@ __global__ void topk_softmax_kernel(const void* logits, int64_t row_stride, int6
 __global__ void combine_kernel(const float* __restrict__ contrib, const void* ids, bool ids64,
                                int64_t ids_stride, int64_t n_tokens, int top_k, int64_t hidden, float* out,
                                int64_t out_stride, const int64_t* __restrict__ rows) {
+    grid_dependency_wait();      // when launched chained: the contributions' producer has finished
     const int64_t t = blockIdx.y;
     int idx[kMaxTopK];
     int key[kMaxTopK];
@@ -456,14 +458,25 @@ __global__ void combine_kernel(const float* __restrict__ contrib, const void* id
         key[b + 1] = kv;
         idx[b + 1] = iv;
     }
+    // the slots' contribution rows in summation order: their own positions, or where `rows` says
+    // they landed (-1: none)
+    int64_t row[kMaxTopK];
+    for (int k = 0; k < top_k; ++k)
+        row[k] = key[k] == INT32_MAX ? -1 : (rows ? rows[t * top_k + idx[k]] : t * top_k + idx[k]);
+    constexpr int kBatch = 8;   // contributions loaded together, then added in order
     for (int64_t c = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; c < hidden;
          c += int64_t(gridDim.x) * blockDim.x) {
         float acc = 0.f;
-        for (int k = 0; k < top_k; ++k) {
-            if (key[k] == INT32_MAX) continue;
-            // the slot's contribution row: its own position, or where `rows` says it landed
-            const int64_t r = rows ? rows[t * top_k + idx[k]] : t * top_k + idx[k];
-            if (r >= 0) acc += contrib[r * hidden + c];
+        for (int k0 = 0; k0 < top_k; k0 += kBatch) {
+            float v[kBatch];
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                const int64_t r = k0 + j < top_k ? row[k0 + j] : -1;
+                v[j] = r >= 0 ? __ldcg(contrib + r * hidden + c) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j)
+                if (k0 + j < top_k && row[k0 + j] >= 0) acc += v[j];
         }
         out[t * out_stride + c] = acc;
     }
@@ -668,14 +681,21 @@ int launch_layer_combine(const vy_moe_call* c, const float* contrib, const int32
 
 int launch_combine(const float* contrib, const void* ids, bool ids64, int64_t n_tokens,
                    int top_k, int64_t hidden, float* out, int64_t out_stride, int sm_count,
-                   cudaStream_t stream, const int64_t* rows, int64_t ids_stride) {
+                   cudaStream_t stream, const int64_t* rows, int64_t ids_stride, bool chained) {
     if (n_tokens == 0) return VY_OK;
     int bx = static_cast<int>((hidden + 255) / 256);
     if (bx > 8) bx = 8;
     (void)sm_count;
     dim3 grid(bx, static_cast<unsigned>(n_tokens));
-    combine_kernel<<<grid, 256, 0, stream>>>(contrib, ids, ids64, ids_stride > 0 ? ids_stride : top_k, n_tokens,
-                                             top_k, hidden, out, out_stride, rows);
+    const int64_t stride = ids_stride > 0 ? ids_stride : top_k;
+    if (chained) {
+        const cudaError_t e = launch_chained(combine_kernel, grid, dim3(256), 0, stream, contrib, ids, ids64, stride,
+                                             n_tokens, top_k, hidden, out, out_stride, rows);
+        if (e != cudaSuccess) return fail(VY_ERR_CUDA, "combine launch: %s", cudaGetErrorString(e));
+    } else {
+        combine_kernel<<<grid, 256, 0, stream>>>(contrib, ids, ids64, stride, n_tokens, top_k, hidden, out,
+                                                 out_stride, rows);
+    }
     return check_launch("combine");
 }
 
