@@ -338,7 +338,8 @@ def cfg4_weights(device, copies=2):
 
 
 def gemv_profile(device):
-    """Three FP8 then three FP4 configuration-4 GEMVs at batch 1 (the launches an ncu capture reads)."""
+    """Three FP8 then three FP4 configuration-4 GEMVs at batch 1, then three FP8 and three FP4
+    dequantisations (the launches an ncu capture reads)."""
     from vaayu_b200 import block_scaled as bs
     N, K, g, fp8, fp4 = cfg4_weights(device, copies=1)
     x = torch.randn(1, K, generator=g, device=device).to(torch.bfloat16)
@@ -347,6 +348,10 @@ def gemv_profile(device):
         bs.fp8_gemv(x, *fp8[0], out=o)
     for _ in range(3):
         bs.fp4_gemv(x, *fp4[0], out=o)
+    for _ in range(3):
+        bs.dequantize_block_scaled(*fp8[0])
+    for _ in range(3):
+        bs.dequantize_fp4_block_scaled(*fp4[0])
     torch.cuda.synchronize(device)
     print(json.dumps({"profile": "gemv", "n": N, "k": K, "tokens": 1}))
 
@@ -736,6 +741,8 @@ def run_ours(args, rank, world, local):
     if args.profile == "gemv":
         return gemv_profile(device)
 
+    if args.profile and args.tokens:
+        T = wl["tokens"] = args.tokens        # profiling only: the headline batch is the workload's
     layers = [pk.ExpertTable(make_layer(1000 * l, wl, device)) for l in range(args.layers)]
     batches = {}
     for t in sorted({T, 1, 8}):
@@ -1003,6 +1010,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the configuration-2 prefill measurement")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baselines")
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="with --profile decode: the decode batch (default: the workload's)")
     ap.add_argument("--workload", default="cfg1", choices=("cfg1", "cfg2", "cfg3", "cfg3-prefill"),
                     help="cfg1 (default): the headline decode workload (expert-parallel for N > 1); "
                          "cfg2: the Mixtral-shaped 2048-token prefill, experts and tokens split over N "
