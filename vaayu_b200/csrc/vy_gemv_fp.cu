@@ -271,11 +271,10 @@ __device__ __forceinline__ void e2m1x8_f16(uint32_t c, uint32_t& d0, uint32_t& d
         : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3) : "r"(c));
 }
 
-// An e4m3 code (low byte) as an f16 pair holding it twice (exact).
-__device__ __forceinline__ uint32_t e4m3_f16_dup(uint32_t b) {
+// Two e4m3 codes (bits 0-15, first in the low byte) as an f16 pair (exact).
+__device__ __forceinline__ uint32_t e4m3x2_f16(uint32_t b) {
     uint32_t d;
-    const uint32_t two = (b & 0xFFu) * 0x101u;
-    asm("{ .reg .b16 h; cvt.u16.u32 h, %1; cvt.rn.f16x2.e4m3x2 %0, h; }" : "=r"(d) : "r"(two));
+    asm("{ .reg .b16 h; cvt.u16.u32 h, %1; cvt.rn.f16x2.e4m3x2 %0, h; }" : "=r"(d) : "r"(b));
     return d;
 }
 
@@ -296,6 +295,9 @@ __device__ __forceinline__ float pow2f(int s) {   // 2^s for s in [-126, 127]
     return __int_as_float((s + 127) << 23);
 }
 
+// G16: 16-code groups with 2-byte aligned scale rows -- one 16-bit load brings a row's two group
+// scales of a step.
+template <bool G16>
 __global__ void __launch_bounds__(kT1Warps * 32, 32 / kT1Warps) fp4_t1_kernel(GemvParams p) {
     extern __shared__ uint4 t1_ring[];             // [kT1Warps][kDepth][2][32], then the staged x
     __shared__ float part[kT1Warps][16];
@@ -319,12 +321,15 @@ __global__ void __launch_bounds__(kT1Warps * 32, 32 / kT1Warps) fp4_t1_kernel(Ge
 
     int64_t i_s = s_lo;
     int i_slot = 0;
+    const uint8_t* srcA = wA + (s_lo * kT1StepK + tig * 32) / 2;   // this lane's 16 bytes of the next step
+    const uint8_t* srcB = wB + (s_lo * kT1StepK + tig * 32) / 2;
     auto issue = [&]() {
         if (i_s < s_hi) {
-            const int64_t off = (i_s * kT1StepK + tig * 32) / 2;
             uint4* dst = my_ring + i_slot * 64 + lane;
-            if (okA) cp_async16(dst, wA + off);
-            if (okB) cp_async16(dst + 32, wB + off);
+            if (okA) cp_async16(dst, srcA);
+            if (okB) cp_async16(dst + 32, srcB);
+            srcA += kT1StepK / 2;
+            srcB += kT1StepK / 2;
         }
         cp_async_commit();
         ++i_s;
@@ -361,10 +366,16 @@ __global__ void __launch_bounds__(kT1Warps * 32, 32 / kT1Warps) fp4_t1_kernel(Ge
     auto load_scales = [&](int64_t i, uint32_t& ga, uint32_t& gb) {
         ga = gb = 0u;
         if (i >= s_hi) return;
-        const uint32_t k0 = static_cast<uint32_t>(i * kT1StepK + tig * 32);
-        const uint32_t g0 = kdiv(k0), g1 = kdiv(k0 + 16);
-        if (okA) ga = __ldg(sA + g0) | (uint32_t(__ldg(sA + g1)) << 8);
-        if (okB) gb = __ldg(sB + g0) | (uint32_t(__ldg(sB + g1)) << 8);
+        if constexpr (G16) {
+            const int64_t g0 = i * (kT1StepK / 16) + tig * 2;
+            if (okA) ga = __ldg(reinterpret_cast<const unsigned short*>(sA + g0));
+            if (okB) gb = __ldg(reinterpret_cast<const unsigned short*>(sB + g0));
+        } else {
+            const uint32_t k0 = static_cast<uint32_t>(i * kT1StepK + tig * 32);
+            const uint32_t g0 = kdiv(k0), g1 = kdiv(k0 + 16);
+            if (okA) ga = __ldg(sA + g0) | (uint32_t(__ldg(sA + g1)) << 8);
+            if (okB) gb = __ldg(sB + g0) | (uint32_t(__ldg(sB + g1)) << 8);
+        }
     };
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     int c_slot = 0;
@@ -381,8 +392,10 @@ __global__ void __launch_bounds__(kT1Warps * 32, 32 / kT1Warps) fp4_t1_kernel(Ge
         if (++c_slot == kDepth) c_slot = 0;
         const uint32_t wa[4] = {va.x, va.y, va.z, va.w};
         const uint32_t wb[4] = {vb.x, vb.y, vb.z, vb.w};
-        const uint32_t ha[2] = {e4m3_f16_dup(ga), e4m3_f16_dup(ga >> 8)};   // f16 pairs
-        const uint32_t hb[2] = {e4m3_f16_dup(gb), e4m3_f16_dup(gb >> 8)};
+        // the two groups' scales as f16 pairs holding each twice (exact)
+        const uint32_t pa = e4m3x2_f16(ga), pb = e4m3x2_f16(gb);
+        const uint32_t ha[2] = {__byte_perm(pa, 0, 0x1010), __byte_perm(pa, 0, 0x3232)};
+        const uint32_t hb[2] = {__byte_perm(pb, 0, 0x1010), __byte_perm(pb, 0, 0x3232)};
         const __half* xq = xs + (s - s_lo) * kT1StepK + tig * 32;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {      // word j: codes 8j .. 8j + 7 = mma steps 2j, 2j + 1
@@ -424,18 +437,19 @@ size_t t1_smem(int64_t k) {
 
 // The largest dynamic shared memory fp4_t1_kernel may take on this device (its limit is raised to
 // that once per device; 0 when the setup failed).
+template <bool G16>
 size_t t1_smem_limit() {
     static size_t limit[kMaxDevices] = {};
     const int st = once_per_device(
-        reinterpret_cast<const void*>(fp4_t1_kernel),
+        reinterpret_cast<const void*>(fp4_t1_kernel<G16>),
         [](int dev, void*) -> int {
             cudaFuncAttributes fa;
             int optin = 0;
-            if (cudaFuncGetAttributes(&fa, fp4_t1_kernel) != cudaSuccess ||
+            if (cudaFuncGetAttributes(&fa, fp4_t1_kernel<G16>) != cudaSuccess ||
                 cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
                 return VY_ERR_CUDA;
             const int room = optin - static_cast<int>(fa.sharedSizeBytes);
-            if (room <= 0 || cudaFuncSetAttribute(fp4_t1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            if (room <= 0 || cudaFuncSetAttribute(fp4_t1_kernel<G16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   room) != cudaSuccess)
                 return VY_ERR_CUDA;
             limit[dev] = static_cast<size_t>(room);
@@ -466,8 +480,11 @@ int launch_gemv(int kind, const GemvParams& p, cudaStream_t s) {
     const bool two = p.n_tokens > 8;
     cudaError_t e;
     const size_t t1 = kind == 1 && p.n_tokens == 1 && p.gs % 16 == 0 ? t1_smem(p.k) : 0;
-    if (t1 && t1 <= t1_smem_limit())
-        e = launch_chained(fp4_t1_kernel, dim3(grid), dim3(kT1Warps * 32), t1, s, p);
+    const bool g16 = p.gs == 16 && (reinterpret_cast<uintptr_t>(p.scale) & 1u) == 0 && (p.k / 16) % 2 == 0;
+    if (t1 && g16 && t1 <= t1_smem_limit<true>())
+        e = launch_chained(fp4_t1_kernel<true>, dim3(grid), dim3(kT1Warps * 32), t1, s, p);
+    else if (t1 && !g16 && t1 <= t1_smem_limit<false>())
+        e = launch_chained(fp4_t1_kernel<false>, dim3(grid), dim3(kT1Warps * 32), t1, s, p);
     else
         e = kind == 0 ? (two ? launch_one<0, 2>(grid, p, s) : launch_one<0, 1>(grid, p, s))
                       : (two ? launch_one<1, 2>(grid, p, s) : launch_one<1, 1>(grid, p, s));
