@@ -435,38 +435,39 @@ def test_a_workspace_sized_for_a_large_batch_serves_a_split_call():
 
 @pytest.mark.parametrize("zeros,act", [(False, torch.bfloat16), (True, torch.bfloat16), (False, torch.float16)],
                          ids=["symmetric-bf16", "zero-points-bf16", "symmetric-fp16"])
-def test_few_row_calls_match_the_planned_path_bit_for_bit(zeros, act):
-    """Two tokens at top-8 (16 routed rows) take the few-row kernels, three tokens the planned
-    path; a token's result does not depend on the other tokens of its batch, so the first two
-    tokens' h, contributions and combined rows agree bit for bit."""
-    blobs, x, idx, w = _batched(2048, 768, 128, 32, 8, 3, seed=47, zeros=zeros, act=act)
+def test_the_three_decode_decompositions_agree_bit_for_bit(zeros, act):
+    """Over 64 experts at top-8: two tokens (16 routed rows) take the few-row kernels, five tokens
+    (40 rows) the pass-per-CTA kernels, nine tokens (72 rows) the warp-unit kernels.  A token's
+    result does not depend on the other tokens of its batch, so the shared tokens' h,
+    contributions and combined rows agree bit for bit across the three."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 64, 8, 9, seed=47, zeros=zeros, act=act)
     table = pk.ExpertTable(blobs)
-    h3 = torch.empty(24, 768, dtype=act, device="cuda")
-    h2 = torch.empty(16, 768, dtype=act, device="cuda")
-    out3 = vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, h_out=h3)
-    out2 = vb.moe_forward(x[:2], idx[:2], w[:2], table, path=vb.PATH_DECODE, h_out=h2)
-    assert torch.equal(out2, out3[:2])
-    assert torch.equal(h2, h3[:16])
-    c3 = torch.empty(24, 2048, device="cuda")
-    c2 = torch.empty(16, 2048, device="cuda")
-    vb.moe_forward(x, idx, w, table, path=vb.PATH_DECODE, contrib=c3)
-    vb.moe_forward(x[:2], idx[:2], w[:2], table, path=vb.PATH_DECODE, contrib=c2)
-    assert torch.equal(c2, c3[:16])
+    runs = {}
+    for t in (2, 5, 9):
+        h = torch.empty(t * 8, 768, dtype=act, device="cuda")
+        out = vb.moe_forward(x[:t], idx[:t], w[:t], table, path=vb.PATH_DECODE, h_out=h)
+        c = torch.empty(t * 8, 2048, device="cuda")
+        vb.moe_forward(x[:t], idx[:t], w[:t], table, path=vb.PATH_DECODE, contrib=c)
+        runs[t] = (out, h, c)
+    for a, b in ((2, 5), (2, 9), (5, 9)):
+        assert torch.equal(runs[a][0], runs[b][0][:a]), (a, b)
+        assert torch.equal(runs[a][1], runs[b][1][:a * 8]), (a, b)
+        assert torch.equal(runs[a][2], runs[b][2][:a * 8]), (a, b)
 
 
 def test_few_row_calls_drop_foreign_and_missing_ids_like_the_planned_path():
     """Global ids with expert_base (one expert-parallel rank's range) and -1 slots: rows outside
-    the table add nothing, in both paths."""
-    blobs, x, idx, w = _batched(2048, 768, 128, 16, 8, 3, seed=53)
+    the table add nothing, on the few-row and the pass-per-CTA kernels alike."""
+    blobs, x, idx, w = _batched(2048, 768, 128, 64, 8, 3, seed=53)
     table = pk.ExpertTable(blobs)
-    gid = idx + 16                                   # this table holds experts [16, 32)
+    gid = idx + 16                                   # this table holds experts [16, 80)
     gid[0, 1] = -1
     gid[1, 3] = 3                                    # another rank's expert
-    gid[2, 5] = 40
+    gid[2, 5] = 90
     out3 = vb.moe_forward(x, gid, w, table, path=vb.PATH_DECODE, expert_base=16)
     out2 = vb.moe_forward(x[:2], gid[:2], w[:2], table, path=vb.PATH_DECODE, expert_base=16)
     assert torch.equal(out2, out3[:2])
-    keep = (gid[:2] >= 16) & (gid[:2] < 32)
+    keep = (gid[:2] >= 16) & (gid[:2] < 80)
     ref = T.oracle_layer(blobs, x[:2], torch.where(keep, gid[:2] - 16, torch.zeros_like(gid[:2])),
                          torch.where(keep, w[:2], torch.zeros_like(w[:2])))
     assert T.rel_l2(out2.cpu().numpy(), ref) <= 1e-3

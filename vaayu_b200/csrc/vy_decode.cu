@@ -58,6 +58,7 @@ struct GateUpParams {
     const uint16_t* x_perm;
     uint16_t* h_perm;
     uint16_t* h_out;
+    int max_passes;       // host side: the largest pass count the call can have (grid bound)
     int k_splits;         // warps sharing one unit's K range (1: none)
     float* partial;       // k_splits > 1: [unit][stage][lane][8 NB] per-stage partial dots
     int32_t* tickets;     // k_splits > 1: [unit] finished splits, zeroed by the plan kernel
@@ -677,15 +678,15 @@ __device__ __forceinline__ RowExpert row_expert(const RowParams& p, int r) {
     return x;
 }
 
-// One warp's share of a tile's K range: stages [lo, hi) of `spu`, through a kRowDepth ring of
+// One warp's share of a tile's K range: stages [lo, hi) of `spu`, through a DEPTH-stage ring of
 // `chunks` 16-byte copies per lane and stage.  `src(stage, c)` is copy c's global address.
-template <int CHUNKS, typename Src>
+template <int CHUNKS, int DEPTH, typename Src>
 struct RowRing {
-    uint4* ring;          // this warp's [kRowDepth][CHUNKS][32]
+    uint4* ring;          // this warp's [DEPTH][CHUNKS][32]
     int lo, hi, next;
     __device__ __forceinline__ void issue(const Src& src, int lane) {
         if (next < hi) {
-            uint4* dst = ring + ((next - lo) % kRowDepth) * (CHUNKS * 32) + lane;
+            uint4* dst = ring + ((next - lo) % DEPTH) * (CHUNKS * 32) + lane;
 #pragma unroll
             for (int c = 0; c < CHUNKS; ++c) cp_async16(dst + 32 * c, src(next, c));
         }
@@ -693,7 +694,7 @@ struct RowRing {
         ++next;
     }
     __device__ __forceinline__ const uint4* slot(int stage, int lane) const {
-        return ring + ((stage - lo) % kRowDepth) * (CHUNKS * 32) + lane;
+        return ring + ((stage - lo) % DEPTH) * (CHUNKS * 32) + lane;
     }
 };
 
@@ -787,7 +788,7 @@ __global__ void __launch_bounds__(kRowGuWarps * 32) row_gate_up_kernel(RowParams
         const int32_t* b = (c < 2 ? srcg : srcu) + stage * 16;
         return (c & 1) ? b + 8 * wpr : b;
     };
-    RowRing<4, decltype(src)> rg{row_smem + warp * (kRowDepth * 4 * 32), warp * spu / kRowGuWarps,
+    RowRing<4, kRowDepth, decltype(src)> rg{row_smem + warp * (kRowDepth * 4 * 32), warp * spu / kRowGuWarps,
                                  (warp + 1) * spu / kRowGuWarps, warp * spu / kRowGuWarps};
 #pragma unroll
     for (int d = 0; d < kRowDepth - 1; ++d) rg.issue(src, lane);
@@ -884,7 +885,7 @@ __global__ void __launch_bounds__(kRowDnWarps * 32) row_down_kernel(RowParams p)
     const int row = tile * kTileRows + g;
     const int32_t* srcd = ex.pk + p.w_off[2] + int64_t(row) * wpr + tig * 4;
     auto src = [&](int stage, int c) -> const int32_t* { return srcd + stage * 16 + (c ? 8 * wpr : 0); };
-    RowRing<2, decltype(src)> rg{row_smem + warp * (kRowDepth * 2 * 32), warp * spu / kRowDnWarps,
+    RowRing<2, kRowDepth, decltype(src)> rg{row_smem + warp * (kRowDepth * 2 * 32), warp * spu / kRowDnWarps,
                                  (warp + 1) * spu / kRowDnWarps, warp * spu / kRowDnWarps};
 #pragma unroll
     for (int d = 0; d < kRowDepth - 1; ++d) rg.issue(src, lane);
@@ -942,6 +943,234 @@ __global__ void __launch_bounds__(kRowDnWarps * 32) row_down_kernel(RowParams p)
     row_combine(p, r, tile);
 }
 
+// ── planned calls, one CTA per (pass, 16-row tile) ─────────────────────────────────────
+//
+// The same units as gate_up_kernel / down_kernel (a pass of a live expert: up to 8 routed rows;
+// a 16-row tile), but a unit is a CTA whose warps share its K range, instead of a warp walking the
+// whole K range: more loads in flight per unit and no per-warp unit hand-off.  The stage partials
+// of every column meet in shared memory and are added in stage order, so the results are
+// bit-identical to the warp-unit kernels'.  The grid covers the largest possible pass count; CTAs
+// past the call's passes exit at once.
+
+#ifndef VY_PASS_GU_WARPS
+#define VY_PASS_GU_WARPS 8
+#endif
+#ifndef VY_PASS_DN_WARPS
+#define VY_PASS_DN_WARPS 4
+#endif
+#ifndef VY_PASS_DEPTH
+#define VY_PASS_DEPTH 2
+#endif
+constexpr int kPassGuWarps = VY_PASS_GU_WARPS;
+constexpr int kPassDnWarps = VY_PASS_DN_WARPS;
+constexpr int kPassDepth = VY_PASS_DEPTH;     // ring stages per warp (one in flight ahead)
+constexpr int kPassMaxRows = 64;              // routed rows a call may have to take these kernels
+
+size_t pass_gu_smem(int hidden) {
+    return size_t(kPassGuWarps) * kPassDepth * 4 * 32 * sizeof(uint4) + size_t(hidden / kStageK) * kTileRows * 2 * 8 * 4;
+}
+size_t pass_dn_smem(int inter) {
+    return size_t(kPassDnWarps) * kPassDepth * 2 * 32 * sizeof(uint4) + size_t(inter / kStageK) * kTileRows * 8 * 4;
+}
+
+template <int ACT, int SC, bool ZERO>
+__global__ void __launch_bounds__(kPassGuWarps * 32) pass_gate_up_kernel(GateUpParams p) {
+    extern __shared__ uint4 pass_smem[];  // rings [kPassGuWarps][kPassDepth][4][32], then the stash
+    __shared__ int col_row[8];
+    __shared__ int ncols_s;
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const int tile = blockIdx.x, pg = blockIdx.y;
+    const int n_live = p.counters[0];
+    if (n_live <= 0 || pg >= p.unit_start[n_live]) return;
+    const PassEntry& pe = p.passes[pg];
+    const int32_t* pk = reinterpret_cast<const int32_t*>(pe.pk);
+    const void* sc = reinterpret_cast<const void*>(pe.sc);
+    const int32_t* zp = reinterpret_cast<const int32_t*>(pe.zp);
+    const bool ok = pk != nullptr && sc != nullptr && (reinterpret_cast<uintptr_t>(pk) & 15u) == 0;
+    if (!ok) {
+        if (tile == 0 && threadIdx.x == 0) atomicOr(p.counters + 2, 1);
+        return;
+    }
+    if (threadIdx.x < 8) col_row[threadIdx.x] = threadIdx.x < pe.ncols ? pe.rows[threadIdx.x] : -1;
+    if (threadIdx.x == 0) ncols_s = pe.ncols < 8 ? pe.ncols : 8;
+    const int spu = p.hidden / kStageK, wpr = p.hidden / 8, groups = p.hidden >> p.gs_shift;
+    const int row = tile * kTileRows + g;
+    const int32_t* srcg = pk + p.w_off[0] + int64_t(row) * wpr + tig * 4;
+    const int32_t* srcu = pk + p.w_off[1] + int64_t(row) * wpr + tig * 4;
+    auto src = [&](int stage, int c) -> const int32_t* {
+        const int32_t* b = (c < 2 ? srcg : srcu) + stage * 16;
+        return (c & 1) ? b + 8 * wpr : b;
+    };
+    RowRing<4, kPassDepth, decltype(src)> rg{pass_smem + warp * (kPassDepth * 4 * 32), warp * spu / kPassGuWarps,
+                                 (warp + 1) * spu / kPassGuWarps, warp * spu / kPassGuWarps};
+#pragma unroll
+    for (int d = 0; d < kPassDepth - 1; ++d) rg.issue(src, lane);
+    float* stash = reinterpret_cast<float*>(pass_smem + kPassGuWarps * kPassDepth * 4 * 32);   // [spu][16][2][8]
+    __syncthreads();                      // col_row
+    const int myrow = col_row[g];         // this lane's column (token row) in the fragments
+    const int kfirst = tig * 32;
+    const int xoff = myrow >= 0 ? (myrow / p.top_k) * p.hidden + kfirst : -1;
+    int sidx[4], zidx[2];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+        sidx[2 * m] = static_cast<int>(p.s_off[m]) + row * groups;
+        sidx[2 * m + 1] = sidx[2 * m] + 8 * groups;
+        zidx[m] = static_cast<int>(p.z_off[m]) + (row >> 3) * groups;
+    }
+    for (int st = rg.lo; st < rg.hi; ++st) {
+        rg.issue(src, lane);
+        const int kx = st * kStageK;
+        uint4 xv[4];
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi)
+            xv[wi] = xoff >= 0 ? ld_nc_v4(p.x_perm + xoff + kx + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
+        cp_async_wait<kPassDepth - 1>();
+        const uint4* sl = rg.slot(st, lane);
+        const uint4 wg0 = sl[0], wg8 = sl[32], wu0 = sl[64], wu8 = sl[96];
+        const int grp = (kx + kfirst) >> p.gs_shift;
+        const uint32_t sg0 = scale_pair<ACT, SC>(sc, sidx[0] + grp);
+        const uint32_t sg8 = scale_pair<ACT, SC>(sc, sidx[1] + grp);
+        const uint32_t su0 = scale_pair<ACT, SC>(sc, sidx[2] + grp);
+        const uint32_t su8 = scale_pair<ACT, SC>(sc, sidx[3] + grp);
+        const uint32_t bg0 = bias_pair<ACT, ZERO>(zp, zidx[0] + grp, g);
+        const uint32_t bg8 = bias_pair<ACT, ZERO>(zp, zidx[0] + groups + grp, g);
+        const uint32_t bu0 = bias_pair<ACT, ZERO>(zp, zidx[1] + grp, g);
+        const uint32_t bu8 = bias_pair<ACT, ZERO>(zp, zidx[1] + groups + grp, g);
+        float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t wgw0[4] = {wg0.x, wg0.y, wg0.z, wg0.w}, wgw8[4] = {wg8.x, wg8.y, wg8.z, wg8.w};
+        const uint32_t wuw0[4] = {wu0.x, wu0.y, wu0.z, wu0.w}, wuw8[4] = {wu8.x, wu8.y, wu8.z, wu8.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            uint32_t ag0[4], ag8[4], au0[4], au8[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                ag0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wgw0[wi], j), bg0), sg0);
+                ag8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wgw8[wi], j), bg8), sg8);
+                au0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wuw0[wi], j), bu0), su0);
+                au8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(wuw8[wi], j), bu8), su8);
+            }
+            mma_16816<ACT>(sg, ag0[0], ag8[0], ag0[1], ag8[1], xv[wi].x, xv[wi].y);
+            mma_16816<ACT>(sg, ag0[2], ag8[2], ag0[3], ag8[3], xv[wi].z, xv[wi].w);
+            mma_16816<ACT>(su, au0[0], au8[0], au0[1], au8[1], xv[wi].x, xv[wi].y);
+            mma_16816<ACT>(su, au0[2], au8[2], au0[3], au8[3], xv[wi].z, xv[wi].w);
+        }
+        // fragment (row g / g + 8, columns 2 tig / 2 tig + 1) into the stash [st][row][g or u][col]
+        float* sa = stash + ((st * kTileRows + g) * 2) * 8 + 2 * tig;
+        float* sb = stash + ((st * kTileRows + g + 8) * 2) * 8 + 2 * tig;
+        *reinterpret_cast<float2*>(sa) = make_float2(sg[0], sg[1]);
+        *reinterpret_cast<float2*>(sa + 8) = make_float2(su[0], su[1]);
+        *reinterpret_cast<float2*>(sb) = make_float2(sg[2], sg[3]);
+        *reinterpret_cast<float2*>(sb + 8) = make_float2(su[2], su[3]);
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (threadIdx.x < kTileRows * 8) {
+        const int rr = threadIdx.x >> 3, c = threadIdx.x & 7;
+        if (c < ncols_s) {
+            float ag = 0.f, au = 0.f;
+            for (int st = 0; st < spu; ++st) {
+                ag = __fadd_rn(ag, stash[((st * kTileRows + rr) * 2) * 8 + c]);
+                au = __fadd_rn(au, stash[((st * kTileRows + rr) * 2 + 1) * 8 + c]);
+            }
+            const int rrow = tile * kTileRows + rr, rowid = col_row[c];
+            const float gv = round_act<ACT>(ag);
+            const float uv = round_act<ACT>(au);
+            const float av = round_act<ACT>(gv / (1.0f + expf(-gv)));
+            const uint32_t hb = act_bits<ACT>(__fmul_rn(av, uv));
+            p.h_perm[int64_t(rowid) * p.inter + perm8(rrow)] = static_cast<uint16_t>(hb);
+            if (p.h_out) p.h_out[int64_t(rowid) * p.inter + rrow] = static_cast<uint16_t>(hb);
+        }
+    }
+}
+
+template <int ACT, int SC, bool ZERO>
+__global__ void __launch_bounds__(kPassDnWarps * 32) pass_down_kernel(DownParams p) {
+    extern __shared__ uint4 pass_smem[];  // rings [kPassDnWarps][kPassDepth][2][32], then the stash
+    __shared__ int col_row[8];
+    __shared__ int ncols_s;
+    grid_dependency_wait();
+    grid_dependents_launch();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const int tile = blockIdx.x, pg = blockIdx.y;
+    const int n_live = p.counters[0];
+    if (n_live <= 0 || pg >= p.unit_start[n_live]) return;
+    const PassEntry& pe = p.passes[pg];
+    const int32_t* pk = reinterpret_cast<const int32_t*>(pe.pk);
+    const void* sc = reinterpret_cast<const void*>(pe.sc);
+    const int32_t* zp = reinterpret_cast<const int32_t*>(pe.zp);
+    const bool ok = pk != nullptr && sc != nullptr && (reinterpret_cast<uintptr_t>(pk) & 15u) == 0;
+    if (!ok) return;                      // flagged by the gate/up kernel
+    if (threadIdx.x < 8) col_row[threadIdx.x] = threadIdx.x < pe.ncols ? pe.rows[threadIdx.x] : -1;
+    if (threadIdx.x == 0) ncols_s = pe.ncols < 8 ? pe.ncols : 8;
+    const int spu = p.inter / kStageK, wpr = p.inter / 8, groups = p.inter >> p.gs_shift;
+    const int row = tile * kTileRows + g;
+    const int32_t* srcd = pk + p.w_off + int64_t(row) * wpr + tig * 4;
+    auto src = [&](int stage, int c) -> const int32_t* { return srcd + stage * 16 + (c ? 8 * wpr : 0); };
+    RowRing<2, kPassDepth, decltype(src)> rg{pass_smem + warp * (kPassDepth * 2 * 32), warp * spu / kPassDnWarps,
+                                 (warp + 1) * spu / kPassDnWarps, warp * spu / kPassDnWarps};
+#pragma unroll
+    for (int d = 0; d < kPassDepth - 1; ++d) rg.issue(src, lane);
+    float* stash = reinterpret_cast<float*>(pass_smem + kPassDnWarps * kPassDepth * 2 * 32);   // [spu][16][8]
+    __syncthreads();
+    const int myrow = col_row[g];
+    const int kfirst = tig * 32;
+    const int hoff = myrow >= 0 ? myrow * p.inter + kfirst : -1;
+    const int sidx0 = static_cast<int>(p.s_off) + row * groups;
+    const int zidx = static_cast<int>(p.z_off) + (row >> 3) * groups;
+    for (int st = rg.lo; st < rg.hi; ++st) {
+        rg.issue(src, lane);
+        const int kh = st * kStageK;
+        uint4 hv[4];
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi)
+            hv[wi] = hoff >= 0 ? ld_nc_v4(p.h_perm + hoff + kh + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
+        cp_async_wait<kPassDepth - 1>();
+        const uint4* sl = rg.slot(st, lane);
+        const uint4 w0 = sl[0], w8 = sl[32];
+        const int grp = (kh + kfirst) >> p.gs_shift;
+        const uint32_t s0 = scale_pair<ACT, SC>(sc, sidx0 + grp);
+        const uint32_t s8 = scale_pair<ACT, SC>(sc, sidx0 + 8 * groups + grp);
+        const uint32_t b0 = bias_pair<ACT, ZERO>(zp, zidx + grp, g);
+        const uint32_t b8 = bias_pair<ACT, ZERO>(zp, zidx + groups + grp, g);
+        float sp[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t ww0[4] = {w0.x, w0.y, w0.z, w0.w}, ww8[4] = {w8.x, w8.y, w8.z, w8.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+            uint32_t a0[4], a8[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                a0[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(ww0[wi], j), b0), s0);
+                a8[j] = pair_mul<ACT>(pair_sub<ACT>(int4_pair<ACT>(ww8[wi], j), b8), s8);
+            }
+            mma_16816<ACT>(sp, a0[0], a8[0], a0[1], a8[1], hv[wi].x, hv[wi].y);
+            mma_16816<ACT>(sp, a0[2], a8[2], a0[3], a8[3], hv[wi].z, hv[wi].w);
+        }
+        *reinterpret_cast<float2*>(stash + (st * kTileRows + g) * 8 + 2 * tig) = make_float2(sp[0], sp[1]);
+        *reinterpret_cast<float2*>(stash + (st * kTileRows + g + 8) * 8 + 2 * tig) = make_float2(sp[2], sp[3]);
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    if (threadIdx.x < kTileRows * 8) {
+        const int rr = threadIdx.x >> 3, c = threadIdx.x & 7;
+        if (c < ncols_s) {
+            float acc = 0.f;
+            for (int st = 0; st < spu; ++st) acc = __fadd_rn(acc, stash[(st * kTileRows + rr) * 8 + c]);
+            const int rowid = col_row[c];
+            const int64_t t = rowid / p.top_k;
+            const int k = rowid - int(t) * p.top_k;
+            const int widx = p.w_index ? p.w_index[rowid] : k;
+            const float wv = load_as_float(p.weights, p.w_dtype, t * p.w_tok_stride + int64_t(widx) * p.w_slot_stride);
+            float cv = __fmul_rn(round_act<ACT>(acc), wv);
+            if (p.w_round) cv = round_act<ACT>(cv);
+            p.ybuf_g[int64_t(rowid) * p.hidden + tile * kTileRows + rr] = cv;
+        }
+    }
+}
+
 // ── host side ─────────────────────────────────────────────────────────────────────────────
 
 size_t gu_smem() { return size_t(kGuWarps) * kGuDepth * 4 * 32 * sizeof(uint4); }
@@ -961,6 +1190,9 @@ cudaError_t launch_pdl(Kernel kernel, int grid, int warps, size_t smem, cudaStre
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, prm);
 }
+
+// Whether the call takes the pass-per-CTA kernels: the host set a grid bound for them.
+bool use_pass_kernels(const GateUpParams& gu) { return gu.max_passes > 0; }
 
 template <int ACT, int SC, bool ZERO, int NB>
 int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaStream_t s,
@@ -994,6 +1226,29 @@ int run_decode(const GateUpParams& gu, const DownParams& dn, int sm_count, cudaS
     if (st != VY_OK) return st;
     const int dev = current_device();
     const int gu_blocks_per_sm = gu_per_sm[dev], dn_blocks_per_sm = dn_per_sm[dev];
+    if constexpr (NB == 1) {
+        if (gu.k_splits <= 1 && use_pass_kernels(gu)) {
+            const int st2 = once_per_device(
+                reinterpret_cast<const void*>(pass_gate_up_kernel<ACT, SC, ZERO>),
+                [](int, void*) -> int {
+                    const cudaError_t e1 = cudaFuncSetAttribute(pass_gate_up_kernel<ACT, SC, ZERO>,
+                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pass_gu_smem(kRowMaxStages * kStageK)));
+                    const cudaError_t e2 = cudaFuncSetAttribute(pass_down_kernel<ACT, SC, ZERO>,
+                        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pass_dn_smem(4 * kRowMaxStages * kStageK)));
+                    return e1 == cudaSuccess && e2 == cudaSuccess ? VY_OK : fail(VY_ERR_CUDA, "pass kernels shared memory");
+                },
+                nullptr);
+            if (st2 != VY_OK) return st2;
+            cudaError_t e = launch_chained(pass_gate_up_kernel<ACT, SC, ZERO>, dim3(gu.inter / kTileRows, gu.max_passes),
+                                           dim3(kPassGuWarps * 32), pass_gu_smem(gu.hidden), s, gu);
+            if (e != cudaSuccess) return fail(VY_ERR_CUDA, "gate/up launch: %s", cudaGetErrorString(e));
+            if (timed) cudaEventRecord(ev[2], s);
+            e = launch_chained(pass_down_kernel<ACT, SC, ZERO>, dim3(dn.hidden / kTileRows, gu.max_passes),
+                               dim3(kPassDnWarps * 32), pass_dn_smem(dn.inter), s, dn);
+            if (e != cudaSuccess) return fail(VY_ERR_CUDA, "down launch: %s", cudaGetErrorString(e));
+            return check_launch("vy_moe_decode");
+        }
+    }
     cudaError_t e = gu.k_splits > 1
         ? launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB, true>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu)
         : launch_pdl(gate_up_kernel<ACT, SC, ZERO, NB, false>, gu_blocks_per_sm * sm_count, kGuWarps, gu_smem(), s, gu);
@@ -1365,6 +1620,13 @@ extern "C" int vy_moe_decode(const vy_moe_call* call, void* stream) {
     gu.h_perm = L.h_perm;
     gu.h_out = static_cast<uint16_t*>(c->h_out);
     gu.k_splits = L.k_splits;
+    // Pass-per-CTA kernels for a few passes of many experts (cfg1 at 3 / 8 tokens: 44.0 -> 39.3
+    // and 72.2 -> 64.7 us on B200); the warp-unit kernels from 16 tokens on (cfg1 T = 16: 99.6
+    // against 105.5, T = 32: 123.5 against 125.9) and for few large experts, not measured there.
+    const bool pass_ctas = nb == 1 && L.k_splits <= 1 && c->n_tokens * c->top_k <= kPassMaxRows &&
+                           c->n_experts >= 64 && g.hidden / kStageK <= kRowMaxStages &&
+                           g.inter / kStageK <= 4 * kRowMaxStages;
+    gu.max_passes = pass_ctas ? static_cast<int>(L.max_units / (g.inter / kTileRows)) : 0;
     gu.partial = L.partial;
     gu.tickets = L.tickets;
 
