@@ -331,7 +331,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
                 }
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
-                    if (cb * 8 >= cu.ncols) break;     // warp-uniform: no tokens left
+                    if (cb > 0 && cb * 8 >= cu.ncols) break;   // warp-uniform: no tokens left (a pass has one)
                     uint4 xv = xv0[wi];
                     if (cb > 0)
                         xv = xoff[cb] >= 0 ? ld_nc_v4(p.x_perm + xoff[cb] + kx + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
@@ -344,7 +344,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
             if constexpr (!SPLIT) {
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
-                    if (cb * 8 >= cu.ncols) break;
+                    if (cb > 0 && cb * 8 >= cu.ncols) break;
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         acc_g[cb][i] = __fadd_rn(acc_g[cb][i], sg[cb][i]);
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
                               ((int64_t(cu.unit) * spu + cu.split * sps + c_ks) * 32 + lane) * (2 * NB);
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
-                    if (cb * 8 >= cu.ncols) break;
+                    if (cb > 0 && cb * 8 >= cu.ncols) break;
                     __stcg(rec + 2 * cb, make_float4(sg[cb][0], sg[cb][1], sg[cb][2], sg[cb][3]));
                     __stcg(rec + 2 * cb + 1, make_float4(su[cb][0], su[cb][1], su[cb][2], su[cb][3]));
                 }
@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(kGuWarps * 32, NB <= 2 ? 2 : 1) gate_up_kernel
                     for (int st = 0; st < spu; ++st) {
 #pragma unroll
                         for (int cb = 0; cb < NB; ++cb) {
-                            if (cb * 8 >= cu.ncols) break;
+                            if (cb > 0 && cb * 8 >= cu.ncols) break;
                             const float4 a = __ldcg(rec + int64_t(st) * 32 * 2 * NB + 2 * cb);
                             const float4 b = __ldcg(rec + int64_t(st) * 32 * 2 * NB + 2 * cb + 1);
                             acc_g[cb][0] = __fadd_rn(acc_g[cb][0], a.x);
@@ -547,7 +547,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(D
                 }
 #pragma unroll
                 for (int cb = 0; cb < NB; ++cb) {
-                    if (cb * 8 >= cu.ncols) break;     // warp-uniform: no tokens left
+                    if (cb > 0 && cb * 8 >= cu.ncols) break;   // warp-uniform: no tokens left (a pass has one)
                     uint4 hv = hv0[wi];
                     if (cb > 0)
                         hv = hoff[cb] >= 0 ? ld_nc_v4(p.h_perm + hoff[cb] + kh + wi * 8) : make_uint4(0u, 0u, 0u, 0u);
@@ -557,7 +557,7 @@ __global__ void __launch_bounds__(kWarps * 32, kDnBlocksPerSm[NB]) down_kernel(D
             }
 #pragma unroll
             for (int cb = 0; cb < NB; ++cb) {
-                if (cb * 8 >= cu.ncols) break;
+                if (cb > 0 && cb * 8 >= cu.ncols) break;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[cb][i] = __fadd_rn(acc[cb][i], sp[cb][i]);
             }
