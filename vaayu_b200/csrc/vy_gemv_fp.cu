@@ -98,7 +98,8 @@ struct GemvParams {
 // KIND 1: fp4 (16 B = 32 codes; a step covers 128 K per row)
 // Each warp streams its K range through its own cp.async ring in shared memory (kDepth steps of
 // 1 KB: rows g and g + 8 of the tile, 16 B per lane each), kDepth - 1 steps ahead of the math.
-template <int KIND, int NB>
+// SC: the fp8 block scales' dtype, fixed at compile time (no per-step dispatch).
+template <int KIND, int NB, int SC>
 __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_kernel(GemvParams p) {
     constexpr int kPerThread = KIND == 0 ? 16 : 32;    // K elements per thread per step
     constexpr int kStepK = 4 * kPerThread;             // K per step per row
@@ -163,8 +164,8 @@ __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_ker
         uint32_t ha[2] = {0u, 0u}, hb[2] = {0u, 0u};   // fp4 group scales as bf16 pairs (exact)
         if constexpr (KIND == 0) {
             const uint32_t kb = kdiv(k0);
-            sa = okA ? block_scale(p.scale, p.scale_dtype, baseA + kb) : 0.f;
-            sb = okB ? block_scale(p.scale, p.scale_dtype, baseB + kb) : 0.f;
+            sa = okA ? block_scale(p.scale, SC, baseA + kb) : 0.f;
+            sb = okB ? block_scale(p.scale, SC, baseB + kb) : 0.f;
         } else if (halves) {
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
@@ -460,17 +461,27 @@ size_t t1_smem_limit() {
     return (st == VY_OK && d >= 0 && d < kMaxDevices) ? limit[d] : 0;
 }
 
-template <int KIND, int NB>
+template <int KIND, int NB, int SC>
 cudaError_t launch_one(unsigned grid, const GemvParams& p, cudaStream_t s) {
     const int st = once_per_device(
-        reinterpret_cast<const void*>(fp_gemv_kernel<KIND, NB>),
+        reinterpret_cast<const void*>(fp_gemv_kernel<KIND, NB, SC>),
         [](int, void*) -> int {
-            return cudaFuncSetAttribute(fp_gemv_kernel<KIND, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            return cudaFuncSetAttribute(fp_gemv_kernel<KIND, NB, SC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(kRingBytes)) == cudaSuccess ? VY_OK : VY_ERR_CUDA;
         },
         nullptr);
     if (st != VY_OK) return cudaErrorInvalidValue;
-    return launch_chained(fp_gemv_kernel<KIND, NB>, dim3(grid), dim3(kWarps * 32), kRingBytes, s, p);
+    return launch_chained(fp_gemv_kernel<KIND, NB, SC>, dim3(grid), dim3(kWarps * 32), kRingBytes, s, p);
+}
+
+// FP8 launches by block-scale dtype (SC is the first candidate tried).
+template <int SC>
+cudaError_t launch_fp8(int sc, bool two, unsigned grid, const GemvParams& p, cudaStream_t s) {
+    if (sc == SC || SC == VY_E8M0)
+        return two ? launch_one<0, 2, SC>(grid, p, s) : launch_one<0, 1, SC>(grid, p, s);
+    if constexpr (SC == VY_F32) return launch_fp8<VY_BF16>(sc, two, grid, p, s);
+    else if constexpr (SC == VY_BF16) return launch_fp8<VY_F16>(sc, two, grid, p, s);
+    else return launch_fp8<VY_E8M0>(sc, two, grid, p, s);
 }
 
 // One-token NVFP4 calls with whole 16-code groups take fp4_t1_kernel while its staged activations
@@ -486,8 +497,8 @@ int launch_gemv(int kind, const GemvParams& p, cudaStream_t s) {
     else if (t1 && !g16 && t1 <= t1_smem_limit<false>())
         e = launch_chained(fp4_t1_kernel<false>, dim3(grid), dim3(kT1Warps * 32), t1, s, p);
     else
-        e = kind == 0 ? (two ? launch_one<0, 2>(grid, p, s) : launch_one<0, 1>(grid, p, s))
-                      : (two ? launch_one<1, 2>(grid, p, s) : launch_one<1, 1>(grid, p, s));
+        e = kind == 1 ? (two ? launch_one<1, 2, VY_E4M3>(grid, p, s) : launch_one<1, 1, VY_E4M3>(grid, p, s))
+                      : launch_fp8<VY_F32>(p.scale_dtype, two, grid, p, s);
     if (e != cudaSuccess) return fail(VY_ERR_CUDA, "%s launch: %s", kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv",
                                       cudaGetErrorString(e));
     return check_launch(kind == 0 ? "vy_fp8_gemv" : "vy_fp4_gemv");
