@@ -131,12 +131,16 @@ __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_ker
     // ── issue side: one step (rows A and B, 16 B per lane each) per call ──────────────────
     int64_t i_s = s_lo;
     int i_slot = 0;
+    constexpr int kStepBytes = KIND == 0 ? kStepK : kStepK / 2;
+    const uint8_t* srcA = wA + (s_lo * kStepK + tig * kPerThread) / (KIND == 0 ? 1 : 2);
+    const uint8_t* srcB = wB + (s_lo * kStepK + tig * kPerThread) / (KIND == 0 ? 1 : 2);
     auto issue = [&]() {
         if (i_s < s_hi) {
-            const int64_t off = (i_s * kStepK + tig * kPerThread) / (KIND == 0 ? 1 : 2);
             uint4* dst = my_ring + i_slot * 64 + lane;
-            if (okA) cp_async16(dst, wA + off);
-            if (okB) cp_async16(dst + 32, wB + off);
+            if (okA) cp_async16(dst, srcA);
+            if (okB) cp_async16(dst + 32, srcB);
+            srcA += kStepBytes;
+            srcB += kStepBytes;
         }
         cp_async_commit();
         ++i_s;
@@ -144,6 +148,12 @@ __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_ker
     };
 #pragma unroll
     for (int d = 0; d < kDepth - 1; ++d) issue();
+
+    // this lane's token column in each block (null past the batch), at its K offset in a step
+    const __nv_bfloat16* xrow[NB];
+#pragma unroll
+    for (int cb = 0; cb < NB; ++cb)
+        xrow[cb] = cb * 8 + g < p.n_tokens ? p.x + int64_t(cb * 8 + g) * p.x_stride + tig * kPerThread : nullptr;
 
     float acc[NB][4];
 #pragma unroll
@@ -214,10 +224,8 @@ __global__ void __launch_bounds__(kWarps * 32, kWarps >= 16 ? 2 : 1) fp_gemv_ker
             }
 #pragma unroll
             for (int cb = 0; cb < NB; ++cb) {
-                const int t = cb * 8 + g;
                 uint2 xv = make_uint2(0u, 0u);
-                if (t < p.n_tokens)
-                    xv = *reinterpret_cast<const uint2*>(p.x + int64_t(t) * p.x_stride + k0 + 4 * q);
+                if (xrow[cb]) xv = *reinterpret_cast<const uint2*>(xrow[cb] + s * kStepK + 4 * q);
                 mma_16816<VY_BF16>(acc[cb], a0, a1, a2, a3, xv.x, xv.y);
             }
         }
