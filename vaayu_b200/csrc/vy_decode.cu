@@ -21,6 +21,12 @@
 //   combine         (vy_route.cu) each token's contributions summed in ascending expert id,
 //                   then slot -- no atomics on the sums.
 //
+// Two other decompositions of the same units serve small calls (all three give the same bits):
+//   row_gate_up_kernel / row_down_kernel   at most 16 routed rows: one CTA per (routed row,
+//                   16-row tile), no routing plan, the combine fused into the down kernel;
+//   pass_gate_up_kernel / pass_down_kernel 17-64 routed rows over many experts: the planned
+//                   passes, one CTA per (pass, tile) whose warps share the K range.
+//
 // The dequantised operand never touches shared memory, which is what keeps this path on HBM
 // bandwidth: a tcgen05 GEMM would have to write every dequantised weight to shared memory and
 // read it back (2 x 2 bytes per int4 weight), more shared-memory traffic per SM than the SM has
