@@ -82,3 +82,33 @@ def test_an_expert_of_another_format_is_refused():
     arena.ensure([0])
     with pytest.raises(NotImplementedError, match="expert 1"):
         arena.ensure([1])
+
+
+def test_a_rank_range_loads_from_safetensors_into_the_slab(tmp_path):
+    """`from_checkpoint` over experts [4, 8) of an 8-expert layer file: local expert i is file
+    expert 4 + i, its slot holds exactly the blob the checkpoint reader builds, and a miss reads
+    only that expert."""
+    from vaayu_b200 import checkpoint as ck
+    from vaayu_b200 import synthetic
+    g = torch.Generator().manual_seed(3)
+    tensors = {}
+    for e in range(8):
+        by_role = synthetic.make_expert(256, 128, g, group=32)
+        for role, seg in (("gate", "gate_proj"), ("down", "down_proj"), ("up", "up_proj")):
+            for comp, t in by_role[role].items():
+                tensors[f"model.layers.1.mlp.experts.{e}.{seg}.{comp}"] = t
+    ck.write_safetensors(str(tmp_path / "m.safetensors"), tensors)
+    cp = ck.Checkpoint(str(tmp_path / "m.safetensors"))
+    try:
+        arena = vb.ExpertArena.from_checkpoint(cp, "model.layers.1.mlp", capacity=2, experts=range(4, 8),
+                                               device="cpu")
+        assert arena.n_experts == 4 and arena.resident == [0, 1]
+        arena.ensure([3])
+        assert arena.resident == [1, 3]            # expert 0 was the least recently used
+        for local in arena.resident:
+            want = cp.expert_blob("model.layers.1.mlp", 4 + local, device="cpu")
+            got = arena.stream_views(arena._slot_of[local])
+            for name in ("packed", "scale"):
+                assert torch.equal(got[name], want["flat"][name]), (local, name)
+    finally:
+        cp.close()
