@@ -138,6 +138,15 @@ __device__ __forceinline__ uint32_t int4_bias_pair(uint32_t z) {
     return v | (v << 16);
 }
 
+// One byte of NVFP4 codes (two e2m1 values, low nibble first) as an exact f16 pair, by the
+// hardware conversion.  One byte per asm statement: a form that unpacked a word into four byte
+// registers in one statement produced wrong values for half of a fragment's rows in one kernel.
+__device__ __forceinline__ uint32_t e2m1x2_f16(uint32_t byte) {
+    uint32_t d;
+    asm("{ .reg .b8 t;\n  cvt.u8.u32 t, %1;\n  cvt.rn.f16x2.e2m1x2 %0, t;\n}" : "=r"(d) : "r"(byte & 0xFFu));
+    return d;
+}
+
 // ── device: tensor-core fragments (m16n8k16, fp32 accumulate) ────────────────────────────
 
 template <int ACT>

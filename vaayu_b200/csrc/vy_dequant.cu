@@ -307,17 +307,10 @@ __device__ __forceinline__ void e2m1x16_times(const uint2 raw, float s, float (&
     const uint32_t w[2] = {raw.x, raw.y};
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
-        uint32_t h[4];
-        asm("{ .reg .b8 b0, b1, b2, b3;\n"
-            "  mov.b32 {b0, b1, b2, b3}, %4;\n"
-            "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
-            "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-            "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
-            "  cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
-            : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3]) : "r"(w[i]));
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[j]));
+            const uint32_t h = e2m1x2_f16(w[i] >> (8 * j));
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
             v[8 * i + 2 * j] = __fmul_rn(f.x, s);
             v[8 * i + 2 * j + 1] = __fmul_rn(f.y, s);
         }

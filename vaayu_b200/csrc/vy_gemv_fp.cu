@@ -35,17 +35,16 @@ __device__ __forceinline__ float2 e4m3x2f(uint32_t b) {
     return __half22float2(*reinterpret_cast<const __half2*>(&h));
 }
 
-// Four e2m1 codes (bits 0-15, low nibble first) as two bf16 pairs, exactly: the magnitudes
-// index an 8-entry byte table for each half of the bf16 pattern (prmt), the signs are the codes'
-// own sign bits replicated into bit 15 / 31 (prmt's sign-replicate selectors).
+// Four e2m1 codes (bits 0-15, low nibble first) as two bf16 pairs, exactly: each byte to an f16
+// pair by the hardware conversion, widened to fp32 and narrowed to bf16 (e2m1 values are 0, 0.5
+// .. 6, exact in all three).
 __device__ __forceinline__ void e2m1x4_bf16(uint32_t c, uint32_t& e01, uint32_t& e23) {
-    // bf16 of 0, 0.5, 1, 1.5, 2, 3, 4, 6: low bytes 00 00 80 C0 00 40 80 C0, high 00 3F 3F 3F 40 40 40 40
-    const uint32_t mag = c & 0x7777u;
-    const uint32_t lo = __byte_perm(0xC0800000u, 0xC0804000u, mag);
-    const uint32_t hi = __byte_perm(0x3F3F3F00u, 0x40404040u, mag);
-    const uint32_t a = c << 4;   // byte 0 / 1 msb = sign of code 0 / 2; c's byte 0 / 1 msb = code 1 / 3
-    e01 = __byte_perm(lo, hi, 0x5140) | (__byte_perm(a, c, 0xC080) & 0x80008000u);
-    e23 = __byte_perm(lo, hi, 0x7362) | (__byte_perm(a, c, 0xD090) & 0x80008000u);
+    const uint32_t h0 = e2m1x2_f16(c), h1 = e2m1x2_f16(c >> 8);
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&h0));
+    const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&h1));
+    const __nv_bfloat162 p0 = __floats2bfloat162_rn(f0.x, f0.y), p1 = __floats2bfloat162_rn(f1.x, f1.y);
+    e01 = *reinterpret_cast<const uint32_t*>(&p0);
+    e23 = *reinterpret_cast<const uint32_t*>(&p1);
 }
 
 __device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
@@ -269,15 +268,12 @@ constexpr int kT1Warps = VY_GEMV_T1_WARPS;
 constexpr int kT1StepK = 128;                     // K per step per row (16 B of codes a lane)
 constexpr size_t kT1RingBytes = size_t(kT1Warps) * kDepth * 64 * sizeof(uint4);
 
-// Two e2m1 codes (one byte, low nibble first) to an f16 pair, four bytes at a time.
+// Four bytes of e2m1 codes (eight values, low nibble first) as four f16 pairs.
 __device__ __forceinline__ void e2m1x8_f16(uint32_t c, uint32_t& d0, uint32_t& d1, uint32_t& d2, uint32_t& d3) {
-    asm("{ .reg .b8 b0, b1, b2, b3;\n"
-        "  mov.b32 {b0, b1, b2, b3}, %4;\n"
-        "  cvt.rn.f16x2.e2m1x2 %0, b0;\n"
-        "  cvt.rn.f16x2.e2m1x2 %1, b1;\n"
-        "  cvt.rn.f16x2.e2m1x2 %2, b2;\n"
-        "  cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
-        : "=r"(d0), "=r"(d1), "=r"(d2), "=r"(d3) : "r"(c));
+    d0 = e2m1x2_f16(c);
+    d1 = e2m1x2_f16(c >> 8);
+    d2 = e2m1x2_f16(c >> 16);
+    d3 = e2m1x2_f16(c >> 24);
 }
 
 // Two e4m3 codes (bits 0-15, first in the low byte) as an f16 pair (exact).
