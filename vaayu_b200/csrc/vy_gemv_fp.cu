@@ -257,9 +257,9 @@ constexpr size_t kRingBytes = size_t(kWarps) * kDepth * 64 * sizeof(uint4);
 // [2^14, 2^15): a bf16 value (8 significant bits) converts to f16 exactly down to 2^-28 of that
 // largest magnitude.  The warp's partial dots are multiplied back by 2^s (exact), so products
 // and sums equal those of the bf16 operands.  (A range whose largest |x| is below 2^-112 is staged
-// with s = -126 and loses low bits; an infinite or NaN activation is staged unscaled.)  This
-// replaces the byte-permute decode's ~2.6 integer instructions a code with half a conversion and
-// half an f16 multiply.
+// with s = -126 and loses low bits; an infinite or NaN activation is staged unscaled.)  A code
+// costs half a conversion and half an f16 multiply, against the multi-token kernel's conversion,
+// widening and narrowing to bf16 and bf16 multiply.
 
 #ifndef VY_GEMV_T1_WARPS
 #define VY_GEMV_T1_WARPS 16
