@@ -129,6 +129,7 @@ class _Workspace:
 _WORKSPACE = _Workspace()
 _VERDICTS: dict = {}
 _PF_VERDICTS: dict = {}
+_LAYER_VERDICTS: dict = {}     # moe_forward's (geometry, act, scale, weight dtypes) -> refusal or None
 
 
 def _stage(values: torch.Tensor, device, into: "torch.Tensor | None" = None) -> torch.Tensor:
@@ -625,7 +626,10 @@ def moe_forward(x, expert_ids, routing_weights, table: ExpertTable, out=None, *,
     error flags afterwards and raises RuntimeError when any is set."""
     dev = _lib.require_cuda(x, expert_ids, routing_weights, out, contrib, what="moe_forward")
     _check_x(x, "moe_forward")
-    why = _unsupported(table.geom, x.dtype, table.scale_dtype, routing_weights.dtype)
+    key = (table.geom, x.dtype, table.scale_dtype, routing_weights.dtype)
+    why = _LAYER_VERDICTS.get(key, False)
+    if why is False:                     # first call with this geometry and these dtypes
+        why = _LAYER_VERDICTS[key] = _unsupported(*key)
     if why is not None:
         raise NotImplementedError(f"moe_forward: {why}")
     n_tok, top_k = expert_ids.shape
