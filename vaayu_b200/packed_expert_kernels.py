@@ -149,7 +149,10 @@ def _stage(values: torch.Tensor, device, into: "torch.Tensor | None" = None) -> 
 def _make_call(geom_s, x, n_tokens, top_k, n_experts, table_ptr, ids_ptr, ids_code, rw,
                w_tok_stride, w_slot_stride, w_index_ptr, out, contrib, h_out) -> _lib.MoeCall:
     c = _lib.MoeCall()
-    c.geom = ctypes.pointer(geom_s)
+    gp = geom_s.__dict__.get("_pointer")            # built once per geometry struct
+    if gp is None:
+        gp = geom_s.__dict__["_pointer"] = ctypes.pointer(geom_s)
+    c.geom = gp
     c.act_dtype = _DTYPE_CODE[x.dtype]
     c.n_experts, c.top_k, c.ids_dtype, c.n_tokens = n_experts, top_k, ids_code, n_tokens
     c.x, c.x_row_stride = x.data_ptr(), (x.stride(0) if x.dim() == 2 else x.shape[-1])
